@@ -1,0 +1,448 @@
+"""Benchmark: Int8-weight LoRA linear forward + backward on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config block|cfg1]
+
+Workload (the default "block"): every linear of one
+Wan-2.1-1.3B DiT block at 32760 tokens per sample -- self-attention q/k/v/o
+and cross-attention q/o (1536x1536 over 32760 tokens), cross-attention k/v
+(1536x1536 over 512 context tokens), FFN up 1536->8960 and down 8960->1536 --
+int8 per-row weights from N(0, 0.02), LoRA rank 32 / alpha 32 on every
+linear, bf16 activations ~N(0,1).  One step = the forward of the ten linears,
+then their backward in reverse order (dX, dA, dB), and at N > 1 the fp32
+all-reduce of every LoRA gradient (per layer, overlapped with the backward).
+Data-parallel weak scaling: each rank processes its own 32760-token sample.
+
+Our arm prints one JSON line (rank 0).  ``--impl reference`` times the
+reference's CPU code path (oracle/numpy_port.py: dequantise-materialise plus
+OpenBLAS sgemm, the op order of src/layers/lora.jl:56-118) on the host cores
+instead; the reference itself is Julia and cannot run in this image.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HIDDEN, FFN, CONTEXT = 1536, 8960, 512
+
+
+def block_layers(tokens: int, context: int = CONTEXT):
+    """(name, M, K, N) of the ten linears of a Wan-2.1-1.3B block."""
+    L = []
+    for n in ("self_q", "self_k", "self_v", "self_o", "cross_q"):
+        L.append((n, tokens, HIDDEN, HIDDEN))
+    L.append(("cross_k", context, HIDDEN, HIDDEN))
+    L.append(("cross_v", context, HIDDEN, HIDDEN))
+    L.append(("cross_o", tokens, HIDDEN, HIDDEN))
+    L.append(("ffn_up", tokens, HIDDEN, FFN))
+    L.append(("ffn_down", tokens, FFN, HIDDEN))
+    return L
+
+
+def workload(config: str):
+    if config == "cfg1":
+        return dict(name="wan21-1.3b-ffn-up", layers=[("ffn_up", 1280, 1536, 8960)], tokens=1280, rank=16,
+                    alpha=16.0)
+    return dict(name="wan21-1.3b-block-linears", layers=block_layers(32760), tokens=32760, rank=32, alpha=32.0)
+
+
+def step_flops(layers, r):
+    # 4*M*N*K (forward + dX) + 6*M*r*(K+N) (LoRA forward and backward).
+    return float(sum(4.0 * M * N * K + 6.0 * M * r * (K + N) for (_, M, K, N) in layers))
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the q8 GEMM from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "q8_gemm_traffic.txt")
+    if not os.path.exists(p):
+        return None, None
+    vals = {}
+    for line in open(p):
+        if "=" in line and not line.startswith("#"):
+            k, v = line.split("=", 1)
+            vals[k.strip()] = v.strip()
+    try:
+        return float(vals["dram_bytes_per_launch"]), vals.get("workload")
+    except (KeyError, ValueError):
+        return None, None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() in ("active", "yes", "1"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------- CPU baseline
+def cpu_sample(layers, r, alpha, tokens_sample, seconds, seed=0):
+    """Time the reference CPU path (numpy + OpenBLAS fp32) on the block with
+    `tokens_sample` tokens per sample; returns (tokens/s, iters, threads)."""
+    from oracle import numpy_port
+    import oracle
+    g = np.random.default_rng(seed)
+    data = []
+    for (_, M, K, N) in layers:
+        m = min(M, tokens_sample) if M > CONTEXT else M
+        X = g.standard_normal((m, K), dtype=np.float32)
+        dY = g.standard_normal((m, N), dtype=np.float32)
+        W = (0.02 * g.standard_normal((K, N), dtype=np.float32))
+        q, s = oracle.quantize(W, 0)
+        A = (g.standard_normal((K, r), dtype=np.float32) / np.sqrt(K)).astype(np.float32)
+        B = (0.01 * g.standard_normal((r, N), dtype=np.float32)).astype(np.float32)
+        data.append((X, dY, q, s, A, B))
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("internal_api") == "openblas"]
+                      or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+
+    def one():
+        for (X, dY, q, s, A, B) in data:
+            numpy_port.lora_step(X, dY, q, s, 0, A, B, alpha)
+
+    one()  # warm-up
+    t0 = time.perf_counter()
+    it = 0
+    while True:
+        one()
+        it += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    return tokens_sample * it / dt, it, threads, dt
+
+
+# ------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from reels_b200 import build as native_build
+    from reels_b200 import _native as nat
+    from reels_b200 import distributed as rd
+    from reels_b200 import quantize_frozen_matrix
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        rt = rd.init_distributed(backend="nccl", timeout_seconds=120)
+    else:
+        rt = rd.SingleProcessRuntime()
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    native_build.build()
+    L = nat.lib()
+    wl = workload(args.config)
+    layers, r, alpha = wl["layers"], wl["rank"], wl["alpha"]
+    bf = torch.bfloat16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    class Lin:
+        pass
+
+    lins = []
+    for i, (name, M, K, N) in enumerate(layers):
+        o = Lin()
+        o.name, o.M, o.K, o.N = name, M, K, N
+        w = torch.empty((K, N), device=dev).normal_(0.0, 0.02, generator=gen).t()   # (out, in) column-major
+        qm = quantize_frozen_matrix(w)
+        del w
+        o.q, o.s = qm.values, qm.scales
+        o.A = (torch.randn((K, r), device=dev, generator=gen) / K ** 0.5).to(bf)     # [K][r] memory
+        o.B = (0.01 * torch.randn((r, N), device=dev, generator=gen)).to(bf)         # [r][N] memory
+        o.x = torch.randn((M, K), device=dev, generator=gen).to(bf)
+        o.dy = torch.randn((M, N), device=dev, generator=gen).to(bf)
+        o.y = torch.empty((M, N), device=dev, dtype=bf)
+        o.dx = torch.empty((M, K), device=dev, dtype=bf)
+        o.saved = torch.empty((max(L.reels_q8lora_saved_bytes(M, r, nat.BF16), 16),), dtype=torch.uint8,
+                              device=dev)
+        o.grad = torch.zeros((r * (K + N),), dtype=torch.float32, device=dev)     # [dA (K*r) | dB (r*N)]
+        lins.append(o)
+    wsn = max(max(L.reels_q8lora_workspace_bytes(o.M, o.K, o.N, r, nat.BF16, p) for p in (0, 1)) for o in lins)
+    ws = torch.empty((wsn,), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    reducer = rd.OverlappedGradReducer(rt, dev)
+
+    def fwd(o):
+        nat.check("forward", L.reels_q8lora_forward(
+            o.x.data_ptr(), o.q.data_ptr(), o.s.data_ptr(), 0, o.A.data_ptr(), o.B.data_ptr(), None, o.M, o.K,
+            o.N, r, alpha, nat.BF16, o.y.data_ptr(), o.saved.data_ptr(), ws.data_ptr(), wsn, sp))
+
+    def bwd(o):
+        nat.check("backward", L.reels_q8lora_backward(
+            o.x.data_ptr(), o.dy.data_ptr(), o.q.data_ptr(), o.s.data_ptr(), 0, o.A.data_ptr(), o.B.data_ptr(),
+            o.saved.data_ptr(), o.M, o.K, o.N, r, alpha, 1.0, nat.BF16, o.dx.data_ptr(), o.grad.data_ptr(),
+            o.grad.data_ptr() + 4 * o.K * r, 0, ws.data_ptr(), wsn, sp))
+
+    def step():
+        for o in lins:
+            fwd(o)
+        for o in reversed(lins):
+            bwd(o)
+            reducer.layer_done(o.grad)
+        reducer.finish()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    nat.check("device status", L.reels_lowvram_check_device_status(sp))
+
+    # ---------------- device-timed region ----------------
+    clocks = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    nat.profile_enable(True)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk = clocks.stop()
+    q8_ms, q8_n, q8_flops, launches = nat.profile_read()
+    nat.profile_enable(False)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    nat.check("device status", L.reels_lowvram_check_device_status(sp))
+    ms_per_step = ms / args.steps
+    tokens = wl["tokens"]
+    value = world * tokens * args.steps / (ms / 1e3)
+    flops = step_flops(layers, r)
+
+    # ---------------- end to end through the C ABI with host buffers ----------------
+    e2e_steps = max(1, min(args.steps, 10))
+    hx = [o.x.cpu().pin_memory() for o in lins]
+    hdy = [o.dy.cpu().pin_memory() for o in lins]
+    hgrad = [torch.empty(o.grad.shape, dtype=torch.float32).pin_memory() for o in lins]
+    h2d = sum(t.numel() * t.element_size() for t in hx + hdy)
+    d2h = sum(t.numel() * t.element_size() for t in hgrad)
+
+    def e2e_step():
+        for o, a, b in zip(lins, hx, hdy):
+            o.x.copy_(a, non_blocking=True)
+            o.dy.copy_(b, non_blocking=True)
+        step()
+        for o, h in zip(lins, hgrad):
+            h.copy_(o.grad, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    ems = f0.elapsed_time(f1)
+    if world > 1:
+        t = torch.tensor([ems], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e_value = world * tokens * e2e_steps / (ems / 1e3)
+
+    peaks, peak_kind = load_peaks()
+    q8_tflops = (q8_flops / (q8_ms / 1e3) / 1e12) if q8_ms > 0 else None
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    traffic, traffic_src = load_traffic()
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            sample = 512 if args.config == "block" else 256
+            tps, it, threads, secs = cpu_sample(layers, r, alpha, sample, args.cpu_seconds)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"{args.config} linears fwd+bwd at {sample} tokens/sample (context {CONTEXT}), "
+                             f"numpy+OpenBLAS fp32, {it} iterations in {secs:.1f} s"}
+        result = {
+            "metric": "int8-W LoRA linear fwd+bwd tokens/s (TFLOP/s and % of roofline alongside)",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded normal activations, N(0,0.02) weights int8 per row)",
+            "config": {"workload": wl["name"], "tokens_per_sample": tokens, "context_tokens": CONTEXT,
+                       "linears": [list(l) for l in layers], "rank": r, "alpha": alpha,
+                       "weight_layout": "out-contiguous (reference)", "global_batch": world,
+                       "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (about 5 GB of activations and gradients per step)"},
+            "tflops": flops * world * args.steps / (ms / 1e3) / 1e12,
+            "roofline": {"bound": "tensor", "kernel": "q8_gemm_kernel (forward Y and dX)",
+                         "achieved": q8_tflops, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (q8_tflops / peak) if q8_tflops else None,
+                         "peak_source": f"bf16_tflops_sustained of {peak_kind}",
+                         "launches": q8_n, "algorithmic_flops_per_launch": (q8_flops / q8_n) if q8_n else None,
+                         "traffic": traffic, "traffic_source": traffic_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        rd.close_distributed(rt)
+    return result
+
+
+# ------------------------------------------------------- reference arm
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    wl = workload(args.config)
+    layers, r, alpha = wl["layers"], wl["rank"], wl["alpha"]
+    from oracle import numpy_port
+    import oracle
+    sample = 512 if args.config == "block" else 256
+    g = np.random.default_rng(0)
+    data = []
+    for (_, M, K, N) in layers:
+        m = min(M, sample) if M > CONTEXT else M
+        W = (0.02 * g.standard_normal((K, N), dtype=np.float32))
+        q, s = oracle.quantize(W, 0)
+        data.append((g.standard_normal((m, K), dtype=np.float32), g.standard_normal((m, N), dtype=np.float32), q,
+                     s, (g.standard_normal((K, r), dtype=np.float32) / np.sqrt(K)).astype(np.float32),
+                     (0.01 * g.standard_normal((r, N), dtype=np.float32)).astype(np.float32)))
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("internal_api") == "openblas"]
+                      or [1])
+    except Exception:
+        threads = os.cpu_count() or 1
+
+    def one():
+        for (X, dY, q, s, A, B) in data:
+            numpy_port.lora_step(X, dY, q, s, 0, A, B, alpha)
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    secs = time.perf_counter() - t0
+    value = sample * args.steps / secs
+    res = {
+        "impl": "reference",
+        "metric": "int8-W LoRA linear fwd+bwd tokens/s (TFLOP/s and % of roofline alongside)",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": secs / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": wl["name"], "tokens_per_sample": wl["tokens"], "sample_tokens": sample,
+                   "context_tokens": CONTEXT, "rank": r, "alpha": alpha, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"each step: {wl['name']} fwd+bwd at {sample} tokens/sample through "
+                                   "oracle/numpy_port.py (Julia is not installed, so the reference's CPU "
+                                   "path is run as its numpy+OpenBLAS restatement)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(res), flush=True)
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="block", choices=["block", "cfg1"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * reels_lowvram.h -- C ABI of the B200 (sm_100a) Int8-weight LoRA linear.
+ *
+ * Drop-in native backend for Reels.jl's quantised frozen-weight path
+ * (`low_vram.frozen_weight_quantization = "int8"`).  Every entry point:
+ *   - takes plain device pointers and sizes, and a cudaStream_t as `void *`;
+ *   - is asynchronous on that stream unless documented otherwise;
+ *   - returns 0 on success, REELS_EINVAL (-1) for bad arguments (nothing is
+ *     launched) and REELS_EDEVICE (-2) for CUDA launch / device errors, with a
+ *     message in reels_lowvram_last_error() (thread-local, like
+ *     deps/sentencepiece_bridge.cpp:10-17 of the reference);
+ *   - allocates no device memory: scratch space is caller-provided
+ *     (`workspace`, sized by reels_q8lora_workspace_bytes).
+ *
+ * Array layouts are those of the reference's column-major, feature-first
+ * Julia arrays, written as row-major C arrays:
+ *   x, dx      [M][K]   (Julia (in, tokens))
+ *   y, dy      [M][N]   (Julia (out, tokens))
+ *   q          [K][N]   REELS_W_OUT_CONTIGUOUS (Julia QuantizedMatrix.values, (out, in))
+ *              [N][K]   REELS_W_IN_CONTIGUOUS  (PyTorch nn.Linear.weight)
+ *   scales     [N]      fp32, one per output row of the weight
+ *   A, dA      [K][r]   (Julia LoRALinear.A, (rank, in))
+ *   B, dB      [r][N]   (Julia LoRALinear.B, (out, rank))
+ *   bias       [N]
+ * Activations, A, B and bias share one element type `act_dtype`
+ * (REELS_BF16, REELS_F16 or REELS_F32); dA and dB are fp32 accumulators.
+ *
+ * Numerics: weights are dequantised exactly (int8 -> 16-bit is exact, the
+ * per-row scale is applied in fp32), products accumulate in fp32 on the
+ * tensor cores.  bf16/fp16 with K % 16 == 0 and N % 16 == 0 and 16-byte
+ * aligned pointers run on the tcgen05 path; every other case (fp32
+ * activations, ragged feature sizes) runs on CUDA-core kernels.  Both are GPU
+ * code; there is no CPU fallback.
+ */
+#ifndef REELS_LOWVRAM_H
+#define REELS_LOWVRAM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define REELS_LOWVRAM_ABI_VERSION 1
+
+#define REELS_OK 0
+#define REELS_EINVAL (-1)
+#define REELS_EDEVICE (-2)
+
+/* element types */
+#define REELS_F32 0
+#define REELS_F16 1
+#define REELS_BF16 2
+
+/* frozen-weight layouts */
+#define REELS_W_OUT_CONTIGUOUS 0 /* Julia (out, in) column-major == row-major [K][N] */
+#define REELS_W_IN_CONTIGUOUS 1  /* row-major [N][K] */
+
+/* which pass a workspace query is for */
+#define REELS_PASS_FORWARD 0
+#define REELS_PASS_BACKWARD 1
+
+/* execution paths reported by reels_lowvram_last_path() */
+#define REELS_PATH_NONE 0
+#define REELS_PATH_TENSORCORE 1
+#define REELS_PATH_CUDACORE 2
+
+/* Message for the last failing call on this thread ("" if none).
+ * Mirrors reels_sp_last_error, deps/sentencepiece_bridge.cpp:85-87. */
+const char *reels_lowvram_last_error(void);
+
+int reels_lowvram_abi_version(void);
+
+/* Path taken by the last successful compute call on this thread. */
+int reels_lowvram_last_path(void);
+
+/* Synchronises `stream`, then reads and clears the device status word that
+ * kernels set when a bounded pipeline wait gives up.  Returns 0, or
+ * REELS_EDEVICE with the status in the message.  Not needed in normal use;
+ * tests and debug builds call it after a step. */
+int reels_lowvram_check_device_status(void *stream);
+
+/* Profiling (off by default; no reference counterpart -- the reference only
+ * times whole phases with time_ns, src/training/metrics.jl:4-10).  While
+ * enabled, every q8 GEMM launch made by this thread is bracketed by two CUDA
+ * events recorded on its own stream.  Every kernel launch is counted
+ * whether or not profiling is on.  Enabling resets the counters. */
+int reels_lowvram_profile_enable(int enable);
+
+/* Synchronises the recorded events and returns, since the last enable/read:
+ * the summed q8 GEMM kernel time (ms), the number of q8 launches, their
+ * algorithmic FLOPs (2*M*Nout*(Kred + r) each) and the number of kernels this
+ * thread launched; then resets them.  Any pointer may be NULL. */
+int reels_lowvram_profile_read(double *q8_ms, int64_t *q8_launches, double *q8_flops, int64_t *kernel_launches);
+
+/* Per-output-row symmetric Int8 quantiser, bit-exact to
+ * quantize_frozen_matrix (src/layers/quantization.jl:35-44):
+ * scale = max|w_row| / 127 (1 for an all-zero row),
+ * q = round_to_even(clamp(w / scale, -127, 127)).
+ * `w` (w_dtype REELS_F32/F16/BF16, widened to fp32 exactly like
+ * `Float32.(Array(weight))`) and `q` share `layout`.
+ * Synchronises `stream` to report non-finite weights (the reference throws
+ * InexactError there): returns REELS_EINVAL in that case. */
+int reels_q8_quantize(const void *w, int w_dtype, int layout, int64_t N, int64_t K, int8_t *q, float *scales,
+                      void *stream);
+
+/* _materialize_weight / _dequantize_for_compute (quantization.jl:54-64):
+ * out (same layout as q) = Float16(q)*Float16(s) rounded to fp16 for
+ * REELS_F16, Float32(q)*s for REELS_F32, and that fp32 product rounded once
+ * to bf16 for REELS_BF16. */
+int reels_q8_materialize(const int8_t *q, const float *scales, int layout, int64_t N, int64_t K, int out_dtype,
+                         void *out, void *stream);
+
+/* Bytes of scratch a forward or backward call needs (pass =
+ * REELS_PASS_FORWARD / REELS_PASS_BACKWARD; r = 0 for the plain linears). */
+size_t reels_q8lora_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int act_dtype, int pass);
+
+/* Bytes of the `saved` buffer (A*x kept from the forward for the backward). */
+size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype);
+
+/* _weight_mul (quantization.jl:73-74) for a QuantizedMatrix, optional bias
+ * (linear, src/layers/linear.jl:38-46): y = dequant(q) * x (+ bias). */
+int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int layout, const void *bias, int64_t M,
+                        int64_t K, int64_t N, int act_dtype, void *y, void *workspace, size_t ws_bytes,
+                        void *stream);
+
+/* _weight_transpose_mul (quantization.jl:75-76), the frozen-weight pullback
+ * of ad_rules.jl:55-80: dx = dequant(q)' * dy. */
+int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *scales, int layout, int64_t M,
+                                  int64_t K, int64_t N, int act_dtype, void *dx, void *workspace, size_t ws_bytes,
+                                  void *stream);
+
+/* lora_forward (src/layers/lora.jl:56-95; training=false or dropout 0):
+ *   y = dequant(q) * x (+ bias) + (alpha / r) * B * (A * x)
+ * `saved` (nullable, reels_q8lora_saved_bytes) receives A*x for the backward.
+ * alpha/r is formed in fp32 as in lora.jl:89. */
+int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                         const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         int act_dtype, void *y, void *saved, void *workspace, size_t ws_bytes, void *stream);
+
+/* lora_backward (lora.jl:106-118), equal to Zygote's pullback of
+ * lora_forward through the _weight_mul rrule (ad_rules.jl:70-80):
+ *   s  = alpha / r,  ax = A*x,  g = B'*dy
+ *   dx = dequant(q)' * dy + s * A' * g          (dx nullable: skipped)
+ *   dA = s * g * x'          dB = s * dy * ax'
+ * dA/dB are fp32; with accumulate = 0 they are overwritten with
+ * grad_scale * grad, with accumulate = 1 that is added (the fp32 gradient
+ * accumulators of src/training/wan_runner.jl:143,201-203; grad_scale is the
+ * 1/loss_scale of src/training/precision.jl:8-12).
+ * `saved` is the forward's A*x, or NULL to recompute it. */
+int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                          const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N, int64_t r,
+                          float alpha, float grad_scale, int act_dtype, void *dx, float *dA, float *dB,
+                          int accumulate, void *workspace, size_t ws_bytes, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REELS_LOWVRAM_H */

@@ -1,0 +1,181 @@
+"""CPU oracle for the Int8-weight LoRA linear -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
+import this package.  The product path (``reels_b200``) never calls it and
+fails loudly when its CUDA library is missing.
+
+Two restatements of the reference arithmetic live here:
+
+* ``reels_oracle.c`` (wrapped below): bit-exact quantiser
+  (src/layers/quantization.jl:35-44), fp32/fp16/bf16 materialisation
+  (quantization.jl:54-64, src/models/interface.jl:13-25), and the forward /
+  backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation: the gold
+  standard the CUDA results are compared against.
+* ``numpy_port.py``: the reference CPU code path in fp32 through OpenBLAS
+  (what Julia's LinearAlgebra calls), used as the timed CPU baseline.
+
+Parity status: no reference-produced vectors exist (Julia is not installed and
+the reference ships no golden files for this path), so parity against the
+reference's own outputs is UNPINNED.  The oracle is pinned by hand-derived
+known answers and by the reference tests' properties (tests/test_oracle.py).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_LIB = None
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+_i64 = ctypes.c_int64
+
+LAYOUT_OUT_CONTIGUOUS = 0  # Julia (out, in) column-major == row-major [K][N]
+LAYOUT_IN_CONTIGUOUS = 1   # PyTorch nn.Linear == row-major [N][K]
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = _build.build()
+        L = ctypes.CDLL(path)
+        L.oracle_quantize.argtypes = [_f32p, ctypes.c_int, _i64, _i64, _i8p, _f32p]
+        L.oracle_quantize.restype = ctypes.c_int
+        L.oracle_dequantize_f32.argtypes = [_i8p, _f32p, ctypes.c_int, _i64, _i64, _f32p]
+        L.oracle_dequantize_f16.argtypes = [_i8p, _f32p, ctypes.c_int, _i64, _i64, _u16p]
+        L.oracle_bf16_materialise_array.argtypes = [_i8p, _f32p, ctypes.c_int, _i64, _i64, _u16p]
+        L.oracle_bf16_round_array.argtypes = [_f32p, _i64, _u16p]
+        vp = ctypes.c_void_p
+        L.oracle_lora_forward.argtypes = [_f32p, _i8p, _f32p, ctypes.c_int, _f32p, _f32p, vp,
+                                          _i64, _i64, _i64, _i64, ctypes.c_float, _f32p, vp]
+        L.oracle_lora_backward.argtypes = [_f32p, _f32p, _i8p, _f32p, ctypes.c_int, _f32p, _f32p,
+                                           _i64, _i64, _i64, _i64, ctypes.c_float, vp, vp, vp]
+        L.oracle_rel_l2.argtypes = [_f32p, _f32p, _i64]
+        L.oracle_rel_l2.restype = ctypes.c_double
+        _LIB = L
+    return _LIB
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _wshape(layout, N, K):
+    return (K, N) if layout == LAYOUT_OUT_CONTIGUOUS else (N, K)
+
+
+def quantize(w: np.ndarray, layout: int = LAYOUT_OUT_CONTIGUOUS):
+    """Bit-exact restatement of quantization.jl:35-44.  ``w`` is given in
+    ``layout`` ([K][N] for the Julia layout, [N][K] for the PyTorch layout).
+    Returns (q int8 same shape as w, scales fp32 [N]).  Raises ValueError on
+    non-finite weights, as the reference does (InexactError)."""
+    w = _c(w, np.float32)
+    if layout == LAYOUT_OUT_CONTIGUOUS:
+        K, N = w.shape
+    else:
+        N, K = w.shape
+    q = np.empty(w.shape, np.int8)
+    s = np.empty((N,), np.float32)
+    rc = lib().oracle_quantize(w, layout, N, K, q, s)
+    if rc != 0:
+        raise ValueError("frozen weight contains non-finite values")
+    return q, s
+
+
+def dequantize_f32(q, scales, layout=LAYOUT_OUT_CONTIGUOUS):
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    N = scales.shape[0]
+    K = q.size // max(N, 1)
+    out = np.empty(q.shape, np.float32)
+    lib().oracle_dequantize_f32(q, scales, layout, N, K, out)
+    return out
+
+
+def dequantize_f16_bits(q, scales, layout=LAYOUT_OUT_CONTIGUOUS):
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    N = scales.shape[0]
+    K = q.size // max(N, 1)
+    out = np.empty(q.shape, np.uint16)
+    lib().oracle_dequantize_f16(q, scales, layout, N, K, out)
+    return out
+
+
+def dequantize_bf16_bits(q, scales, layout=LAYOUT_OUT_CONTIGUOUS):
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    N = scales.shape[0]
+    K = q.size // max(N, 1)
+    out = np.empty(q.shape, np.uint16)
+    lib().oracle_bf16_materialise_array(q, scales, layout, N, K, out)
+    return out
+
+
+def bf16_bits(x):
+    """interface.jl:19-25 rounding of fp32 to bf16 (returns uint16 bits)."""
+    x = _c(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().oracle_bf16_round_array(x, x.size, out)
+    return out
+
+
+def bf16_to_f32(bits):
+    """interface.jl:13-17: widen bf16 bits to fp32 exactly."""
+    bits = np.asarray(bits, np.uint16)
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x):
+    return bf16_to_f32(bf16_bits(x))
+
+
+def lora_forward(X, q, scales, layout, A, B, alpha, bias=None, want_T=False):
+    """Forward of lora.jl:56-95 on Wdq = Float32(q)*scale, fp64 accumulate.
+    X [M][K], A [K][r], B [r][N] -> Y [M][N] (and T [M][r] if want_T)."""
+    X = _c(X, np.float32)
+    A = _c(A, np.float32)
+    B = _c(B, np.float32)
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    M, K = X.shape
+    r = A.shape[1]
+    N = scales.shape[0]
+    Y = np.empty((M, N), np.float32)
+    T = np.empty((M, r), np.float32) if want_T else None
+    b = _c(bias, np.float32) if bias is not None else None
+    lib().oracle_lora_forward(X, q, scales, layout, A, B,
+                              b.ctypes.data if b is not None else None,
+                              M, K, N, r, float(alpha), Y,
+                              T.ctypes.data if T is not None else None)
+    return (Y, T) if want_T else Y
+
+
+def lora_backward(X, dY, q, scales, layout, A, B, alpha):
+    """lora.jl:106-118, fp64 accumulate.  Returns (dX [M][K], dA [K][r], dB [r][N])."""
+    X = _c(X, np.float32)
+    dY = _c(dY, np.float32)
+    A = _c(A, np.float32)
+    B = _c(B, np.float32)
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    M, K = X.shape
+    r = A.shape[1]
+    N = scales.shape[0]
+    dX = np.empty((M, K), np.float32)
+    dA = np.empty((K, r), np.float32)
+    dB = np.empty((r, N), np.float32)
+    lib().oracle_lora_backward(X, dY, q, scales, layout, A, B, M, K, N, r, float(alpha),
+                               dX.ctypes.data, dA.ctypes.data, dB.ctypes.data)
+    return dX, dA, dB
+
+
+def rel_l2(a, b) -> float:
+    a = _c(a, np.float32).ravel()
+    b = _c(b, np.float32).ravel()
+    return float(lib().oracle_rel_l2(a, b, a.size))

@@ -1,0 +1,242 @@
+/*
+ * CPU oracle for the Int8-weight LoRA linear (TEST INFRASTRUCTURE ONLY).
+ *
+ * This file restates, in plain C, the arithmetic of Reels.jl's quantised LoRA
+ * linear so that the CUDA path can be checked against it.  It is linked only by
+ * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg, never by the
+ * product library.
+ *
+ * Layout convention (matches the reference's column-major, feature-first
+ * arrays, written here as row-major C arrays):
+ *   X  [M][K]   activations  (Julia `x`  is (in, tokens))
+ *   Y  [M][N]   outputs      (Julia `y`  is (out, tokens))
+ *   W  [K][N]   "out-contiguous" (Julia weight (out, in))      layout 0
+ *      [N][K]   "in-contiguous"  (PyTorch nn.Linear weight)     layout 1
+ *   A  [K][r]   (Julia A is (rank, in))
+ *   B  [r][N]   (Julia B is (out, rank))
+ *   scales[N]   one fp32 scale per output row of the weight
+ *
+ * Parity status: the reference is Julia, which is not installed here, so no
+ * reference output could be generated.  The quantiser is pinned by hand-derived
+ * known answers (exact scales, ties-to-even), the linear algebra by the
+ * reference test properties (B = 0 identity, merged weight, finite
+ * differences).  Against reference-produced vectors parity is UNPINNED.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stddef.h>
+#include <string.h>
+#include <stdlib.h>
+
+#define OIDX_W(layout, n, k, N, K) ((layout) == 0 ? ((int64_t)(k) * (N) + (n)) : ((int64_t)(n) * (K) + (k)))
+
+/* quantization.jl:35-44 `quantize_frozen_matrix`:
+ *   maxima = maximum(abs, host; dims=2)       (fp32, per output row)
+ *   scales = maxima ./ 127f0                  (IEEE fp32 division)
+ *   scales[maxima .== 0f0] .= 1f0
+ *   values = Int8.(round.(clamp.(host ./ scales, -127f0, 127f0)))
+ * Julia's `round` is RoundNearest (ties to even); `rintf` under the default
+ * FE_TONEAREST mode is the same rule.  Returns -1 if any weight is not finite:
+ * the reference raises InexactError converting NaN to Int8 there. */
+int oracle_quantize(const float *w, int layout, int64_t N, int64_t K, int8_t *q, float *scales)
+{
+    int bad = 0;
+    for (int64_t n = 0; n < N; ++n) {
+        float m = 0.0f;
+        for (int64_t k = 0; k < K; ++k) {
+            float v = w[OIDX_W(layout, n, k, N, K)];
+            if (!isfinite(v)) bad = 1;
+            float a = fabsf(v);
+            if (a > m) m = a;
+        }
+        volatile float s = m / 127.0f;          /* keep the IEEE division */
+        float sc = (m == 0.0f) ? 1.0f : s;
+        scales[n] = sc;
+        for (int64_t k = 0; k < K; ++k) {
+            int64_t i = OIDX_W(layout, n, k, N, K);
+            volatile float t = w[i] / sc;
+            float c = t;
+            if (c > 127.0f) c = 127.0f;
+            if (c < -127.0f) c = -127.0f;
+            q[i] = (int8_t)(int)rintf(c);
+        }
+    }
+    return bad ? -1 : 0;
+}
+
+/* quantization.jl:63-64 `_dequantize_for_compute(values, scales, Float32)`:
+ * Float32.(values) .* Float32.(scales), written in the weight's own layout. */
+void oracle_dequantize_f32(const int8_t *q, const float *scales, int layout, int64_t N, int64_t K, float *out)
+{
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t k = 0; k < K; ++k) {
+            int64_t i = OIDX_W(layout, n, k, N, K);
+            out[i] = (float)q[i] * scales[n];
+        }
+}
+
+/* quantization.jl:61-62 `_dequantize_for_compute(values, scales, Float16)`:
+ * Float16.(values) .* Float16.(scales); the product is rounded to fp16.
+ * Output is the fp16 bit pattern. */
+void oracle_dequantize_f16(const int8_t *q, const float *scales, int layout, int64_t N, int64_t K, uint16_t *out)
+{
+    for (int64_t n = 0; n < N; ++n) {
+        _Float16 s = (_Float16)scales[n];
+        for (int64_t k = 0; k < K; ++k) {
+            int64_t i = OIDX_W(layout, n, k, N, K);
+            _Float16 v = (_Float16)(float)q[i];
+            _Float16 p = v * s;
+            memcpy(&out[i], &p, 2);
+        }
+    }
+}
+
+/* interface.jl:19-25 `bfloat16_values`: round fp32 to bf16 with
+ * (bits + 0x7fff + ((bits >> 16) & 1)) >> 16. */
+uint16_t oracle_bf16_from_f32(float x)
+{
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    b = b + 0x7fffu + ((b >> 16) & 1u);
+    return (uint16_t)(b >> 16);
+}
+
+/* interface.jl:13-17 `float32_values`: bf16 bits << 16. */
+float oracle_f32_from_bf16(uint16_t h)
+{
+    uint32_t b = (uint32_t)h << 16;
+    float x;
+    memcpy(&x, &b, 4);
+    return x;
+}
+
+void oracle_bf16_round_array(const float *x, int64_t n, uint16_t *out)
+{
+    for (int64_t i = 0; i < n; ++i) out[i] = oracle_bf16_from_f32(x[i]);
+}
+
+void oracle_bf16_materialise_array(const int8_t *q, const float *scales, int layout, int64_t N, int64_t K, uint16_t *out)
+{
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t k = 0; k < K; ++k) {
+            int64_t i = OIDX_W(layout, n, k, N, K);
+            out[i] = oracle_bf16_from_f32((float)q[i] * scales[n]);
+        }
+}
+
+/* Forward, lora.jl:56-95 with training=false / dropout 0, on the fp32
+ * dequantised weight Wdq = Float32(q) * scale (quantization.jl:63-64):
+ *   y  = Wdq * x            (quantization.jl:73-74)
+ *   y += bias               (lora.jl:64-67, mixed_add)
+ *   T  = A * x              (lora.jl:86, inner product)
+ *   y += (alpha/r) * B * T  (lora.jl:86-94)
+ * Inputs are fp32 (bf16/fp16 inputs are widened exactly by the caller);
+ * accumulation is fp64, the result is rounded once to fp32.
+ * T_out (nullable) receives T as [M][r]. */
+void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, int layout,
+                         const float *A, const float *B, const float *bias,
+                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         float *Y, float *T_out)
+{
+    double s = r > 0 ? (double)(alpha / (float)r) : 0.0;  /* r = 0: no adapter */
+    double *T = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
+    float *Wd = (float *)malloc(sizeof(float) * (size_t)(N * K));
+    oracle_dequantize_f32(q, scales, layout, N, K, Wd);
+    #pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        const float *x = X + m * K;
+        for (int64_t j = 0; j < r; ++j) {
+            double acc = 0.0;
+            for (int64_t k = 0; k < K; ++k) acc += (double)x[k] * (double)A[k * r + j];
+            T[m * r + j] = acc;
+            if (T_out) T_out[m * r + j] = (float)acc;
+        }
+        for (int64_t n = 0; n < N; ++n) {
+            double acc = 0.0;
+            for (int64_t k = 0; k < K; ++k)
+                acc += (double)x[k] * (double)Wd[OIDX_W(layout, n, k, N, K)];
+            if (bias) acc += (double)bias[n];
+            double lora = 0.0;
+            for (int64_t j = 0; j < r; ++j) lora += T[m * r + j] * (double)B[j * N + n];
+            Y[m * N + n] = (float)(acc + s * lora);
+        }
+    }
+    free(Wd);
+    free(T);
+}
+
+/* Backward, lora.jl:106-118 (identical to Zygote's pullback of lora_forward
+ * through the rrule at ad_rules.jl:70-80):
+ *   ax = A * x
+ *   dA = s * (B' * dy) * x'           -> [K][r] here (Julia (r, in))
+ *   dB = s * dy * ax'                 -> [r][N] here (Julia (out, r))
+ *   dx = Wdq' * dy + s * A' * (B' * dy)
+ * fp64 accumulation, fp32 results.  Any of dX, dA, dB may be NULL. */
+void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, const float *scales, int layout,
+                          const float *A, const float *B,
+                          int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                          float *dX, float *dA, float *dB)
+{
+    double s = r > 0 ? (double)(alpha / (float)r) : 0.0;  /* r = 0: no adapter */
+    double *G = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
+    double *T = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
+    float *Wd = (float *)malloc(sizeof(float) * (size_t)(N * K));
+    oracle_dequantize_f32(q, scales, layout, N, K, Wd);
+    #pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        for (int64_t j = 0; j < r; ++j) {
+            double g = 0.0, t = 0.0;
+            for (int64_t n = 0; n < N; ++n) g += (double)dY[m * N + n] * (double)B[j * N + n];
+            for (int64_t k = 0; k < K; ++k) t += (double)X[m * K + k] * (double)A[k * r + j];
+            G[m * r + j] = g;
+            T[m * r + j] = t;
+        }
+    }
+    if (dX) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t m = 0; m < M; ++m) {
+            for (int64_t k = 0; k < K; ++k) {
+                double acc = 0.0;
+                for (int64_t n = 0; n < N; ++n)
+                    acc += (double)dY[m * N + n] * (double)Wd[OIDX_W(layout, n, k, N, K)];
+                double lora = 0.0;
+                for (int64_t j = 0; j < r; ++j) lora += (double)A[k * r + j] * G[m * r + j];
+                dX[m * K + k] = (float)(acc + s * lora);
+            }
+        }
+    }
+    if (dA) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t k = 0; k < K; ++k)
+            for (int64_t j = 0; j < r; ++j) {
+                double acc = 0.0;
+                for (int64_t m = 0; m < M; ++m) acc += G[m * r + j] * (double)X[m * K + k];
+                dA[k * r + j] = (float)(s * acc);
+            }
+    }
+    if (dB) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t n = 0; n < N; ++n)
+            for (int64_t j = 0; j < r; ++j) {
+                double acc = 0.0;
+                for (int64_t m = 0; m < M; ++m) acc += (double)dY[m * N + n] * T[m * r + j];
+                dB[j * N + n] = (float)(s * acc);
+            }
+    }
+    free(Wd);
+    free(T);
+    free(G);
+}
+
+/* Relative L2 error ||a - b|| / ||b|| in fp64 (the north-star metric). */
+double oracle_rel_l2(const float *a, const float *b, int64_t n)
+{
+    double num = 0.0, den = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        double d = (double)a[i] - (double)b[i];
+        num += d * d;
+        den += (double)b[i] * (double)b[i];
+    }
+    if (den == 0.0) return num == 0.0 ? 0.0 : INFINITY;
+    return sqrt(num / den);
+}

@@ -1,0 +1,26 @@
+"""B200-native (sm_100a) Int8-weight LoRA linear for Reels.jl's low-VRAM path.
+
+The compute lives in libreels_lowvram.so (include/reels_lowvram.h); this
+package is the Python-side mirror of the reference's layer API
+(:mod:`reels_b200.lowvram`) and its data-parallel gradient all-reduce
+(:mod:`reels_b200.distributed`).
+"""
+from .lowvram import (  # noqa: F401
+    DenseLayer,
+    LoRALinear,
+    LoRALinearFunction,
+    QuantizedMatrix,
+    check_device_status,
+    linear,
+    lora_backward,
+    lora_forward,
+    materialize_weight,
+    merged_weight,
+    quantize_frozen_matrix,
+    saved_buffer,
+    set_adapter_enabled,
+    weight_mul,
+    weight_transpose_mul,
+)
+
+__version__ = "0.1.0"

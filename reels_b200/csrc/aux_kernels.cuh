@@ -1,0 +1,255 @@
+// Memory-bound helper kernels: the bit-exact quantiser, weight
+// materialisation, the rank-r transpose, split-K reductions, and the
+// CUDA-core "generic" path that serves shapes and dtypes the tensor-core
+// path does not take (ragged feature sizes, fp32 activations).
+#pragma once
+#include "common.cuh"
+
+namespace reels {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// ----------------------------------------------------------- quantiser
+// src/layers/quantization.jl:35-44, per output row n:
+//   m = max_k |w[n,k]| (fp32),  s = m / 127 (IEEE),  s = 1 if m == 0,
+//   q = Int8(round(clamp(w / s, -127, 127)))   with round = ties-to-even.
+// Layout 0 (Julia (out, in) column-major): w[k*N + n].  One block handles
+// 32 consecutive rows n (one per lane, coalesced along n); its 8 warps split
+// the k range and combine maxima in shared memory.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_outcontig_kernel(const T *__restrict__ w, int64_t N, int64_t K,
+                                                                 int8_t *__restrict__ q, float *__restrict__ scales,
+                                                                 unsigned *err) {
+    __shared__ float smax[8][32];
+    __shared__ float sscale[32];
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int64_t n = (int64_t)blockIdx.x * 32 + lane;
+    float m = 0.0f;
+    bool bad = false;
+    if (n < N) {
+        for (int64_t k = wp; k < K; k += 8) {
+            float v = to_f32(w[k * N + n]);
+            bad |= !isfinite(v);
+            m = fmaxf(m, fabsf(v));
+        }
+    }
+    smax[wp][lane] = m;
+    __syncthreads();
+    if (wp == 0) {
+        float mm = smax[0][lane];
+        for (int i = 1; i < 8; ++i) mm = fmaxf(mm, smax[i][lane]);
+        const float s = (mm == 0.0f) ? 1.0f : __fdiv_rn(mm, 127.0f);
+        sscale[lane] = s;
+        if (n < N) scales[n] = s;
+    }
+    if (bad) atomicOr(err, DEVERR_NONFINITE_WEIGHT);
+    __syncthreads();
+    if (n < N) {
+        const float s = sscale[lane];
+        for (int64_t k = wp; k < K; k += 8) {
+            float t = __fdiv_rn(to_f32(w[k * N + n]), s);
+            t = fminf(fmaxf(t, -127.0f), 127.0f);
+            q[k * N + n] = (int8_t)__float2int_rn(t);
+        }
+    }
+}
+
+// Layout 1 (PyTorch nn.Linear): w[n*K + k]; one warp per row.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_incontig_kernel(const T *__restrict__ w, int64_t N, int64_t K,
+                                                                int8_t *__restrict__ q, float *__restrict__ scales,
+                                                                unsigned *err) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const T *row = w + n * K;
+    float m = 0.0f;
+    bool bad = false;
+    for (int64_t k = lane; k < K; k += 32) {
+        float v = to_f32(row[k]);
+        bad |= !isfinite(v);
+        m = fmaxf(m, fabsf(v));
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(err, DEVERR_NONFINITE_WEIGHT);
+    const float s = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
+    if (lane == 0) scales[n] = s;
+    int8_t *qr = q + n * K;
+    for (int64_t k = lane; k < K; k += 32) {
+        float t = __fdiv_rn(to_f32(row[k]), s);
+        t = fminf(fmaxf(t, -127.0f), 127.0f);
+        qr[k] = (int8_t)__float2int_rn(t);
+    }
+}
+
+// ------------------------------------------------------- materialise
+// quantization.jl:54-64: fp16 -> Float16(q) * Float16(s) rounded to fp16;
+// fp32 -> Float32(q) * s; bf16 (not offered by the reference) -> the fp32
+// product rounded once to bf16, the rule of interface.jl:19-25.
+__global__ void materialize_kernel(const int8_t *__restrict__ q, const float *__restrict__ scales, int layout,
+                                   int64_t N, int64_t K, int out_dt, void *out) {
+    const int64_t total = N * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = (layout == 0) ? (i % N) : (i / K);
+        const float s = scales[n];
+        const float qv = (float)q[i];
+        if (out_dt == DT_F16) {
+            reinterpret_cast<__half *>(out)[i] = __hmul(__float2half_rn(qv), __float2half_rn(s));
+        } else if (out_dt == DT_BF16) {
+            reinterpret_cast<__nv_bfloat16 *>(out)[i] = __float2bfloat16_rn(qv * s);
+        } else {
+            reinterpret_cast<float *>(out)[i] = qv * s;
+        }
+    }
+}
+
+// A [K][r] -> At [r][K] (same element type, 2 bytes).
+__global__ void transpose_rank_kernel(const uint16_t *__restrict__ a, int64_t K, int r, uint16_t *__restrict__ at) {
+    const int64_t total = K * r;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / K, k = i % K;
+        at[i] = a[k * r + j];
+    }
+}
+
+// -------------------------------------------------- split-K reductions
+// Sum q8 partials [splits][M][Nout] and apply the output epilogue.
+__global__ void q8_reduce_kernel(const float *__restrict__ partial, int splits, int64_t M, int64_t Nout,
+                                 const float *__restrict__ col_scale, const void *bias, int dt, void *out,
+                                 int64_t ldo) {
+    const int64_t total = M * Nout;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = 0.0f;
+        for (int s = 0; s < splits; ++s) acc += partial[(int64_t)s * total + i];
+        const int64_t row = i / Nout, col = i % Nout;
+        if (col_scale) acc *= col_scale[col];
+        if (bias) acc += load_act(bias, col, dt);
+        store_act(out, row * ldo + col, dt, acc);
+    }
+}
+
+// Sum skinny partials [splits][rows][npad] and apply epi 0 (transposed
+// store, act dtype) or epi 1 (fp32 accumulate into out[row*rs + j*cs]).
+__global__ void sk_reduce_kernel(const float *__restrict__ partial, int splits, int64_t rows, int npad, int ncols,
+                                 int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
+                                 int64_t cs) {
+    const int64_t total = rows * (int64_t)ncols;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / rows, row = i % rows;
+        float acc = 0.0f;
+        for (int s = 0; s < splits; ++s) acc += partial[((int64_t)s * rows + row) * npad + j];
+        if (epi == 0) {
+            store_act(out, j * ldo + row, dt, alpha * acc);
+        } else {
+            float *o = reinterpret_cast<float *>(out);
+            const int64_t idx = row * rs + j * cs;
+            o[idx] = (accumulate ? o[idx] : 0.0f) + alpha * acc;
+        }
+    }
+}
+
+// ------------------------------------------------- generic (CUDA cores)
+// One thread per output element, fp32 accumulation, any shape.  Weight
+// element (n, k) is dequantised as fp32(q) * s[n] (quantization.jl:63-64).
+__device__ __forceinline__ float wdq(const int8_t *q, const float *s, int layout, int64_t N, int64_t K, int64_t n,
+                                     int64_t k) {
+    const int64_t idx = (layout == 0) ? (k * N + n) : (n * K + k);
+    return (float)q[idx] * s[n];
+}
+
+// T[j][m] (act dtype, pitch ldt) = sum_k X[m][k] * A[k][j]
+__global__ void gen_rank_down_kernel(const void *x, const void *a, int64_t M, int64_t K, int r, int dt, void *t,
+                                     int64_t ldt) {
+    const int64_t total = M * (int64_t)r;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / M, m = i % M;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < K; ++k) acc += load_act(x, m * K + k, dt) * load_act(a, k * r + j, dt);
+        store_act(t, j * ldt + m, dt, acc);
+    }
+}
+
+// G[j][m] (act dtype) = alpha * sum_n dY[m][n] * B[j][n]
+__global__ void gen_rank_grad_kernel(const void *dy, const void *b, int64_t M, int64_t N, int r, float alpha, int dt,
+                                     void *g, int64_t ldg) {
+    const int64_t total = M * (int64_t)r;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / M, m = i % M;
+        float acc = 0.0f;
+        for (int64_t n = 0; n < N; ++n) acc += load_act(dy, m * N + n, dt) * load_act(b, j * N + n, dt);
+        store_act(g, j * ldg + m, dt, alpha * acc);
+    }
+}
+
+// Y[m][n] = sum_k X[m][k] Wdq(n,k) + bias[n] + s * sum_j T[j][m] B[j][n]
+__global__ void gen_forward_kernel(const void *x, const int8_t *q, const float *sc, int layout, const void *bias,
+                                   const void *t, int64_t ldt, const void *b, int64_t M, int64_t K, int64_t N, int r,
+                                   float s, int dt, void *y) {
+    const int64_t total = M * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / N, n = i % N;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < K; ++k) acc += load_act(x, m * K + k, dt) * wdq(q, sc, layout, N, K, n, k);
+        if (bias) acc += load_act(bias, n, dt);
+        float lora = 0.0f;
+        for (int j = 0; j < r; ++j) lora += load_act(t, j * ldt + m, dt) * load_act(b, (int64_t)j * N + n, dt);
+        store_act(y, i, dt, acc + s * lora);
+    }
+}
+
+// dX[m][k] = sum_n dY[m][n] Wdq(n,k) + sum_j G[j][m] A[k][j]   (G already * s)
+__global__ void gen_dx_kernel(const void *dy, const int8_t *q, const float *sc, int layout, const void *g,
+                              int64_t ldg, const void *a, int64_t M, int64_t K, int64_t N, int r, int dt, void *dx) {
+    const int64_t total = M * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / K, k = i % K;
+        float acc = 0.0f;
+        for (int64_t n = 0; n < N; ++n) acc += load_act(dy, m * N + n, dt) * wdq(q, sc, layout, N, K, n, k);
+        float lora = 0.0f;
+        for (int j = 0; j < r; ++j) lora += load_act(g, j * ldg + m, dt) * load_act(a, k * r + j, dt);
+        store_act(dx, i, dt, acc + lora);
+    }
+}
+
+// dA[k][j] = beta*dA + alpha * sum_m G[j][m] X[m][k]
+__global__ void gen_da_kernel(const void *g, int64_t ldg, const void *x, int64_t M, int64_t K, int r, float alpha,
+                              int accumulate, int dt, float *da) {
+    const int64_t total = K * (int64_t)r;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t k = i / r, j = i % r;
+        float acc = 0.0f;
+        for (int64_t m = 0; m < M; ++m) acc += load_act(g, j * ldg + m, dt) * load_act(x, m * K + k, dt);
+        da[i] = (accumulate ? da[i] : 0.0f) + alpha * acc;
+    }
+}
+
+// dB[j][n] = beta*dB + alpha * sum_m dY[m][n] T[j][m]
+__global__ void gen_db_kernel(const void *dy, const void *t, int64_t ldt, int64_t M, int64_t N, int r, float alpha,
+                              int accumulate, int dt, float *db) {
+    const int64_t total = N * (int64_t)r;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / N, n = i % N;
+        float acc = 0.0f;
+        for (int64_t m = 0; m < M; ++m) acc += load_act(dy, m * N + n, dt) * load_act(t, j * ldt + m, dt);
+        db[i] = (accumulate ? db[i] : 0.0f) + alpha * acc;
+    }
+}
+
+}  // namespace reels

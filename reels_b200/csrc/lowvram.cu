@@ -1,0 +1,831 @@
+// Host side of libreels_lowvram.so: argument checks, tile planning, TMA
+// tensor maps and kernel launches behind the C ABI of include/reels_lowvram.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/reels_lowvram.h"
+#include "aux_kernels.cuh"
+#include "tc_kernels.cuh"
+
+using namespace reels;
+
+// Status words the kernels OR error bits into (one per device context).
+__device__ unsigned g_dev_status;
+__device__ unsigned g_quant_status;
+
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_last_path = REELS_PATH_NONE;
+
+// Opt-in profiling: events around each q8 GEMM launch on its own stream.
+struct Profile {
+    bool on = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pool;
+    size_t used = 0;
+    double flops = 0.0;
+};
+thread_local Profile t_prof;
+thread_local long long t_launches = 0;
+
+inline void count_launch(int n = 1) { t_launches += n; }
+
+int fail(const std::string &msg) {
+    t_last_error = msg;
+    return REELS_EINVAL;
+}
+int fail_dev(const std::string &msg) {
+    t_last_error = msg;
+    return REELS_EDEVICE;
+}
+int ok(int path) {
+    t_last_error.clear();
+    t_last_path = path;
+    return REELS_OK;
+}
+
+#define REELS_LAUNCHED()                                                                                \
+    do {                                                                                                \
+        cudaError_t e_ = cudaGetLastError();                                                            \
+        if (e_ != cudaSuccess) return fail_dev(std::string("kernel launch: ") + cudaGetErrorString(e_)); \
+        count_launch();                                                                                 \
+    } while (0)
+
+#define REELS_CUDA(call)                                                                                \
+    do {                                                                                                \
+        cudaError_t e_ = (call);                                                                        \
+        if (e_ != cudaSuccess) return fail_dev(std::string(#call) + ": " + cudaGetErrorString(e_));    \
+    } while (0)
+
+// ------------------------------------------------------------ device state
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    bool ready = false;
+    int sms = 148;
+    unsigned *status = nullptr;
+    unsigned *quant_status = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+
+int bind_device(const void *ptr, DeviceState **out) {
+    int dev = -1;
+    cudaPointerAttributes attr;
+    if (ptr && cudaPointerGetAttributes(&attr, ptr) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {
+        dev = attr.device;
+    } else {
+        cudaGetLastError();
+        REELS_CUDA(cudaGetDevice(&dev));
+    }
+    if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
+    int cur = -1;
+    REELS_CUDA(cudaGetDevice(&cur));
+    if (cur != dev) REELS_CUDA(cudaSetDevice(dev));
+    std::lock_guard<std::mutex> lock(g_dev_mu);
+    DeviceState &st = g_dev[dev];
+    if (!st.ready) {
+        int major = 0, minor = 0;
+        REELS_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+        REELS_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+        if (major != 10 || minor != 0)
+            return fail("libreels_lowvram is built for sm_100a (B200); device " + std::to_string(dev) +
+                        " is sm_" + std::to_string(major) + std::to_string(minor));
+        REELS_CUDA(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev));
+        REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.status), g_dev_status));
+        REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.quant_status), g_quant_status));
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_BF16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8Geom<1>::SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_BF16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8Geom<2>::SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_F16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8Geom<1>::SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_F16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8Geom<2>::SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SK_SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SK_SMEM_BYTES));
+        if (!g_encode) {
+            void *fn = nullptr;
+            cudaDriverEntryPointQueryResult qr;
+            REELS_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr));
+            if (qr != cudaDriverEntryPointSuccess || !fn) return fail_dev("cuTensorMapEncodeTiled unavailable");
+            g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+        }
+        st.ready = true;
+    }
+    *out = &st;
+    return REELS_OK;
+}
+
+// ------------------------------------------------------------- tensor maps
+int tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, uint64_t inner, uint64_t outer,
+            uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(tm, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[200];
+        snprintf(buf, sizeof buf, "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu pitch %llu box %u x %u", (int)r,
+                 (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)pitch_bytes, box_inner,
+                 box_outer);
+        return fail(buf);
+    }
+    return REELS_OK;
+}
+
+CUtensorMapDataType tma_act_type(int dt) {
+    return dt == REELS_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// ---------------------------------------------------------------- planning
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+int esize(int dt) { return dt == REELS_F32 ? 4 : 2; }
+int64_t ld_tokens(int64_t M) { return round_up(std::max<int64_t>(M, 1), 8); }
+
+struct Split {
+    int splits = 1;
+    int kb_per = 1;
+};
+
+// Spread the reduction over more CTAs when the output tiles alone do not
+// fill the machine; every split keeps at least `min_kb` blocks of 64.
+Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb) {
+    Split s;
+    kb = std::max<int64_t>(kb, 1);
+    int64_t want = 1;
+    if (tiles < sms) want = cdiv(sms, tiles);
+    want = std::min<int64_t>(want, std::max<int64_t>(1, kb / min_kb));
+    want = std::max<int64_t>(want, 1);
+    s.kb_per = (int)cdiv(kb, want);
+    s.splits = (int)cdiv(kb, s.kb_per);
+    return s;
+}
+
+struct Q8Plan {
+    int mt = 1;
+    int64_t ntiles = 1, mtiles = 1;
+    Split split;
+};
+
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
+    Q8Plan p;
+    const int64_t nt = cdiv(Nout, Q8_BN);
+    const int64_t t1 = nt * cdiv(M, 128), t2 = nt * cdiv(M, 256);
+    const double c1 = (double)cdiv(t1, sms), c2 = 2.0 * (double)cdiv(t2, sms);
+    p.mt = (M >= 256 && c2 <= 1.1 * c1) ? 2 : 1;
+    p.ntiles = nt;
+    p.mtiles = cdiv(M, 128 * p.mt);
+    p.split = plan_split(p.ntiles * p.mtiles, cdiv(Kred, BK), sms, 4);
+    return p;
+}
+
+Split plan_sk(int64_t rows, int64_t red, int sms) { return plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4); }
+
+int npad_of(int64_t r) { return (int)std::max<int64_t>(16, round_up(r, 16)); }
+
+// Workspace layout shared by the forward and backward passes.
+struct Ws {
+    size_t at = 0, tbuf = 0, gbuf = 0, part = 0, total = 0;
+};
+
+Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int sms) {
+    Ws w;
+    const int64_t ldm = ld_tokens(M);
+    size_t off = 0;
+    const size_t at_bytes = r > 0 ? align256((size_t)r * K * 2) : 0;
+    const size_t tg_bytes = r > 0 ? align256((size_t)r * ldm * esize(dt)) : 0;
+    w.at = off;
+    off += at_bytes;
+    w.tbuf = off;
+    off += tg_bytes;
+    w.gbuf = off;
+    if (pass == REELS_PASS_BACKWARD) off += tg_bytes;
+    size_t part = 0;
+    const int64_t np = npad_of(r);
+    auto sk_part = [&](int64_t rows, int64_t red) {
+        Split s = plan_sk(rows, red, sms);
+        if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
+    };
+    auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
+        Q8Plan p = plan_q8(rows, cols, red, sms);
+        if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
+    };
+    if (M > 0) {
+        if (r > 0) sk_part(M, K);  // A*x (forward, or recompute in the backward)
+        if (pass == REELS_PASS_FORWARD) {
+            q8_part(M, N, K);
+        } else {
+            if (r > 0) {
+                sk_part(M, N);  // B'*dy
+                sk_part(K, M);  // dA
+                sk_part(N, M);  // dB
+            }
+            q8_part(M, K, N);
+        }
+    }
+    w.part = off;
+    off += align256(part);
+    w.total = off;
+    return w;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int layout) {
+    if (M < 0 || K <= 0 || N <= 0) return fail("dimensions must be positive (M may be 0)");
+    if (r < 0 || r > 256) return fail("LoRA rank must be in [0, 256]");
+    if (dt != REELS_F32 && dt != REELS_F16 && dt != REELS_BF16) return fail("unknown activation dtype");
+    if (layout != REELS_W_OUT_CONTIGUOUS && layout != REELS_W_IN_CONTIGUOUS) return fail("unknown weight layout");
+    if (K > INT32_MAX / 2 || N > INT32_MAX / 2 || M > INT32_MAX / 2) return fail("dimension too large");
+    return REELS_OK;
+}
+
+int launch_grid(int64_t total) { return (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), 148 * 16)); }
+
+// -------------------------------------------------------- tensor-core ops
+// D[rows][r] = act[rows][red] . Bop[r][red]^T  (A-op K-major), or
+// D[rows][r] = act[red][rows]^T . Bop[r][red]^T (A-op MN-major), epilogue epi.
+struct SkCall {
+    const void *act;     // 16-bit activation tensor
+    int64_t act_inner;   // contiguous extent of act
+    int64_t act_outer;
+    bool a_mn;
+    const void *bop;     // 16-bit [r][red], row pitch bop_pitch elements
+    int64_t bop_pitch;
+    int64_t rows, red, r;
+    int epi_final;       // 0 transposed store, 1 fp32 accumulate
+    float alpha;
+    int accumulate;
+    void *out;
+    int64_t ldo, rs, cs;
+};
+
+int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
+    CUtensorMap ta, tb;
+    int rc;
+    const uint64_t pitch = (uint64_t)c.act_inner * 2;
+    if (c.a_mn) rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.act_inner, c.act_outer, pitch, 64, 64,
+                             CU_TENSOR_MAP_SWIZZLE_128B);
+    else rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.act_inner, c.act_outer, pitch, 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const int np = npad_of(c.r);
+    rc = tmap_2d(&tb, c.bop, tma_act_type(dt), c.red, c.r, (uint64_t)c.bop_pitch * 2, 64, np,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    Split s = plan_sk(c.rows, c.red, ds.sms);
+    SkArgs a;
+    a.rows = (int)c.rows;
+    a.kb_total = (int)cdiv(c.red, BK);
+    a.kb_per_split = s.kb_per;
+    a.npad = np;
+    a.a_mn = c.a_mn ? 1 : 0;
+    a.ncols = (int)c.r;
+    a.alpha = c.alpha;
+    a.accumulate = c.accumulate;
+    a.out = c.out;
+    a.ldo = c.ldo;
+    a.rs = c.rs;
+    a.cs = c.cs;
+    a.partial = reinterpret_cast<float *>(ws_base + wl.part);
+    a.err = ds.status;
+    a.epi = s.splits > 1 ? 2 : c.epi_final;
+    dim3 grid((unsigned)cdiv(c.rows, 128), (unsigned)s.splits);
+    if (dt == REELS_BF16) sk_gemm_kernel<DT_BF16><<<grid, SK_THREADS, SK_SMEM_BYTES, st>>>(ta, tb, a);
+    else sk_gemm_kernel<DT_F16><<<grid, SK_THREADS, SK_SMEM_BYTES, st>>>(ta, tb, a);
+    REELS_LAUNCHED();
+    if (s.splits > 1) {
+        sk_reduce_kernel<<<launch_grid(c.rows * c.r), 256, 0, st>>>(a.partial, s.splits, c.rows, np, (int)c.r,
+                                                                    c.epi_final, c.alpha, c.accumulate, dt, c.out,
+                                                                    c.ldo, c.rs, c.cs);
+        REELS_LAUNCHED();
+    }
+    return REELS_OK;
+}
+
+// Q8 GEMM: D[M][Nout] over reduction Kred of act[M][Kred] and the int8 weight,
+// plus the LoRA extension.  `fwd` selects the weight orientation.
+struct Q8Call {
+    bool fwd;
+    const void *act;   // [M][Kred]
+    int64_t M, Nout, Kred;
+    const int8_t *q;
+    const float *scales;
+    int layout;
+    int64_t N_w, K_w;  // weight dims (out, in)
+    int64_t r;
+    const void *ext_act;  // [r][ldm] 16-bit
+    const void *lora;     // fwd: B [r][N]; dX: A [K][r]
+    float ext_scale;
+    const void *bias;
+    void *out;
+};
+
+int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms);
+    CUtensorMap ta, tw, te;
+    int rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, 128 * p.mt,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    // Weight tensor as stored: layout 0 is [K][N] (inner N), layout 1 is [N][K] (inner K).
+    const uint64_t w_inner = c.layout == REELS_W_OUT_CONTIGUOUS ? c.N_w : c.K_w;
+    const uint64_t w_outer = c.layout == REELS_W_OUT_CONTIGUOUS ? c.K_w : c.N_w;
+    // Orientation 0 (staging rows = D columns) when the weight's contiguous
+    // dimension is the reduction: forward on [N][K], dX on [K][N].
+    const bool inner_is_red = c.fwd ? (c.layout == REELS_W_IN_CONTIGUOUS) : (c.layout == REELS_W_OUT_CONTIGUOUS);
+    const int orient = inner_is_red ? 0 : 1;
+    if (orient == 0) rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, 256,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+    else rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 256, 64,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    const int64_t ldm = ld_tokens(c.M);
+    if (c.r > 0) {
+        rc = tmap_2d(&te, c.ext_act, tma_act_type(dt), c.M, c.r, (uint64_t)ldm * 2, 64, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    } else {
+        te = ta;
+    }
+    Q8Args a;
+    memset(&a, 0, sizeof a);
+    a.M = (int)c.M;
+    a.Nout = (int)c.Nout;
+    a.kb_total = (int)cdiv(c.Kred, BK);
+    a.kb_per_split = p.split.kb_per;
+    a.w_orient = orient;
+    a.wscale = c.scales;
+    a.wscale_len = (int)c.N_w;
+    if (c.fwd) {
+        // bf16: exact int8 in the MMA, per-column scale in the epilogue.
+        // fp16: scale folded into the dequant (keeps B*s in fp16 range).
+        if (dt == REELS_BF16) {
+            a.scale_mode = 0;
+            a.col_scale = c.scales;
+            a.ext_div = c.scales;
+        } else {
+            a.scale_mode = orient == 0 ? 1 : 2;
+            a.col_scale = nullptr;
+            a.ext_div = nullptr;
+        }
+        a.ext_kind = 0;
+    } else {
+        // dX: the scale sits on the reduction index n.
+        a.scale_mode = orient == 1 ? 1 : 2;
+        a.col_scale = nullptr;
+        a.ext_div = nullptr;
+        a.ext_kind = 1;
+    }
+    a.r = (int)c.r;
+    a.lora = c.lora;
+    a.ext_scale = c.ext_scale;
+    a.bias = c.bias;
+    a.out = c.out;
+    a.ldo = c.Nout;
+    a.partial = reinterpret_cast<float *>(ws_base + wl.part);
+    a.epi_partial = p.split.splits > 1 ? 1 : 0;
+    a.err = ds.status;
+    dim3 grid((unsigned)p.ntiles, (unsigned)p.mtiles, (unsigned)p.split.splits);
+    cudaEvent_t ev_stop = nullptr;
+    if (t_prof.on) {
+        if (t_prof.used == t_prof.pool.size()) {
+            cudaEvent_t a, b;
+            REELS_CUDA(cudaEventCreate(&a));
+            REELS_CUDA(cudaEventCreate(&b));
+            t_prof.pool.emplace_back(a, b);
+        }
+        auto &pr = t_prof.pool[t_prof.used++];
+        REELS_CUDA(cudaEventRecord(pr.first, st));
+        ev_stop = pr.second;
+        t_prof.flops += 2.0 * (double)c.M * (double)c.Nout * (double)(c.Kred + c.r);
+    }
+    if (dt == REELS_BF16) {
+        if (p.mt == 2) q8_gemm_kernel<DT_BF16, 2><<<grid, Q8_THREADS, Q8Geom<2>::SMEM_BYTES, st>>>(ta, tw, te, a);
+        else q8_gemm_kernel<DT_BF16, 1><<<grid, Q8_THREADS, Q8Geom<1>::SMEM_BYTES, st>>>(ta, tw, te, a);
+    } else {
+        if (p.mt == 2) q8_gemm_kernel<DT_F16, 2><<<grid, Q8_THREADS, Q8Geom<2>::SMEM_BYTES, st>>>(ta, tw, te, a);
+        else q8_gemm_kernel<DT_F16, 1><<<grid, Q8_THREADS, Q8Geom<1>::SMEM_BYTES, st>>>(ta, tw, te, a);
+    }
+    REELS_LAUNCHED();
+    if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
+    if (p.split.splits > 1) {
+        q8_reduce_kernel<<<launch_grid(c.M * c.Nout), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+                                                                    a.col_scale, c.bias, dt, c.out, c.Nout);
+        REELS_LAUNCHED();
+    }
+    return REELS_OK;
+}
+
+bool tc_eligible(int64_t K, int64_t N, int dt, std::initializer_list<const void *> ptrs) {
+    if (dt == REELS_F32) return false;
+    if (K % 16 != 0 || N % 16 != 0) return false;
+    for (const void *p : ptrs)
+        if (p && !aligned16(p)) return false;
+    return true;
+}
+
+int check_ws(void *ws, size_t ws_bytes, const Ws &wl) {
+    if (wl.total == 0) return REELS_OK;
+    if (!ws) return fail("workspace is NULL; size it with reels_q8lora_workspace_bytes");
+    if (ws_bytes < wl.total)
+        return fail("workspace too small: need " + std::to_string(wl.total) + " bytes, got " +
+                    std::to_string(ws_bytes));
+    if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail("workspace must be 256-byte aligned");
+    return REELS_OK;
+}
+
+// A [K][r] -> At [r][K]
+int transpose_rank(const void *A, int64_t K, int64_t r, void *At, cudaStream_t st) {
+    transpose_rank_kernel<<<launch_grid(K * r), 256, 0, st>>>(reinterpret_cast<const uint16_t *>(A), K, (int)r,
+                                                              reinterpret_cast<uint16_t *>(At));
+    REELS_LAUNCHED();
+    return REELS_OK;
+}
+
+int rank_down_tc(const void *x, const void *A, int64_t M, int64_t K, int64_t r, int dt, void *tbuf, void *at,
+                 const DeviceState &ds, char *ws, const Ws &wl, cudaStream_t st) {
+    int rc = transpose_rank(A, K, r, at, st);
+    if (rc) return rc;
+    SkCall c{};
+    c.act = x;
+    c.act_inner = K;
+    c.act_outer = M;
+    c.a_mn = false;
+    c.bop = at;
+    c.bop_pitch = K;
+    c.rows = M;
+    c.red = K;
+    c.r = r;
+    c.epi_final = 0;
+    c.alpha = 1.0f;
+    c.out = tbuf;
+    c.ldo = ld_tokens(M);
+    return run_sk(c, dt, ds, ws, wl, st);
+}
+
+}  // namespace
+
+// =====================================================================
+extern "C" {
+
+const char *reels_lowvram_last_error(void) { return t_last_error.c_str(); }
+int reels_lowvram_abi_version(void) { return REELS_LOWVRAM_ABI_VERSION; }
+int reels_lowvram_last_path(void) { return t_last_path; }
+
+int reels_lowvram_profile_enable(int enable) {
+    t_prof.on = enable != 0;
+    t_prof.used = 0;
+    t_prof.flops = 0.0;
+    t_launches = 0;
+    return REELS_OK;
+}
+
+int reels_lowvram_profile_read(double *q8_ms, int64_t *q8_launches, double *q8_flops, int64_t *kernel_launches) {
+    double total = 0.0;
+    for (size_t i = 0; i < t_prof.used; ++i) {
+        REELS_CUDA(cudaEventSynchronize(t_prof.pool[i].second));
+        float ms = 0.0f;
+        REELS_CUDA(cudaEventElapsedTime(&ms, t_prof.pool[i].first, t_prof.pool[i].second));
+        total += ms;
+    }
+    if (q8_ms) *q8_ms = total;
+    if (q8_launches) *q8_launches = (int64_t)t_prof.used;
+    if (q8_flops) *q8_flops = t_prof.flops;
+    if (kernel_launches) *kernel_launches = t_launches;
+    t_prof.used = 0;
+    t_prof.flops = 0.0;
+    t_launches = 0;
+    return REELS_OK;
+}
+
+int reels_lowvram_check_device_status(void *stream) {
+    DeviceState *ds;
+    int rc = bind_device(nullptr, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned h = 0, zero = 0;
+    REELS_CUDA(cudaStreamSynchronize(st));
+    REELS_CUDA(cudaMemcpy(&h, ds->status, 4, cudaMemcpyDeviceToHost));
+    if (h) {
+        REELS_CUDA(cudaMemcpy(ds->status, &zero, 4, cudaMemcpyHostToDevice));
+        char buf[128];
+        snprintf(buf, sizeof buf, "device status 0x%x: a pipeline wait timed out", h);
+        return fail_dev(buf);
+    }
+    t_last_error.clear();
+    return REELS_OK;
+}
+
+int reels_q8_quantize(const void *w, int w_dtype, int layout, int64_t N, int64_t K, int8_t *q, float *scales,
+                      void *stream) {
+    if (!w || !q || !scales) return fail("null pointer passed to reels_q8_quantize");
+    if (N <= 0 || K <= 0) return fail("weight dimensions must be positive");
+    if (layout != REELS_W_OUT_CONTIGUOUS && layout != REELS_W_IN_CONTIGUOUS) return fail("unknown weight layout");
+    if (w_dtype != REELS_F32 && w_dtype != REELS_F16 && w_dtype != REELS_BF16) return fail("unknown weight dtype");
+    DeviceState *ds;
+    int rc = bind_device(w, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    REELS_CUDA(cudaMemsetAsync(ds->quant_status, 0, 4, st));
+    if (layout == REELS_W_OUT_CONTIGUOUS) {
+        dim3 grid((unsigned)cdiv(N, 32));
+        if (w_dtype == REELS_F32)
+            quantize_outcontig_kernel<float><<<grid, 256, 0, st>>>((const float *)w, N, K, q, scales,
+                                                                   ds->quant_status);
+        else if (w_dtype == REELS_F16)
+            quantize_outcontig_kernel<__half><<<grid, 256, 0, st>>>((const __half *)w, N, K, q, scales,
+                                                                    ds->quant_status);
+        else
+            quantize_outcontig_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16 *)w, N, K, q,
+                                                                           scales, ds->quant_status);
+    } else {
+        dim3 grid((unsigned)cdiv(N, 8));
+        if (w_dtype == REELS_F32)
+            quantize_incontig_kernel<float><<<grid, 256, 0, st>>>((const float *)w, N, K, q, scales,
+                                                                  ds->quant_status);
+        else if (w_dtype == REELS_F16)
+            quantize_incontig_kernel<__half><<<grid, 256, 0, st>>>((const __half *)w, N, K, q, scales,
+                                                                   ds->quant_status);
+        else
+            quantize_incontig_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16 *)w, N, K, q,
+                                                                          scales, ds->quant_status);
+    }
+    REELS_LAUNCHED();
+    unsigned h = 0;
+    REELS_CUDA(cudaMemcpyAsync(&h, ds->quant_status, 4, cudaMemcpyDeviceToHost, st));
+    REELS_CUDA(cudaStreamSynchronize(st));
+    if (h & DEVERR_NONFINITE_WEIGHT) return fail("frozen weight contains non-finite values (NaN or Inf)");
+    return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_q8_materialize(const int8_t *q, const float *scales, int layout, int64_t N, int64_t K, int out_dtype,
+                         void *out, void *stream) {
+    if (!q || !scales || !out) return fail("null pointer passed to reels_q8_materialize");
+    if (N <= 0 || K <= 0) return fail("weight dimensions must be positive");
+    if (layout != REELS_W_OUT_CONTIGUOUS && layout != REELS_W_IN_CONTIGUOUS) return fail("unknown weight layout");
+    if (out_dtype != REELS_F32 && out_dtype != REELS_F16 && out_dtype != REELS_BF16) return fail("unknown dtype");
+    DeviceState *ds;
+    int rc = bind_device(q, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    materialize_kernel<<<launch_grid(N * K), 256, 0, st>>>(q, scales, layout, N, K, out_dtype, out);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
+}
+
+size_t reels_q8lora_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int act_dtype, int pass) {
+    if (M < 0 || K <= 0 || N <= 0 || r < 0) return 0;
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    } else {
+        cudaGetLastError();
+    }
+    return ws_layout(M, K, N, r, act_dtype, pass, sms).total;
+}
+
+size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype) {
+    if (M < 0 || r <= 0) return 0;
+    return (size_t)r * ld_tokens(M) * esize(act_dtype);
+}
+
+int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                         const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         int dt, void *y, void *saved, void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_common(M, K, N, r, dt, layout);
+    if (rc) return rc;
+    if (!x || !q || !scales || !y) return fail("null x, q, scales or y");
+    if (r > 0 && (!A || !B)) return fail("null LoRA A or B");
+    if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
+    if (M == 0) return ok(REELS_PATH_NONE);
+    DeviceState *ds;
+    rc = bind_device(x, &ds);
+    if (rc) return rc;
+    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_FORWARD, ds->sms);
+    rc = check_ws(workspace, ws_bytes, wl);
+    if (rc) return rc;
+    if (saved && !aligned16(saved)) return fail("saved buffer must be 16-byte aligned");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char *ws = reinterpret_cast<char *>(workspace);
+    const float s = r > 0 ? alpha / (float)r : 0.0f;
+    const int64_t ldm = ld_tokens(M);
+    void *tbuf = r > 0 ? (saved ? saved : ws + wl.tbuf) : nullptr;
+
+    if (tc_eligible(K, N, dt, {x, q, y, B, saved})) {
+        if (r > 0) {
+            rc = rank_down_tc(x, A, M, K, r, dt, tbuf, ws + wl.at, *ds, ws, wl, st);
+            if (rc) return rc;
+        }
+        Q8Call c{};
+        c.fwd = true;
+        c.act = x;
+        c.M = M;
+        c.Nout = N;
+        c.Kred = K;
+        c.q = q;
+        c.scales = scales;
+        c.layout = layout;
+        c.N_w = N;
+        c.K_w = K;
+        c.r = r;
+        c.ext_act = tbuf;
+        c.lora = B;
+        c.ext_scale = s;
+        c.bias = bias;
+        c.out = y;
+        rc = run_q8(c, dt, *ds, ws, wl, st);
+        if (rc) return rc;
+        return ok(REELS_PATH_TENSORCORE);
+    }
+    if (r > 0) {
+        gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(x, A, M, K, (int)r, dt, tbuf, ldm);
+        REELS_LAUNCHED();
+    }
+    gen_forward_kernel<<<launch_grid(M * N), 256, 0, st>>>(x, q, scales, layout, bias, tbuf, ldm, B, M, K, N,
+                                                           (int)r, s, dt, y);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int layout, const void *bias, int64_t M,
+                        int64_t K, int64_t N, int act_dtype, void *y, void *workspace, size_t ws_bytes,
+                        void *stream) {
+    return reels_q8lora_forward(x, q, scales, layout, nullptr, nullptr, bias, M, K, N, 0, 1.0f, act_dtype, y,
+                                nullptr, workspace, ws_bytes, stream);
+}
+
+int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                          const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N, int64_t r,
+                          float alpha, float grad_scale, int dt, void *dx, float *dA, float *dB, int accumulate,
+                          void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_common(M, K, N, r, dt, layout);
+    if (rc) return rc;
+    if (!dy || !q || !scales) return fail("null dy, q or scales");
+    if (r > 0 && (!A || !B || !dA || !dB || !x)) return fail("null x, A, B, dA or dB with r > 0");
+    if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
+    if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
+    if (!dx && r == 0) return ok(REELS_PATH_NONE);
+    DeviceState *ds;
+    rc = bind_device(dy, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (M == 0) {
+        // No tokens: gradients are zero (or unchanged when accumulating).
+        if (r > 0 && !accumulate) {
+            REELS_CUDA(cudaMemsetAsync(dA, 0, sizeof(float) * K * r, st));
+            REELS_CUDA(cudaMemsetAsync(dB, 0, sizeof(float) * N * r, st));
+        }
+        return ok(REELS_PATH_NONE);
+    }
+    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_BACKWARD, ds->sms);
+    rc = check_ws(workspace, ws_bytes, wl);
+    if (rc) return rc;
+    if (saved && !aligned16(saved)) return fail("saved buffer must be 16-byte aligned");
+    char *ws = reinterpret_cast<char *>(workspace);
+    const float s = r > 0 ? alpha / (float)r : 0.0f;
+    const int64_t ldm = ld_tokens(M);
+    const void *tbuf = r > 0 ? (saved ? saved : (const void *)(ws + wl.tbuf)) : nullptr;
+    void *gbuf = r > 0 ? (void *)(ws + wl.gbuf) : nullptr;
+
+    if (tc_eligible(K, N, dt, {x, dy, q, dx, B, saved})) {
+        if (r > 0) {
+            if (!saved) {
+                rc = rank_down_tc(x, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st);
+                if (rc) return rc;
+            }
+            // g' = s * (B' * dy), stored [r][ldm]
+            SkCall g{};
+            g.act = dy;
+            g.act_inner = N;
+            g.act_outer = M;
+            g.a_mn = false;
+            g.bop = B;
+            g.bop_pitch = N;
+            g.rows = M;
+            g.red = N;
+            g.r = r;
+            g.epi_final = 0;
+            g.alpha = s;
+            g.out = gbuf;
+            g.ldo = ldm;
+            rc = run_sk(g, dt, *ds, ws, wl, st);
+            if (rc) return rc;
+        }
+        if (dx) {
+            Q8Call c{};
+            c.fwd = false;
+            c.act = dy;
+            c.M = M;
+            c.Nout = K;
+            c.Kred = N;
+            c.q = q;
+            c.scales = scales;
+            c.layout = layout;
+            c.N_w = N;
+            c.K_w = K;
+            c.r = r;
+            c.ext_act = gbuf;
+            c.lora = A;
+            c.ext_scale = 1.0f;
+            c.bias = nullptr;
+            c.out = dx;
+            rc = run_q8(c, dt, *ds, ws, wl, st);
+            if (rc) return rc;
+        }
+        if (r > 0) {
+            // dA[k][j] = grad_scale * sum_m g'[j][m] x[m][k]
+            SkCall da{};
+            da.act = x;
+            da.act_inner = K;
+            da.act_outer = M;
+            da.a_mn = true;
+            da.bop = gbuf;
+            da.bop_pitch = ldm;
+            da.rows = K;
+            da.red = M;
+            da.r = r;
+            da.epi_final = 1;
+            da.alpha = grad_scale;
+            da.accumulate = accumulate;
+            da.out = dA;
+            da.rs = r;
+            da.cs = 1;
+            rc = run_sk(da, dt, *ds, ws, wl, st);
+            if (rc) return rc;
+            // dB[j][n] = grad_scale * s * sum_m dy[m][n] t[j][m]
+            SkCall db{};
+            db.act = dy;
+            db.act_inner = N;
+            db.act_outer = M;
+            db.a_mn = true;
+            db.bop = tbuf;
+            db.bop_pitch = ldm;
+            db.rows = N;
+            db.red = M;
+            db.r = r;
+            db.epi_final = 1;
+            db.alpha = grad_scale * s;
+            db.accumulate = accumulate;
+            db.out = dB;
+            db.rs = 1;
+            db.cs = N;
+            rc = run_sk(db, dt, *ds, ws, wl, st);
+            if (rc) return rc;
+        }
+        return ok(REELS_PATH_TENSORCORE);
+    }
+
+    if (r > 0) {
+        if (!saved) {
+            gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(x, A, M, K, (int)r, dt, ws + wl.tbuf, ldm);
+            REELS_LAUNCHED();
+        }
+        gen_rank_grad_kernel<<<launch_grid(M * r), 256, 0, st>>>(dy, B, M, N, (int)r, s, dt, gbuf, ldm);
+        REELS_LAUNCHED();
+    }
+    if (dx) {
+        gen_dx_kernel<<<launch_grid(M * K), 256, 0, st>>>(dy, q, scales, layout, gbuf, ldm, A, M, K, N, (int)r, dt,
+                                                          dx);
+        REELS_LAUNCHED();
+    }
+    if (r > 0) {
+        gen_da_kernel<<<launch_grid(K * r), 256, 0, st>>>(gbuf, ldm, x, M, K, (int)r, grad_scale, accumulate, dt, dA);
+        REELS_LAUNCHED();
+        gen_db_kernel<<<launch_grid(N * r), 256, 0, st>>>(dy, tbuf, ldm, M, N, (int)r, grad_scale * s, accumulate, dt,
+                                                          dB);
+        REELS_LAUNCHED();
+    }
+    return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *scales, int layout, int64_t M,
+                                  int64_t K, int64_t N, int act_dtype, void *dx, void *workspace, size_t ws_bytes,
+                                  void *stream) {
+    if (!dx) return fail("null dx");
+    return reels_q8lora_backward(nullptr, dy, q, scales, layout, nullptr, nullptr, nullptr, M, K, N, 0, 1.0f, 1.0f,
+                                 act_dtype, dx, nullptr, nullptr, 0, workspace, ws_bytes, stream);
+}
+
+}  // extern "C"

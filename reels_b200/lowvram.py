@@ -1,0 +1,403 @@
+"""Python mirror of Reels.jl's quantised frozen-weight / LoRA layer API.
+
+Names, argument meaning and error behaviour follow the reference:
+
+==============================  ===============================================
+reference (src/...)             here
+==============================  ===============================================
+QuantizedMatrix                 :class:`QuantizedMatrix` (layers/quantization.jl:5-9)
+quantize_frozen_matrix          :func:`quantize_frozen_matrix` (quantization.jl:35-44)
+_materialize_weight             :func:`materialize_weight` (quantization.jl:54-64)
+_weight_mul                     :func:`weight_mul` (quantization.jl:73-74)
+_weight_transpose_mul           :func:`weight_transpose_mul` (quantization.jl:75-76)
+DenseLayer / linear             :class:`DenseLayer`, :func:`linear` (layers/linear.jl:1-46)
+LoRALinear                      :class:`LoRALinear` (layers/lora.jl:1-35)
+lora_forward                    :func:`lora_forward` (lora.jl:56-95)
+lora_backward                   :func:`lora_backward` (lora.jl:106-118)
+merged_weight                   :func:`merged_weight` (lora.jl:120-122)
+rrule(_weight_mul) / Zygote     :class:`LoRALinearFunction` (training/ad_rules.jl:70-80)
+==============================  ===============================================
+
+Shapes: parameters keep the reference's logical shapes (weight (out, in),
+A (rank, in), B (out, rank)); activations are tokens-first, ``x`` (..., in),
+which is the same memory as the reference's feature-first column-major
+``(in, tokens...)``.  The reference stores parameters column-major; a tensor
+here may be either column-major (a transposed view, zero-copy) or row-major.
+
+All arithmetic runs in libreels_lowvram.so on the GPU.  Tensors must be CUDA
+tensors; there is no CPU execution path (the reference's own CPU path is
+restated only in the test oracle).
+"""
+from __future__ import annotations
+
+from collections import namedtuple
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _native as nat
+
+_DT = {torch.float32: nat.F32, torch.float16: nat.F16, torch.bfloat16: nat.BF16}
+
+
+def _dt(dtype) -> int:
+    try:
+        return _DT[dtype]
+    except KeyError:
+        raise ValueError(f"unsupported compute precision: {dtype}") from None
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("low-VRAM int8 kernels require CUDA tensors (no CPU path)")
+
+
+class _Workspace:
+    """Per-device scratch buffer, grown on demand by the caller side (the
+    native library itself never allocates)."""
+
+    def __init__(self):
+        self._bufs = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.type, device.index)
+        buf = self._bufs.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self._bufs[key] = buf
+        return buf
+
+
+_WS = _Workspace()
+
+
+def _workspace(device, M, K, N, r, dt, which):
+    n = nat.lib().reels_q8lora_workspace_bytes(M, K, N, r, dt, which)
+    buf = _WS.get(device, n)
+    return buf.data_ptr(), buf.numel()
+
+
+# ------------------------------------------------------------- QuantizedMatrix
+@dataclass
+class QuantizedMatrix:
+    """Per-output-channel symmetric Int8 storage of a frozen linear weight
+    (quantization.jl:5-9).  ``values`` has logical shape (out, in) and is
+    either column-major (the reference's layout: out-contiguous) or
+    row-major; ``scales`` is fp32 (out,).  ``dtype`` is the compute dtype
+    produced when the weight is materialised."""
+
+    values: torch.Tensor
+    scales: torch.Tensor
+    dtype: torch.dtype = torch.float32
+
+    @property
+    def shape(self):
+        return tuple(self.values.shape)
+
+    def size(self, dim=None):
+        return self.values.shape if dim is None else self.values.shape[dim]
+
+    @property
+    def layout(self) -> int:
+        return _weight_layout(self.values)
+
+    def __getitem__(self, idx):
+        # quantization.jl:18-19: T(values[i, j]) * T(scales[i])
+        i, j = idx
+        return (self.values[i, j].to(torch.float32) * self.scales[i]).to(self.dtype)
+
+
+def _weight_layout(values: torch.Tensor) -> int:
+    N, K = values.shape
+    if values.stride() == (1, N) or (K == 1 and values.stride()[0] == 1):
+        return nat.W_OUT_CONTIGUOUS
+    if values.is_contiguous():
+        return nat.W_IN_CONTIGUOUS
+    raise ValueError("QuantizedMatrix values must be row- or column-major")
+
+
+def _wmem(values: torch.Tensor) -> int:
+    _weight_layout(values)
+    return values.data_ptr()
+
+
+def quantize_frozen_matrix(weight: torch.Tensor, dtype: Optional[torch.dtype] = None,
+                           layout: Optional[int] = None) -> QuantizedMatrix:
+    """Bit-exact per-row Int8 quantisation (quantization.jl:35-44).
+
+    ``weight`` has logical shape (out, in); its memory layout (column-major as
+    in the reference, or row-major) is kept for the int8 values unless
+    ``layout`` asks for the other one.  Raises ValueError on non-finite
+    weights, as the reference raises InexactError."""
+    _require_cuda(weight)
+    if weight.dim() != 2:
+        raise ValueError("frozen weight must be a matrix")
+    N, K = weight.shape
+    if dtype is None:
+        dtype = weight.dtype
+    src_layout = _weight_layout(weight) if (weight.stride() == (1, N) or weight.is_contiguous()) else nat.W_IN_CONTIGUOUS
+    if layout is None:
+        layout = src_layout
+    if layout == nat.W_OUT_CONTIGUOUS:
+        w_mem = weight.t().contiguous()           # [K][N]
+        values = torch.empty((K, N), dtype=torch.int8, device=weight.device).t()
+    else:
+        w_mem = weight.contiguous()                # [N][K]
+        values = torch.empty((N, K), dtype=torch.int8, device=weight.device)
+    scales = torch.empty((N,), dtype=torch.float32, device=weight.device)
+    code = nat.lib().reels_q8_quantize(w_mem.data_ptr(), _dt(w_mem.dtype), layout, N, K, values.data_ptr(),
+                                       scales.data_ptr(), _stream(weight.device))
+    nat.check("quantize_frozen_matrix", code)
+    return QuantizedMatrix(values, scales, dtype)
+
+
+def materialize_weight(weight: QuantizedMatrix, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """_materialize_weight / _dequantize_for_compute (quantization.jl:54-64);
+    returns a dense (out, in) tensor in the values' memory layout."""
+    dtype = dtype or weight.dtype
+    v = weight.values
+    _require_cuda(v)
+    N, K = v.shape
+    layout = weight.layout
+    if layout == nat.W_OUT_CONTIGUOUS:
+        out = torch.empty((K, N), dtype=dtype, device=v.device).t()
+    else:
+        out = torch.empty((N, K), dtype=dtype, device=v.device)
+    code = nat.lib().reels_q8_materialize(v.data_ptr(), weight.scales.data_ptr(), layout, N, K, _dt(dtype),
+                                          out.data_ptr(), _stream(v.device))
+    nat.check("materialize_weight", code)
+    return out
+
+
+def _flat(x: torch.Tensor, feat: int):
+    if x.shape[-1] != feat:
+        raise ValueError("input and weight dimensions differ")  # DimensionMismatch in the reference
+    return x.reshape(-1, feat).contiguous()
+
+
+def weight_mul(weight: QuantizedMatrix, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """_weight_mul (quantization.jl:73-74): y = dequant(W) x (+ bias)."""
+    N, K = weight.shape
+    _require_cuda(x, weight.values)
+    xf = _flat(x, K)
+    M = xf.shape[0]
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    dt = _dt(x.dtype)
+    ws, wsn = _workspace(x.device, M, K, N, 0, dt, nat.PASS_FORWARD)
+    b = bias.contiguous().to(x.dtype) if bias is not None else None
+    code = nat.lib().reels_q8_weight_mul(xf.data_ptr(), _wmem(weight.values), weight.scales.data_ptr(),
+                                         weight.layout, _ptr(b), M, K, N, dt, y.data_ptr(), ws, wsn,
+                                         _stream(x.device))
+    nat.check("weight_mul", code)
+    return y.reshape(*x.shape[:-1], N)
+
+
+def weight_transpose_mul(weight: QuantizedMatrix, dy: torch.Tensor) -> torch.Tensor:
+    """_weight_transpose_mul (quantization.jl:75-76): dx = dequant(W)' dy."""
+    N, K = weight.shape
+    _require_cuda(dy, weight.values)
+    dyf = _flat(dy, N)
+    M = dyf.shape[0]
+    dx = torch.empty((M, K), dtype=dy.dtype, device=dy.device)
+    dt = _dt(dy.dtype)
+    ws, wsn = _workspace(dy.device, M, K, N, 0, dt, nat.PASS_BACKWARD)
+    code = nat.lib().reels_q8_weight_transpose_mul(dyf.data_ptr(), _wmem(weight.values), weight.scales.data_ptr(),
+                                                   weight.layout, M, K, N, dt, dx.data_ptr(), ws, wsn,
+                                                   _stream(dy.device))
+    nat.check("weight_transpose_mul", code)
+    return dx.reshape(*dy.shape[:-1], K)
+
+
+# ------------------------------------------------------------------- layers
+@dataclass
+class DenseLayer:
+    """Frozen dense layer (linear.jl:1-4) over a QuantizedMatrix."""
+
+    weight: QuantizedMatrix
+    bias: Optional[torch.Tensor] = None
+
+
+def linear(layer: DenseLayer, x: torch.Tensor) -> torch.Tensor:
+    """linear (linear.jl:38-46)."""
+    return weight_mul(layer.weight, x, layer.bias)
+
+
+class LoRALinear:
+    """LoRA adapter over a frozen (Int8) weight (lora.jl:1-35).
+
+    ``A`` (rank, in) and ``B`` (out, rank) are stored column-major, as in the
+    reference; ``alpha``/``rank`` is the adapter scale."""
+
+    def __init__(self, weight: QuantizedMatrix, bias=None, A=None, B=None, alpha=None, dropout=0.0,
+                 enabled=True, train_bias=False, rank=None, generator=None):
+        N, K = weight.shape
+        if A is None:
+            # lora.jl:13-28: A ~ randn / sqrt(in), B = 0
+            if rank is None or rank <= 0:
+                raise ValueError("rank must be positive")
+            dev = weight.values.device
+            A = (torch.randn((K, rank), generator=generator, device=dev, dtype=torch.float32)
+                 * (1.0 / K ** 0.5)).to(weight.dtype).t()
+            B = torch.zeros((rank, N), device=dev, dtype=weight.dtype).t()
+        r = A.shape[0]
+        if alpha is None:
+            alpha = float(r)
+        if not (torch.isfinite(torch.tensor(float(alpha))) and alpha > 0):
+            raise ValueError("alpha must be finite and positive")
+        if not (0 <= dropout < 1):
+            raise ValueError("dropout must be in [0, 1)")
+        if train_bias and bias is None:
+            raise ValueError("cannot train a missing linear bias")
+        if tuple(A.shape) != (r, K) or tuple(B.shape) != (N, r):
+            raise ValueError("LoRA A must be (rank, in) and B (out, rank)")
+        self.weight = weight
+        self.bias = bias.clone() if (train_bias and bias is not None) else bias
+        self.base_bias = bias
+        self.A = A
+        self.B = B
+        self.alpha = float(alpha)
+        self.dropout = float(dropout)
+        self.enabled = bool(enabled)
+        self.train_bias = bool(train_bias)
+
+    @property
+    def rank(self) -> int:
+        return self.A.shape[0]
+
+    def __call__(self, x, **kw):
+        return lora_forward(self, x, **kw)
+
+
+def set_adapter_enabled(layer: LoRALinear, enabled: bool) -> LoRALinear:
+    layer.enabled = bool(enabled)
+    return layer
+
+
+def _colmajor(t: torch.Tensor, dtype) -> torch.Tensor:
+    """Memory of logical (a, b) tensor `t` as the reference's column-major
+    [b][a] contiguous array."""
+    return t.t().contiguous().to(dtype)
+
+
+def lora_forward(layer: LoRALinear, x: torch.Tensor, training: bool = False, dropout_seed=None,
+                 dropout_stream: int = 0, saved: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lora_forward (lora.jl:56-95).  ``saved`` (optional uint8 buffer of
+    reels_q8lora_saved_bytes) receives A*x for :func:`lora_backward`."""
+    if training and layer.dropout > 0:
+        raise NotImplementedError("LoRA dropout is not implemented on the native int8 path")
+    N, K = layer.weight.shape
+    _require_cuda(x, layer.weight.values)
+    xf = _flat(x, K)
+    M = xf.shape[0]
+    dt = _dt(x.dtype)
+    active_bias = layer.base_bias if (layer.train_bias and not layer.enabled) else layer.bias
+    b = active_bias.contiguous().to(x.dtype) if active_bias is not None else None
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    r = layer.rank if layer.enabled else 0
+    ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_FORWARD)
+    if r > 0:
+        A_mem = _colmajor(layer.A, x.dtype)   # [K][r]
+        B_mem = _colmajor(layer.B, x.dtype)   # [r][N]
+        code = nat.lib().reels_q8lora_forward(xf.data_ptr(), _wmem(layer.weight.values),
+                                              layer.weight.scales.data_ptr(), layer.weight.layout,
+                                              A_mem.data_ptr(), B_mem.data_ptr(), _ptr(b), M, K, N, r,
+                                              layer.alpha, dt, y.data_ptr(), _ptr(saved), ws, wsn,
+                                              _stream(x.device))
+    else:
+        code = nat.lib().reels_q8_weight_mul(xf.data_ptr(), _wmem(layer.weight.values),
+                                             layer.weight.scales.data_ptr(), layer.weight.layout, _ptr(b), M, K,
+                                             N, dt, y.data_ptr(), ws, wsn, _stream(x.device))
+    nat.check("lora_forward", code)
+    return y.reshape(*x.shape[:-1], N)
+
+
+LoRAGradients = namedtuple("LoRAGradients", ["dx", "A", "B"])
+
+
+def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: Optional[torch.Tensor] = None,
+                  grad_scale: float = 1.0, dA_acc: Optional[torch.Tensor] = None,
+                  dB_acc: Optional[torch.Tensor] = None, need_dx: bool = True) -> LoRAGradients:
+    """lora_backward (lora.jl:106-118) -> (dx, A=dA, B=dB).
+
+    dA/dB are fp32 with the logical shapes of A and B (column-major).  With
+    ``dA_acc``/``dB_acc`` given (fp32 accumulators of that memory layout) the
+    gradients times ``grad_scale`` are added into them instead."""
+    if tuple(x.shape[:-1]) != tuple(dy.shape[:-1]):
+        raise ValueError("LoRA input and output trailing dimensions differ")
+    N, K = layer.weight.shape
+    _require_cuda(x, dy, layer.weight.values)
+    xf = _flat(x, K)
+    dyf = _flat(dy, N)
+    M = xf.shape[0]
+    r = layer.rank
+    dt = _dt(x.dtype)
+    A_mem = _colmajor(layer.A, x.dtype)
+    B_mem = _colmajor(layer.B, x.dtype)
+    accumulate = dA_acc is not None
+    if accumulate:
+        dA_mem, dB_mem = dA_acc.t(), dB_acc.t()
+        if not (dA_mem.is_contiguous() and dB_mem.is_contiguous()):
+            raise ValueError("gradient accumulators must be column-major fp32")
+    else:
+        dA_mem = torch.empty((K, r), dtype=torch.float32, device=x.device)
+        dB_mem = torch.empty((r, N), dtype=torch.float32, device=x.device)
+    dx = torch.empty((M, K), dtype=x.dtype, device=x.device) if need_dx else None
+    ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_BACKWARD)
+    code = nat.lib().reels_q8lora_backward(xf.data_ptr(), dyf.data_ptr(), _wmem(layer.weight.values),
+                                           layer.weight.scales.data_ptr(), layer.weight.layout, A_mem.data_ptr(),
+                                           B_mem.data_ptr(), _ptr(saved), M, K, N, r, layer.alpha,
+                                           float(grad_scale), dt, _ptr(dx), dA_mem.data_ptr(), dB_mem.data_ptr(),
+                                           1 if accumulate else 0, ws, wsn, _stream(x.device))
+    nat.check("lora_backward", code)
+    return LoRAGradients(dx.reshape(x.shape) if dx is not None else None, dA_mem.t(), dB_mem.t())
+
+
+def saved_buffer(layer: LoRALinear, x: torch.Tensor) -> torch.Tensor:
+    """Allocate the buffer that carries A*x from the forward to the backward."""
+    M = x.numel() // x.shape[-1]
+    n = nat.lib().reels_q8lora_saved_bytes(M, layer.rank, _dt(x.dtype))
+    return torch.empty((max(n, 16),), dtype=torch.uint8, device=x.device)
+
+
+def merged_weight(layer: LoRALinear) -> torch.Tensor:
+    """merged_weight (lora.jl:120-122), fp32 (out, in) on the layer's device."""
+    w = materialize_weight(layer.weight, torch.float32)
+    s = layer.alpha / layer.rank
+    return w + s * (layer.B.float() @ layer.A.float())
+
+
+def check_device_status(device=None) -> None:
+    """Synchronise and raise if a kernel's bounded pipeline wait gave up."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    nat.check("device status", nat.lib().reels_lowvram_check_device_status(_stream(dev)))
+
+
+class LoRALinearFunction(torch.autograd.Function):
+    """Autograd rule for a quantised LoRALinear: the forward saves A*x, the
+    backward is the fused native backward.  The counterpart of the rrule that
+    routes the frozen weight's pullback to _weight_transpose_mul
+    (ad_rules.jl:70-80) plus Zygote's adjoints of B*(A*x)."""
+
+    @staticmethod
+    def forward(ctx, x, A, B, layer):
+        saved = saved_buffer(layer, x)
+        y = lora_forward(layer, x, saved=saved)
+        ctx.layer = layer
+        ctx.save_for_backward(x, saved)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, saved = ctx.saved_tensors
+        g = lora_backward(ctx.layer, x, dy.contiguous(), saved=saved)
+        return g.dx, g.A.to(ctx.layer.A.dtype), g.B.to(ctx.layer.B.dtype), None

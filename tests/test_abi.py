@@ -1,0 +1,99 @@
+"""CPU checks of the C ABI: the library loads, exports exactly what
+include/*.h declares, and rejects bad arguments before touching a GPU
+(status -1 plus a thread-local message, the convention of the reference's
+deps/sentencepiece_bridge.cpp:10-17)."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from reels_b200 import _native as nat
+from reels_b200 import build as native_build
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_functions():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names += re.findall(r"\b(reels_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    native_build.build()
+    return nat.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_functions()
+    assert declared, "no declarations found"
+    for name in declared:
+        assert hasattr(lib, name), name
+    # and the binding table covers the header exactly
+    assert sorted(nat.SIGNATURES) == declared
+
+
+def test_abi_version(lib):
+    assert lib.reels_lowvram_abi_version() == 1
+
+
+def test_workspace_queries_need_no_gpu(lib):
+    fw = lib.reels_q8lora_workspace_bytes(32760, 1536, 8960, 32, nat.BF16, nat.PASS_FORWARD)
+    bw = lib.reels_q8lora_workspace_bytes(32760, 1536, 8960, 32, nat.BF16, nat.PASS_BACKWARD)
+    assert fw > 0 and bw >= fw
+    assert lib.reels_q8lora_workspace_bytes(-1, 1, 1, 0, nat.BF16, 0) == 0
+    assert lib.reels_q8lora_saved_bytes(7, 3, nat.BF16) == 3 * 8 * 2   # tokens padded to 8
+    assert lib.reels_q8lora_saved_bytes(32760, 32, nat.F16) == 32 * 32760 * 2
+    assert lib.reels_q8lora_saved_bytes(5, 0, nat.BF16) == 0
+
+
+def _err(lib):
+    return lib.reels_lowvram_last_error().decode()
+
+
+@pytest.mark.parametrize("bad", ["null_x", "neg_dim", "rank", "dtype", "layout"])
+def test_forward_rejects_bad_arguments(lib, bad):
+    p = ctypes.c_void_p(0x1000)  # never dereferenced: checks run first
+    args = dict(x=p, q=p, s=p, layout=0, A=p, B=p, bias=None, M=4, K=16, N=16, r=2, alpha=2.0, dt=nat.BF16,
+                y=p, saved=None, ws=None, wsn=0, stream=None)
+    if bad == "null_x":
+        args["x"] = None
+    elif bad == "neg_dim":
+        args["K"] = -3
+    elif bad == "rank":
+        args["r"] = 1000
+    elif bad == "dtype":
+        args["dt"] = 9
+    elif bad == "layout":
+        args["layout"] = 5
+    rc = lib.reels_q8lora_forward(*args.values())
+    assert rc == nat.EINVAL
+    assert _err(lib) != ""
+
+
+def test_backward_rejects_null_gradients(lib):
+    p = ctypes.c_void_p(0x1000)
+    rc = lib.reels_q8lora_backward(p, p, p, p, 0, p, p, None, 4, 16, 16, 2, 2.0, 1.0, nat.BF16, p, None, None,
+                                   0, None, 0, None)
+    assert rc == nat.EINVAL
+    assert "dA" in _err(lib)
+
+
+def test_quantize_rejects_bad_arguments(lib):
+    p = ctypes.c_void_p(0x1000)
+    assert lib.reels_q8_quantize(None, nat.F32, 0, 4, 4, p, p, None) == nat.EINVAL
+    assert lib.reels_q8_quantize(p, nat.F32, 0, 0, 4, p, p, None) == nat.EINVAL
+    assert lib.reels_q8_materialize(p, p, 0, 4, 4, 7, p, None) == nat.EINVAL
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setenv("REELS_LOWVRAM_LIBRARY", str(tmp_path / "nope.so"))
+    monkeypatch.setattr(nat, "_lib", None)
+    with pytest.raises(RuntimeError, match="not found"):
+        nat.lib()
