@@ -52,6 +52,11 @@ def workload(config: str):
     if config == "cfg1":
         return dict(name="wan21-1.3b-ffn-up", layers=[("ffn_up", 1280, 1536, 8960)], tokens=1280, rank=16,
                     alpha=16.0)
+    if config == "ffn8k":
+        # One FFN up-projection at 8192 tokens: operands larger than L2 but a
+        # few hundred MB in total, the case the ncu captures use.
+        return dict(name="wan21-1.3b-ffn-up-8k", layers=[("ffn_up", 8192, 1536, 8960)], tokens=8192, rank=32,
+                    alpha=32.0)
     return dict(name="wan21-1.3b-block-linears", layers=block_layers(32760), tokens=32760, rank=32, alpha=32.0)
 
 
@@ -432,7 +437,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="block", choices=["block", "cfg1"])
+    ap.add_argument("--config", default="block", choices=["block", "cfg1", "ffn8k"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -82,14 +82,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
+// try_wait with a suspend-time hint: a waiting thread is parked (it issues
+// nothing) until the phase completes or the hint (ns) elapses, so pipeline
+// waits do not steal issue slots from the warps doing the work.
+#ifndef REELS_SUSPEND_HINT_NS
+#define REELS_SUSPEND_HINT_NS 1000000u
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
         : "memory");
     return ok != 0;
 }
@@ -219,8 +225,15 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
 }
 __device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
     uint2 v;
-    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
     return v;
+}
+
+// 32-byte global stores (sm_100): one instruction per 16 bf16/fp16 or 8 fp32.
+__device__ __forceinline__ void st_global_v8(void *p, uint4 a, uint4 b) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w),
+                 "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                 : "memory");
 }
 
 }  // namespace reels

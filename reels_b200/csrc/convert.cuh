@@ -55,45 +55,40 @@ __device__ __forceinline__ uint4 i8x8_to_f16(uint2 v) {
     return o;
 }
 
-// Exact fp32 value of byte i of (w ^ 0x80808080): the word 0x4B0000xx is the
-// float 2^23 + xx, and xx = q + 128, so subtracting 2^23 + 128 leaves q.
-__device__ __forceinline__ float byte_to_f32(uint32_t wx, uint32_t i) {
-    return __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | i)) - 8388736.0f;
+// Scaled path: byte i of (w ^ 0x80808080) placed under the exponent of
+// 2^23 gives the float 2^23 + q + 128 exactly; adding -(2^23 + 128) leaves q.
+// fp32(q) * scale rounded once to the 16-bit type; scale per element.
+// Packed f32x2 add/multiply (sm_100) halve the instruction count; the add
+// is exact (it recovers q), so the only rounding is the product's.
+template <int DT>
+__device__ __forceinline__ uint32_t scaled_pair(uint32_t wx, uint32_t i, float s0, float s1) {
+    const float2 magic = make_float2(-8388736.0f, -8388736.0f);
+    float2 f = make_float2(__int_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | i)),
+                           __int_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u | (i + 1))));
+    f = __fmul2_rn(__fadd2_rn(f, magic), make_float2(s0, s1));
+    return Elem<DT>::pack2(f.x, f.y);
 }
 
-// fp32(q) * scale rounded once to the 16-bit type; scale per element.
 template <int DT>
 __device__ __forceinline__ uint4 i8x8_scaled(uint2 v, const float (&sc)[8]) {
-    uint32_t a = v.x ^ 0x80808080u, b = v.y ^ 0x80808080u;
-    float f[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        f[i] = byte_to_f32(a, i) * sc[i];
-        f[i + 4] = byte_to_f32(b, i) * sc[i + 4];
-    }
+    const uint32_t a = v.x ^ 0x80808080u, b = v.y ^ 0x80808080u;
     uint4 o;
-    o.x = Elem<DT>::pack2(f[0], f[1]);
-    o.y = Elem<DT>::pack2(f[2], f[3]);
-    o.z = Elem<DT>::pack2(f[4], f[5]);
-    o.w = Elem<DT>::pack2(f[6], f[7]);
+    o.x = scaled_pair<DT>(a, 0, sc[0], sc[1]);
+    o.y = scaled_pair<DT>(a, 2, sc[2], sc[3]);
+    o.z = scaled_pair<DT>(b, 0, sc[4], sc[5]);
+    o.w = scaled_pair<DT>(b, 2, sc[6], sc[7]);
     return o;
 }
 
 // Same with one scale for all eight elements.
 template <int DT>
 __device__ __forceinline__ uint4 i8x8_scaled1(uint2 v, float s) {
-    uint32_t a = v.x ^ 0x80808080u, b = v.y ^ 0x80808080u;
-    float f[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        f[i] = byte_to_f32(a, i) * s;
-        f[i + 4] = byte_to_f32(b, i) * s;
-    }
+    const uint32_t a = v.x ^ 0x80808080u, b = v.y ^ 0x80808080u;
     uint4 o;
-    o.x = Elem<DT>::pack2(f[0], f[1]);
-    o.y = Elem<DT>::pack2(f[2], f[3]);
-    o.z = Elem<DT>::pack2(f[4], f[5]);
-    o.w = Elem<DT>::pack2(f[6], f[7]);
+    o.x = scaled_pair<DT>(a, 0, s, s);
+    o.y = scaled_pair<DT>(a, 2, s, s);
+    o.z = scaled_pair<DT>(b, 0, s, s);
+    o.w = scaled_pair<DT>(b, 2, s, s);
     return o;
 }
 

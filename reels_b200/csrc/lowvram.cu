@@ -9,11 +9,12 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/reels_lowvram.h"
 #include "aux_kernels.cuh"
-#include "tc_kernels.cuh"
+#include "q8_gemm.cuh"
 
 using namespace reels;
 
@@ -81,6 +82,20 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 
+template <int DT, int MT, int BN>
+cudaError_t set_q8_attr() {
+    return cudaFuncSetAttribute(q8_gemm_kernel<DT, MT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Q8Geom<MT, BN>::SMEM_BYTES);
+}
+template <int DT>
+cudaError_t set_q8_attrs() {
+    cudaError_t e;
+    if ((e = set_q8_attr<DT, 1, 128>()) != cudaSuccess) return e;
+    if ((e = set_q8_attr<DT, 1, 256>()) != cudaSuccess) return e;
+    if ((e = set_q8_attr<DT, 2, 128>()) != cudaSuccess) return e;
+    return set_q8_attr<DT, 2, 256>();
+}
+
 int bind_device(const void *ptr, DeviceState **out) {
     int dev = -1;
     cudaPointerAttributes attr;
@@ -91,9 +106,10 @@ int bind_device(const void *ptr, DeviceState **out) {
         REELS_CUDA(cudaGetDevice(&dev));
     }
     if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
-    int cur = -1;
-    REELS_CUDA(cudaGetDevice(&cur));
-    if (cur != dev) REELS_CUDA(cudaSetDevice(dev));
+    // Always bind: on a thread that has not used this device yet (e.g. an
+    // autograd worker) this also makes the primary context current, which
+    // the driver-API tensor-map encoder needs.
+    REELS_CUDA(cudaSetDevice(dev));
     std::lock_guard<std::mutex> lock(g_dev_mu);
     DeviceState &st = g_dev[dev];
     if (!st.ready) {
@@ -106,14 +122,8 @@ int bind_device(const void *ptr, DeviceState **out) {
         REELS_CUDA(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev));
         REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.status), g_dev_status));
         REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.quant_status), g_quant_status));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_BF16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8Geom<1>::SMEM_BYTES));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_BF16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8Geom<2>::SMEM_BYTES));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_F16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8Geom<1>::SMEM_BYTES));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_kernel<DT_F16, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8Geom<2>::SMEM_BYTES));
+        REELS_CUDA(set_q8_attrs<DT_BF16>());
+        REELS_CUDA(set_q8_attrs<DT_F16>());
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         SK_SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -182,21 +192,47 @@ Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb) {
 }
 
 struct Q8Plan {
-    int mt = 1;
+    int mt = 1, bn = 256;
     int64_t ntiles = 1, mtiles = 1;
     Split split;
 };
 
+// Tile shape from measured cycles per 64-wide reduction block and tile
+// shape.  The kernel is persistent, so a CTA runs ceil(tiles / SMs) tiles;
+// the cost is that count times the per-tile time.
 Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
-    Q8Plan p;
-    const int64_t nt = cdiv(Nout, Q8_BN);
-    const int64_t t1 = nt * cdiv(M, 128), t2 = nt * cdiv(M, 256);
-    const double c1 = (double)cdiv(t1, sms), c2 = 2.0 * (double)cdiv(t2, sms);
-    p.mt = (M >= 256 && c2 <= 1.1 * c1) ? 2 : 1;
-    p.ntiles = nt;
-    p.mtiles = cdiv(M, 128 * p.mt);
-    p.split = plan_split(p.ntiles * p.mtiles, cdiv(Kred, BK), sms, 4);
-    return p;
+    static const int forced = [] {
+        const char *e = getenv("REELS_Q8_TILE");  // "MTxBN", e.g. "2x128"
+        if (!e) return 0;
+        int a = 0, b = 0;
+        if (sscanf(e, "%dx%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 128 || b == 256)) return a * 1000 + b;
+        return 0;
+    }();
+    const int64_t kb = cdiv(Kred, BK);
+    double best = 1e300;
+    Q8Plan bestp;
+    for (int mt = 1; mt <= 2; ++mt)
+        for (int bn = 128; bn <= 256; bn += 128) {
+            if (forced && forced != mt * 1000 + bn) continue;
+            if (!forced && mt == 2 && M < 256) continue;
+            Q8Plan p;
+            p.mt = mt;
+            p.bn = bn;
+            p.ntiles = cdiv(Nout, bn);
+            p.mtiles = cdiv(M, 128 * mt);
+            p.split = plan_split(p.ntiles * p.mtiles, kb, sms, 4);
+            // Measured on B200 (bf16, 8192..32760 tokens): 2x256 tiles beat 2x128
+            // by 15-25% despite their serialised epilogue, and 1x256 runs at
+            // about 0.7x of 2x256 (the dequant is shared by half the rows).
+            const double per_kb = (mt == 2 ? (bn == 256 ? 1.0 : 0.62) : (bn == 256 ? 0.72 : 0.45)) * 1150.0;
+            const double tile = per_kb * p.split.kb_per + 1500.0;
+            const double cost = (double)cdiv(p.ntiles * p.mtiles * p.split.splits, sms) * tile;
+            if (cost < best * 0.999) {
+                best = cost;
+                bestp = p;
+            }
+        }
+    return bestp;
 }
 
 Split plan_sk(int64_t rows, int64_t red, int sms) { return plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4); }
@@ -205,8 +241,10 @@ int npad_of(int64_t r) { return (int)std::max<int64_t>(16, round_up(r, 16)); }
 
 // Workspace layout shared by the forward and backward passes.
 struct Ws {
-    size_t at = 0, tbuf = 0, gbuf = 0, part = 0, total = 0;
+    size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, part = 0, total = 0;
 };
+
+int64_t rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 64); }
 
 Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int sms) {
     Ws w;
@@ -220,6 +258,8 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
     off += tg_bytes;
     w.gbuf = off;
     if (pass == REELS_PASS_BACKWARD) off += tg_bytes;
+    w.ext = off;
+    if (r > 0) off += align256((size_t)rank_pad(r) * std::max(N, K) * 2);
     size_t part = 0;
     const int64_t np = npad_of(r);
     auto sk_part = [&](int64_t rows, int64_t red) {
@@ -325,6 +365,36 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
 
 // Q8 GEMM: D[M][Nout] over reduction Kred of act[M][Kred] and the int8 weight,
 // plus the LoRA extension.  `fwd` selects the weight orientation.
+// Prepared LoRA operand of the q8 GEMM's extension blocks (rows or columns
+// past r are zero):  forward  E[j][n] = B[j][n] * s (/ scale[n] when the
+//                     column scale is applied in the epilogue), [rp][N]
+//                     dX       E[k][j] = A[k][j],                  [K][rp]
+template <typename T>
+__global__ void prep_ext_fwd_kernel(const T *__restrict__ B, const float *__restrict__ scales, float s, int divide,
+                                    int64_t r, int64_t rp, int64_t N, T *__restrict__ out) {
+    const int64_t total = rp * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = i / N, n = i % N;
+        float v = 0.0f;
+        if (j < r) {
+            v = to_f32(B[j * N + n]) * s;
+            if (divide) v = v / scales[n];
+        }
+        out[i] = Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(v);
+    }
+}
+
+__global__ void prep_ext_dx_kernel(const uint16_t *__restrict__ A, int64_t K, int64_t r, int64_t rp,
+                                   uint16_t *__restrict__ out) {
+    const int64_t total = K * rp;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t k = i / rp, j = i % rp;
+        out[i] = j < r ? A[k * r + j] : (uint16_t)0;
+    }
+}
+
 struct Q8Call {
     bool fwd;
     const void *act;   // [M][Kred]
@@ -337,9 +407,31 @@ struct Q8Call {
     const void *ext_act;  // [r][ldm] 16-bit
     const void *lora;     // fwd: B [r][N]; dX: A [K][r]
     float ext_scale;
+    void *ext_buf;        // workspace for the prepared ext operand
     const void *bias;
     void *out;
 };
+
+template <int DT, int MT, int BN>
+void launch_q8_t(dim3 grid, cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tw, const CUtensorMap &te,
+                 const Q8Args &a) {
+    q8_gemm_kernel<DT, MT, BN><<<grid, Q8_THREADS, Q8Geom<MT, BN>::SMEM_BYTES, st>>>(ta, tw, te, a);
+}
+
+void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tw,
+               const CUtensorMap &te, const Q8Args &a) {
+    const int key = (dt == REELS_BF16 ? 100 : 0) + mt * 10 + (bn == 256 ? 1 : 0);
+    switch (key) {
+        case 110: launch_q8_t<DT_BF16, 1, 128>(grid, st, ta, tw, te, a); break;
+        case 111: launch_q8_t<DT_BF16, 1, 256>(grid, st, ta, tw, te, a); break;
+        case 120: launch_q8_t<DT_BF16, 2, 128>(grid, st, ta, tw, te, a); break;
+        case 121: launch_q8_t<DT_BF16, 2, 256>(grid, st, ta, tw, te, a); break;
+        case 10: launch_q8_t<DT_F16, 1, 128>(grid, st, ta, tw, te, a); break;
+        case 11: launch_q8_t<DT_F16, 1, 256>(grid, st, ta, tw, te, a); break;
+        case 20: launch_q8_t<DT_F16, 2, 128>(grid, st, ta, tw, te, a); break;
+        default: launch_q8_t<DT_F16, 2, 256>(grid, st, ta, tw, te, a); break;
+    }
+}
 
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
     Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms);
@@ -354,9 +446,9 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     // dimension is the reduction: forward on [N][K], dX on [K][N].
     const bool inner_is_red = c.fwd ? (c.layout == REELS_W_IN_CONTIGUOUS) : (c.layout == REELS_W_OUT_CONTIGUOUS);
     const int orient = inner_is_red ? 0 : 1;
-    if (orient == 0) rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, 256,
+    if (orient == 0) rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, p.bn,
                                   CU_TENSOR_MAP_SWIZZLE_NONE);
-    else rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 256, 64,
+    else rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, p.bn, 64,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const int64_t ldm = ld_tokens(c.M);
@@ -373,39 +465,60 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.Nout = (int)c.Nout;
     a.kb_total = (int)cdiv(c.Kred, BK);
     a.kb_per_split = p.split.kb_per;
+    a.splits = p.split.splits;
+    a.ntiles = (int)p.ntiles;
+    a.mtiles = (int)p.mtiles;
     a.w_orient = orient;
     a.wscale = c.scales;
     a.wscale_len = (int)c.N_w;
+    bool ext_divide = false;
     if (c.fwd) {
         // bf16: exact int8 in the MMA, per-column scale in the epilogue.
         // fp16: scale folded into the dequant (keeps B*s in fp16 range).
         if (dt == REELS_BF16) {
             a.scale_mode = 0;
             a.col_scale = c.scales;
-            a.ext_div = c.scales;
+            ext_divide = true;
         } else {
             a.scale_mode = orient == 0 ? 1 : 2;
             a.col_scale = nullptr;
-            a.ext_div = nullptr;
         }
         a.ext_kind = 0;
     } else {
         // dX: the scale sits on the reduction index n.
         a.scale_mode = orient == 1 ? 1 : 2;
         a.col_scale = nullptr;
-        a.ext_div = nullptr;
         a.ext_kind = 1;
     }
     a.r = (int)c.r;
-    a.lora = c.lora;
-    a.ext_scale = c.ext_scale;
+    if (c.r > 0) {
+        const int64_t rp = rank_pad(c.r);
+        a.ext_w = c.ext_buf;
+        if (c.fwd) {
+            a.ext_ld = (int)c.Nout;
+            if (dt == REELS_BF16)
+                prep_ext_fwd_kernel<__nv_bfloat16><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                    (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, c.r, rp, c.Nout,
+                    (__nv_bfloat16 *)c.ext_buf);
+            else
+                prep_ext_fwd_kernel<__half><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                    (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
+        } else {
+            a.ext_ld = (int)rp;
+            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp), 256, 0, st>>>((const uint16_t *)c.lora, c.Nout, c.r, rp,
+                                                                         (uint16_t *)c.ext_buf);
+        }
+        REELS_LAUNCHED();
+    }
     a.bias = c.bias;
     a.out = c.out;
     a.ldo = c.Nout;
+    a.out_v8 = (reinterpret_cast<uintptr_t>(c.out) & 31u) == 0 ? 1 : 0;
     a.partial = reinterpret_cast<float *>(ws_base + wl.part);
     a.epi_partial = p.split.splits > 1 ? 1 : 0;
     a.err = ds.status;
-    dim3 grid((unsigned)p.ntiles, (unsigned)p.mtiles, (unsigned)p.split.splits);
+    const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
+    dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
     cudaEvent_t ev_stop = nullptr;
     if (t_prof.on) {
         if (t_prof.used == t_prof.pool.size()) {
@@ -419,13 +532,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
         ev_stop = pr.second;
         t_prof.flops += 2.0 * (double)c.M * (double)c.Nout * (double)(c.Kred + c.r);
     }
-    if (dt == REELS_BF16) {
-        if (p.mt == 2) q8_gemm_kernel<DT_BF16, 2><<<grid, Q8_THREADS, Q8Geom<2>::SMEM_BYTES, st>>>(ta, tw, te, a);
-        else q8_gemm_kernel<DT_BF16, 1><<<grid, Q8_THREADS, Q8Geom<1>::SMEM_BYTES, st>>>(ta, tw, te, a);
-    } else {
-        if (p.mt == 2) q8_gemm_kernel<DT_F16, 2><<<grid, Q8_THREADS, Q8Geom<2>::SMEM_BYTES, st>>>(ta, tw, te, a);
-        else q8_gemm_kernel<DT_F16, 1><<<grid, Q8_THREADS, Q8Geom<1>::SMEM_BYTES, st>>>(ta, tw, te, a);
-    }
+    launch_q8(dt, p.mt, p.bn, grid, st, ta, tw, te, a);
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
@@ -653,6 +760,7 @@ int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, in
         c.ext_act = tbuf;
         c.lora = B;
         c.ext_scale = s;
+        c.ext_buf = ws + wl.ext;
         c.bias = bias;
         c.out = y;
         rc = run_q8(c, dt, *ds, ws, wl, st);
@@ -749,6 +857,7 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
             c.ext_act = gbuf;
             c.lora = A;
             c.ext_scale = 1.0f;
+            c.ext_buf = ws + wl.ext;
             c.bias = nullptr;
             c.out = dx;
             rc = run_q8(c, dt, *ds, ws, wl, st);

@@ -1,0 +1,205 @@
+// Skinny rank-r GEMMs on tcgen05 (sm_100a): both operands 16-bit and fed by
+// TMA, N = r <= 256.  They compute T = A.x and G = s.(B'.dy) (lora.jl:86 and
+// lora.jl:112-116) with the token dimension as rows, and the adapter
+// gradients dA, dB (lora.jl:113-114) with the token dimension as the
+// reduction, split across CTAs when the output alone does not fill the GPU.
+#pragma once
+#include "common.cuh"
+
+namespace reels {
+
+constexpr int BK = 64;  // reduction elements per pipeline stage (128 B of 16-bit)
+
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *err,
+                                          unsigned code) {
+    int ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = wait_bar(bar, parity, abort, err, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok != 0;
+}
+
+// ------------------------------------------------------------ skinny gemm
+constexpr int SK_THREADS = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
+constexpr int SK_STAGES = 4;
+constexpr int SK_A_BYTES = 128 * 128;
+constexpr int SK_B_MAX = 256 * 128;
+constexpr int SK_STAGE_BYTES = SK_A_BYTES + SK_B_MAX;
+constexpr int SK_BAR_OFF = SK_STAGES * SK_STAGE_BYTES;
+constexpr int SK_SMEM_BYTES = SK_BAR_OFF + (2 * SK_STAGES + 1) * 8 + 16 + 1024;
+
+struct SkArgs {
+    int rows;          // rows of D
+    int kb_total;      // reduction blocks of 64
+    int kb_per_split;
+    int npad;          // MMA N = B-operand rows (multiple of 16, <= 256)
+    int a_mn;          // A operand MN-major (rows of D contiguous in memory)
+    int epi;           // 0 transposed store act dtype, 1 fp32 accumulate, 2 fp32 partial
+    int ncols;         // valid D columns (rank)
+    float alpha;
+    int accumulate;
+    void *out;
+    long long ldo;     // epi 0: row pitch of out[j][row]
+    long long rs, cs;  // epi 1: out[row*rs + j*cs]
+    float *partial;    // epi 2: [splits][rows][npad]
+    unsigned *err;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(SK_THREADS, 1)
+    sk_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const SkArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + SK_BAR_OFF);
+    uint64_t *empty = full + SK_STAGES;
+    uint64_t *acc_full = full + 2 * SK_STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SK_BAR_OFF + (2 * SK_STAGES + 1) * 8);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * 128;
+    const int sp = blockIdx.y;
+    const int kb0 = sp * args.kb_per_split;
+    const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
+    const int n_iter = max(0, kb1 - kb0);
+    const uint32_t b_bytes = (uint32_t)args.npad * 128u;
+    const uint32_t tmem_cols = args.npad <= 32 ? 32u : (args.npad <= 64 ? 64u : (args.npad <= 128 ? 128u : 256u));
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < SK_STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(acc_full, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool aborted_here = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int it = 0; it < n_iter; ++it) {
+                const int s = it % SK_STAGES;
+                const uint32_t ph = (it / SK_STAGES) & 1;
+                if (!wait_bar(&empty[s], ph ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
+                    aborted_here = true;
+                    break;
+                }
+                uint8_t *a_dst = smem + s * SK_STAGE_BYTES;
+                uint8_t *b_dst = a_dst + SK_A_BYTES;
+                const int kb = kb0 + it;
+                mbar_arrive_expect_tx(&full[s], SK_A_BYTES + b_bytes);
+                if (args.a_mn) {
+                    tma_load_2d(a_dst, &tmA, row0, kb * BK, &full[s]);
+                    tma_load_2d(a_dst + 8192, &tmA, row0 + 64, kb * BK, &full[s]);
+                } else {
+                    tma_load_2d(a_dst, &tmA, kb * BK, row0, &full[s]);
+                }
+                tma_load_2d(b_dst, &tmB, kb * BK, 0, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const int ab = (DT == DT_BF16) ? 1 : 0;
+            const uint32_t id = idesc_f16(ab, args.a_mn, 0, 128, args.npad);
+            for (int it = 0; it < n_iter; ++it) {
+                const int s = it % SK_STAGES;
+                const uint32_t ph = (it / SK_STAGES) & 1;
+                if (!wait_bar(&full[s], ph, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
+                    aborted_here = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_base = sbase + s * SK_STAGE_BYTES;
+                const uint32_t b_base = a_base + SK_A_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; ++kk) {
+                    const uint64_t ad = args.a_mn ? sdesc_sw128(a_base + kk * 2048, 8192, 1024)
+                                                  : sdesc_sw128(a_base + kk * 32, 16, 1024);
+                    const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
+                    mma_f16_ss(tmem, ad, bd, id, (it > 0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(acc_full);
+        }
+    } else {
+        const int q = warp & 3;
+        if (warp_wait(acc_full, 0, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+            tc_fence_after();
+            const int row = row0 + 32 * q + lane;
+            for (int c = 0; c < args.npad; c += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
+                tmem_wait_ld();
+                if (row >= args.rows) continue;
+                if (n_iter == 0) {
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) v[t] = 0u;
+                }
+                if (args.epi == 2) {
+                    float *dst = args.partial + ((long long)sp * args.rows + row) * args.npad + c;
+#pragma unroll
+                    for (int t = 0; t < 16; t += 4)
+                        *reinterpret_cast<float4 *>(dst + t) =
+                            make_float4(__uint_as_float(v[t]), __uint_as_float(v[t + 1]), __uint_as_float(v[t + 2]),
+                                        __uint_as_float(v[t + 3]));
+                } else if (args.epi == 0) {
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        const int j = c + t;
+                        if (j < args.ncols)
+                            store_act(args.out, (long long)j * args.ldo + row, DT, args.alpha * __uint_as_float(v[t]));
+                    }
+                } else {
+                    float *o = reinterpret_cast<float *>(args.out);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        const int j = c + t;
+                        if (j < args.ncols) {
+                            const long long idx = (long long)row * args.rs + (long long)j * args.cs;
+                            const float prev = args.accumulate ? o[idx] : 0.0f;
+                            o[idx] = prev + args.alpha * __uint_as_float(v[t]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    if (aborted_here && warp == 0) {
+        for (int i = 0; i < 64; ++i) __nanosleep(2000);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        if (lane == 0) {
+            long long t0 = clock64();
+            while (!mbar_try_wait(acc_full, 0)) {
+                if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
+                    atomicOr(args.err, DEVERR_TIMEOUT_ACC);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+        tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+}  // namespace reels
