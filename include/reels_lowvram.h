@@ -119,6 +119,31 @@ size_t reels_q8lora_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, 
 /* Bytes of the `saved` buffer (A*x kept from the forward for the backward). */
 size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype);
 
+/* Size of the library-owned scratch used by reels_q8lora_forward_static_ws. */
+#define REELS_STATIC_WS_BYTES (32u << 20)
+
+/* reels_q8lora_forward without a caller-supplied workspace.  No counterpart
+ * in the reference: it exists for callers that cannot allocate device memory
+ * themselves -- a foreign-function binding that is only handed raw device
+ * pointers and has no device allocator of its own, or a loop that must run
+ * inside a fixed device-memory budget where a per-call allocation could fail
+ * or fragment the pool.  Its scratch is a file-scope device array of
+ * REELS_STATIC_WS_BYTES (32 MiB) inside the library; every GPU that loads the
+ * library holds that array until the process exits.  Arguments and results
+ * are those of reels_q8lora_forward; a shape whose forward workspace
+ * (reels_q8lora_workspace_bytes, REELS_PASS_FORWARD) exceeds the array is
+ * rejected with REELS_EINVAL and nothing runs.
+ *  - The first call on a device looks the array's device address up with that
+ *    device current; make that first call before any stream capture.
+ *  - All calls share the one array and it keeps the last call's contents.
+ *    Nothing in it needs to start at zero (every byte a call reads it wrote
+ *    earlier in the same call), but calls that overlap on the GPU (other
+ *    streams, other host threads) race on it: serialise them.
+ *  - Allocates nothing: no cudaMalloc, cudaFree or allocating library call. */
+int reels_q8lora_forward_static_ws(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                                   const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                                   float alpha, int act_dtype, void *y, void *saved, void *stream);
+
 /* _weight_mul (quantization.jl:73-74) for a QuantizedMatrix, optional bias
  * (linear, src/layers/linear.jl:38-46): y = dequant(q) * x (+ bias). */
 int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int layout, const void *bias, int64_t M,

@@ -44,6 +44,8 @@ SIGNATURES = {
                                     _vp, _vp, _vp, _sz, _vp]),
     "reels_q8lora_backward": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _f,
                                      _int, _vp, _vp, _vp, _int, _vp, _sz, _vp]),
+    "reels_q8lora_forward_static_ws": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f,
+                                              _int, _vp, _vp, _vp]),
 }
 
 _lock = threading.Lock()

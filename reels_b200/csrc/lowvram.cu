@@ -938,3 +938,65 @@ int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *
 }
 
 }  // extern "C"
+
+// =====================================================================
+// Forward with library-owned scratch, for callers that cannot allocate
+// device memory (see include/reels_lowvram.h).  The scratch is this
+// file-scope array; in host code its name is only a stand-in, so the device
+// address is looked up with cudaGetSymbolAddress, once per device, with that
+// device current, and handed to the kernels as an ordinary pointer.
+static __device__ __align__(256) unsigned char g_static_ws[REELS_STATIC_WS_BYTES];
+
+namespace {
+void *g_static_ws_addr[kMaxDevices];
+int g_static_ws_sms[kMaxDevices];
+std::mutex g_static_ws_mu;
+}  // namespace
+
+extern "C" int reels_q8lora_forward_static_ws(const void *x, const int8_t *q, const float *scales, int layout,
+                                              const void *A, const void *B, const void *bias, int64_t M, int64_t K,
+                                              int64_t N, int64_t r, float alpha, int act_dtype, void *y, void *saved,
+                                              void *stream) {
+    int rc = check_common(M, K, N, r, act_dtype, layout);
+    if (rc) return rc;
+    if (!x) return fail("null x");
+    if (M == 0) return ok(REELS_PATH_NONE);
+    int dev = -1;
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, x) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {
+        dev = attr.device;
+    } else {
+        cudaGetLastError();
+        REELS_CUDA(cudaGetDevice(&dev));
+    }
+    if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
+    REELS_CUDA(cudaSetDevice(dev));
+    void *ws = nullptr;
+    int sms = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_static_ws_mu);
+        if (!g_static_ws_addr[dev]) {
+            void *p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_static_ws);
+            if (e != cudaSuccess || !p)
+                return fail_dev(std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
+            int v = 0;
+            REELS_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+            g_static_ws_sms[dev] = v;
+            g_static_ws_addr[dev] = p;
+        }
+        ws = g_static_ws_addr[dev];
+        sms = g_static_ws_sms[dev];
+    }
+    const size_t need = ws_layout(M, K, N, r, act_dtype, REELS_PASS_FORWARD, sms).total;
+    if (need > REELS_STATIC_WS_BYTES) {
+        char buf[200];
+        snprintf(buf, sizeof buf,
+                 "shape needs %zu bytes of scratch, more than the %u-byte static array; use reels_q8lora_forward "
+                 "with a caller workspace",
+                 need, (unsigned)REELS_STATIC_WS_BYTES);
+        return fail(buf);
+    }
+    return reels_q8lora_forward(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, act_dtype, y, saved, ws,
+                                REELS_STATIC_WS_BYTES, stream);
+}
