@@ -197,9 +197,12 @@ struct Q8Plan {
     Split split;
 };
 
-// Tile shape from measured cycles per 64-wide reduction block and tile
-// shape.  The kernel is persistent, so a CTA runs ceil(tiles / SMs) tiles;
-// the cost is that count times the per-tile time.
+// Tile shape and reduction split from a time model fitted to B200
+// measurements (bf16; microseconds): a 64-wide reduction block costs about
+// 1.18 (2x256 tiles), 0.85 (2x128), 1.0 (1x256) or 0.75 (1x128); a 2x256 tile
+// also pays ~3 us of epilogue its single accumulator cannot overlap.  The
+// kernel is persistent, so a CTA runs ceil(work units / SMs) units; a split
+// reduction adds the write and re-read of fp32 partials (~5 TB/s).
 Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN", e.g. "2x128"
@@ -215,21 +218,27 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
         for (int bn = 128; bn <= 256; bn += 128) {
             if (forced && forced != mt * 1000 + bn) continue;
             if (!forced && mt == 2 && M < 256) continue;
-            Q8Plan p;
-            p.mt = mt;
-            p.bn = bn;
-            p.ntiles = cdiv(Nout, bn);
-            p.mtiles = cdiv(M, 128 * mt);
-            p.split = plan_split(p.ntiles * p.mtiles, kb, sms, 4);
-            // Measured on B200 (bf16, 8192..32760 tokens): 2x256 tiles beat 2x128
-            // by 15-25% despite their serialised epilogue, and 1x256 runs at
-            // about 0.7x of 2x256 (the dequant is shared by half the rows).
-            const double per_kb = (mt == 2 ? (bn == 256 ? 1.0 : 0.62) : (bn == 256 ? 0.72 : 0.45)) * 1150.0;
-            const double tile = per_kb * p.split.kb_per + 1500.0;
-            const double cost = (double)cdiv(p.ntiles * p.mtiles * p.split.splits, sms) * tile;
-            if (cost < best * 0.999) {
-                best = cost;
-                bestp = p;
+            const double per_kb = mt == 2 ? (bn == 256 ? 1.18 : 0.85) : (bn == 256 ? 1.0 : 0.75);
+            const double epi = (mt == 2 && bn == 256) ? 3.0 : 0.5;
+            const int64_t ntiles = cdiv(Nout, bn), mtiles = cdiv(M, 128 * mt);
+            const int64_t tiles = ntiles * mtiles;
+            for (int64_t want = 1; want <= std::max<int64_t>(1, kb / 4); want = want < 4 ? want + 1 : want * 2) {
+                Split sp;
+                sp.kb_per = (int)cdiv(kb, want);
+                sp.splits = (int)cdiv(kb, sp.kb_per);
+                if (want > 1 && sp.splits == 1) continue;
+                const double units = (double)cdiv(tiles * sp.splits, sms);
+                double cost = units * (sp.kb_per * per_kb + epi + 1.0);
+                if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
+                if (cost < best * 0.999) {
+                    best = cost;
+                    bestp.mt = mt;
+                    bestp.bn = bn;
+                    bestp.ntiles = ntiles;
+                    bestp.mtiles = mtiles;
+                    bestp.split = sp;
+                }
+                if (tiles >= sms) break;  // enough tiles: never split
             }
         }
     return bestp;

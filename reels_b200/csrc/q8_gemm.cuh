@@ -29,7 +29,11 @@
 
 namespace reels {
 
-constexpr int Q8_NCW = 8;         // dequant warps (3..10)
+#ifndef REELS_Q8_DEQUANT_WARPS
+#define REELS_Q8_DEQUANT_WARPS 8
+#endif
+constexpr int Q8_NCW = REELS_Q8_DEQUANT_WARPS;  // dequant warps (3 .. 2 + Q8_NCW)
+constexpr int Q8_NDT = 32 * Q8_NCW;             // dequant threads
 constexpr int Q8_NEW = 8;         // epilogue warps (11..18)
 constexpr int Q8_THREADS = 32 * (3 + Q8_NCW + Q8_NEW);
 
@@ -63,7 +67,9 @@ struct Q8Args {
 
 // Shared-memory plan per (MT, BN): A ring (activation tiles), B ring (16-bit
 // weight tiles written by the dequant warps), W ring (int8 TMA staging),
-// about 224 KB in total.  TMEM holds 512 fp32 columns: two accumulators of
+// at most 224 KB.  For 2x256 a sweep on B200 put the third B stage ahead of
+// a third A or fourth W stage (+10% forward): the MMA and the dequant warps
+// run at similar rates, and two B stages made them wait on each other.  TMEM holds 512 fp32 columns: two accumulators of
 // MT*BN columns when that is 256 (double buffered), one when it is 512.
 template <int MT, int BN>
 struct Q8Geom {
@@ -72,10 +78,20 @@ struct Q8Geom {
     static constexpr int A_BYTES = MT * 128 * 128;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int W_BYTES = BN * BK;
-    static constexpr int SA = (MT == 2) ? (BN == 256 ? 3 : 4) : (BN == 256 ? 4 : 6);
-    static constexpr int SB = (MT == 2) ? (BN == 256 ? 2 : 3) : (BN == 256 ? 3 : 4);
-    static constexpr int S8 = (BN == 256) ? 4 : (MT == 2 ? 6 : 8);
-    static constexpr int CPT = W_BYTES / 8 / 256;  // 8-byte chunks per dequant thread
+    // Ring depths of the 2x256 plan; tuning builds may override them.
+#ifndef REELS_Q8_SA
+#define REELS_Q8_SA 2
+#endif
+#ifndef REELS_Q8_SB
+#define REELS_Q8_SB 3
+#endif
+#ifndef REELS_Q8_S8
+#define REELS_Q8_S8 3
+#endif
+    static constexpr int SA = (MT == 2) ? (BN == 256 ? REELS_Q8_SA : 4) : (BN == 256 ? 4 : 6);
+    static constexpr int SB = (MT == 2) ? (BN == 256 ? REELS_Q8_SB : 3) : (BN == 256 ? 3 : 4);
+    static constexpr int S8 = (MT == 2 && BN == 256) ? REELS_Q8_S8 : (BN == 256 ? 4 : (MT == 2 ? 6 : 8));
+    static constexpr int CPT = W_BYTES / 8 / Q8_NDT;  // 8-byte chunks per dequant thread
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + SA * A_BYTES;
     static constexpr int W_OFF = B_OFF + SB * B_BYTES;
@@ -157,8 +173,8 @@ __device__ __forceinline__ void epilogue_store16(const Q8Args &args, const uint3
 }
 
 // One int8 staging tile (BN x 64 bytes, row-major as TMA left it) to the
-// 16-bit B-operand tile.  Each of the 256 dequant threads handles BN/32
-// 8-byte chunks; their shared loads are issued back to back before any
+// 16-bit B-operand tile.  Each of the Q8_NDT dequant threads handles
+// BN*8/Q8_NDT 8-byte chunks; their shared loads are issued back to back before any
 // conversion so the latencies overlap.
 //   ORIENT 0: staging rows are D columns, 64 B each   -> K-major B (SW128)
 //   ORIENT 1: staging rows are reduction, BN B each   -> MN-major B (SW128,
@@ -169,7 +185,9 @@ __device__ __forceinline__ void epilogue_store16(const Q8Args &args, const uint3
 template <int DT, int BN, int ORIENT, int SMODE>
 __device__ __forceinline__ void dequant_stage(uint32_t w_base, uint32_t b_base, int ct, int x0, int y0,
                                               const float *__restrict__ wscale, int wlen) {
-    constexpr int CPT = BN / 32;
+    constexpr int CPT = BN * 8 / Q8_NDT;
+    constexpr int BATCH = CPT < 4 ? CPT : 4;
+    static_assert(CPT % BATCH == 0, "dequant chunks per thread must split into equal batches");
     constexpr int RC = (ORIENT == 0) ? 8 : BN / 8;  // chunks per staging row
     const int c8 = ct % RC;
     float cs[8];
@@ -180,21 +198,21 @@ __device__ __forceinline__ void dequant_stage(uint32_t w_base, uint32_t b_base, 
     }
     // Batches of four chunks: four loads in flight, then convert and store.
 #pragma unroll
-    for (int jb = 0; jb < CPT; jb += 4) {
-        uint2 v[4];
-        float rs[4];
+    for (int jb = 0; jb < CPT; jb += BATCH) {
+        uint2 v[BATCH];
+        float rs[BATCH];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] = ld_shared_v2(w_base + (ct + 256 * (jb + j)) * 8);
+        for (int j = 0; j < BATCH; ++j) v[j] = ld_shared_v2(w_base + (ct + Q8_NDT * (jb + j)) * 8);
         if constexpr (SMODE == 1) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int row = (ct + 256 * (jb + j)) / RC;
+            for (int j = 0; j < BATCH; ++j) {
+                const int row = (ct + Q8_NDT * (jb + j)) / RC;
                 rs[j] = (y0 + row) < wlen ? __ldg(wscale + y0 + row) : 0.0f;
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int row = (ct + 256 * (jb + j)) / RC;
+        for (int j = 0; j < BATCH; ++j) {
+            const int row = (ct + Q8_NDT * (jb + j)) / RC;
             uint32_t dst;
             if constexpr (ORIENT == 0) dst = b_base + sw128_off(row, c8);
             else dst = b_base + (c8 >> 3) * 8192 + sw128_off(row, c8 & 7);
@@ -378,7 +396,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         }
     } else if (warp < 3 + Q8_NCW) {
         // ------------------------------------------------ dequant warps
-        const int ct = threadIdx.x - 3 * 32;  // 0..255
+        const int ct = threadIdx.x - 3 * 32;  // 0 .. Q8_NDT-1
         uint32_t gb = 0, gw = 0;
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
             const TileCoord c = q8_tile<MT, BN>(args, t);
@@ -417,7 +435,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                     const typename E::T *src = reinterpret_cast<const typename E::T *>(args.ext_w);
 #pragma unroll
                     for (int j = 0; j < G::CPT; ++j) {
-                        const int i = ct + 256 * j;
+                        const int i = ct + Q8_NDT * j;
                         uint4 o = make_uint4(0, 0, 0, 0);
                         uint32_t dst;
                         if (args.ext_kind == 0) {
@@ -447,7 +465,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
         }
     } else {
         // ------------------------------------------------ epilogue warps
-        const int ew = warp - (3 + Q8_NCW);  // 0..7
+        const int ew = warp - (3 + Q8_NCW);  // 0..7 (epilogue warp index)
         const int q = warp & 3;              // TMEM lane quarter this warp may read
         const int set = ew >> 2;             // 0 or 1
         uint32_t local = 0;
