@@ -73,8 +73,9 @@ def load_peaks():
     return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}, "fallback"
 
 
-def load_traffic():
-    """Per-launch DRAM bytes of the q8 GEMM from the committed ncu summary."""
+def load_traffic_ratio():
+    """DRAM traffic / algorithmic bytes of one q8 GEMM launch, from the
+    committed ncu summary (a smaller case of the same kernel)."""
     p = os.path.join(ROOT, "profiles", "q8_gemm_traffic.txt")
     if not os.path.exists(p):
         return None, None
@@ -84,9 +85,22 @@ def load_traffic():
             k, v = line.split("=", 1)
             vals[k.strip()] = v.strip()
     try:
-        return float(vals["dram_bytes_per_launch"]), vals.get("workload")
+        return float(vals["traffic_over_algorithmic"]), vals.get("workload")
     except (KeyError, ValueError):
         return None, None
+
+
+def q8_algorithmic_bytes(layers, r):
+    """Minimum DRAM bytes of the step's q8 GEMM launches (forward Y and dX per
+    linear, bf16): activations in and out, int8 weight, scales, the rank-r
+    operands of the LoRA blocks."""
+    rp = ((r + 63) // 64) * 64
+    total, n = 0.0, 0
+    for (_, M, K, N) in layers:
+        total += 2 * M * K + K * N + 4 * N + 2 * M * N + 2 * r * M + 2 * rp * N   # forward
+        total += 2 * M * N + K * N + 4 * N + 2 * M * K + 2 * r * M + 2 * rp * K   # dX
+        n += 2
+    return total, n
 
 
 # ---------------------------------------------------------------- clocks
@@ -318,7 +332,10 @@ def run_ours(args):
     peaks, peak_kind = load_peaks()
     q8_tflops = (q8_flops / (q8_ms / 1e3) / 1e12) if q8_ms > 0 else None
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    traffic, traffic_src = load_traffic()
+    ratio, ratio_src = load_traffic_ratio()
+    alg_bytes, alg_n = q8_algorithmic_bytes(layers, r)
+    alg_per_launch = alg_bytes / alg_n
+    traffic = ratio * alg_per_launch if ratio is not None else None
 
     result = None
     if rank == 0:
@@ -353,7 +370,12 @@ def run_ours(args):
                          "frac": (q8_tflops / peak) if q8_tflops else None,
                          "peak_source": f"bf16_tflops_sustained of {peak_kind}",
                          "launches": q8_n, "algorithmic_flops_per_launch": (q8_flops / q8_n) if q8_n else None,
-                         "traffic": traffic, "traffic_source": traffic_src},
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": alg_per_launch,
+                         "traffic_source": (f"ncu DRAM read+write of one launch of the same kernel on a smaller case "
+                                            f"({ratio_src}) as a fraction of its algorithmic bytes ({ratio:.3f}), "
+                                            f"times this workload's algorithmic bytes per launch"
+                                            if ratio is not None else None)},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
