@@ -229,6 +229,99 @@ __device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
     return v;
 }
 
+// ------------------------------------------------------------ clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+// Arrive on an mbarrier in another CTA of the cluster.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait that acquires at cluster scope (for phases completed by a peer CTA).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool wait_bar_cluster(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *err,
+                                                 unsigned code) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if (*abort) return false;
+        if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
+            *abort = 1;
+            if (err) atomicOr(err, code);
+            return false;
+        }
+    }
+}
+// TMA load issued by either CTA of a cta_group::2 pair whose completion is
+// counted on an mbarrier that may live in the peer CTA (`bar_cluster` is a
+// shared::cluster address, e.g. from mapa).  No multicast: the data lands
+// only in this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, int x, int y,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Pair-CTA (cta_group::2) tensor-core forms: the leader CTA issues the MMA for
+// both CTAs; A and D rows are split between them, B columns too.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on `bar` in every CTA of `cta_mask` when the pair's MMAs issued
+// so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+
 // 32-byte global stores (sm_100): one instruction per 16 bf16/fp16 or 8 fp32.
 __device__ __forceinline__ void st_global_v8(void *p, uint4 a, uint4 b) {
     asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w),

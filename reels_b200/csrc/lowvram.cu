@@ -15,6 +15,7 @@
 #include "../../include/reels_lowvram.h"
 #include "aux_kernels.cuh"
 #include "q8_gemm.cuh"
+#include "q8_gemm_2sm.cuh"
 
 using namespace reels;
 
@@ -71,6 +72,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceState {
     bool ready = false;
     int sms = 148;
+    int pair_clusters = 0;  // co-resident 2-CTA clusters of the pair kernel
     unsigned *status = nullptr;
     unsigned *quant_status = nullptr;
 };
@@ -124,6 +126,33 @@ int bind_device(const void *ptr, DeviceState **out) {
         REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.quant_status), g_quant_status));
         REELS_CUDA(set_q8_attrs<DT_BF16>());
         REELS_CUDA(set_q8_attrs<DT_F16>());
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8PairGeom::SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Q8PairGeom::SMEM_BYTES));
+        {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * 74);
+            cfg.blockDim = dim3(Q8_THREADS);
+            cfg.dynamicSmemBytes = Q8PairGeom::SMEM_BYTES;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 2;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, q8_gemm_pair_kernel<DT_BF16>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+            st.pair_clusters = n;
+            if (const char *e = getenv("REELS_PAIR_CLUSTERS")) st.pair_clusters = std::max(0, atoi(e));
+            if (getenv("REELS_LOWVRAM_DEBUG"))
+                fprintf(stderr, "reels_lowvram: device %d: %d SMs, %d co-resident 2-CTA clusters (queried %d)\n",
+                        dev, st.sms, st.pair_clusters, n);
+        }
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         SK_SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -193,6 +222,7 @@ Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb) {
 
 struct Q8Plan {
     int mt = 1, bn = 256;
+    bool pair = false;  // 2-CTA cluster kernel on 256x256 tiles
     int64_t ntiles = 1, mtiles = 1;
     Split split;
 };
@@ -203,10 +233,11 @@ struct Q8Plan {
 // also pays ~3 us of epilogue its single accumulator cannot overlap.  The
 // kernel is persistent, so a CTA runs ceil(work units / SMs) units; a split
 // reduction adds the write and re-read of fp32 partials (~5 TB/s).
-Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters) {
     static const int forced = [] {
-        const char *e = getenv("REELS_Q8_TILE");  // "MTxBN", e.g. "2x128"
+        const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128") or "pair"
         if (!e) return 0;
+        if (strcmp(e, "pair") == 0) return 1;
         int a = 0, b = 0;
         if (sscanf(e, "%dx%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 128 || b == 256)) return a * 1000 + b;
         return 0;
@@ -241,6 +272,24 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms) {
                 if (tiles >= sms) break;  // enough tiles: never split
             }
         }
+    // The pair kernel (256x256 tiles on 2-CTA clusters) is correct but
+    // measured slower than the single-CTA 2x256 plan on every BASELINE shape
+    // (about 770 vs 920-1130 TFLOP/s forward), so it runs only when forced.
+    if (pair_clusters > 0 && forced == 1) {
+        const int64_t ntiles = cdiv(Nout, 256), mtiles = cdiv(M, 256);
+        const double units = (double)cdiv(ntiles * mtiles, pair_clusters);
+        const double cost = units * (kb * 0.95 * 1.18 + 1.5);
+        if (forced == 1 || cost < best) {
+            bestp = Q8Plan();
+            bestp.mt = 2;
+            bestp.bn = 256;
+            bestp.pair = true;
+            bestp.ntiles = ntiles;
+            bestp.mtiles = mtiles;
+            bestp.split.splits = 1;
+            bestp.split.kb_per = (int)kb;
+        }
+    }
     return bestp;
 }
 
@@ -276,7 +325,7 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
         if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
     };
     auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
-        Q8Plan p = plan_q8(rows, cols, red, sms);
+        Q8Plan p = plan_q8(rows, cols, red, sms, 0);  // the pair plan never splits
         if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
     };
     if (M > 0) {
@@ -443,9 +492,13 @@ void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtenso
 }
 
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
-    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms);
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters);
     CUtensorMap ta, tw, te;
-    int rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, 128 * p.mt,
+    // Per-CTA boxes: the pair kernel loads 128 token rows and 128 weight
+    // columns per CTA of a 256x256 tile.
+    const int a_rows = p.pair ? 128 : 128 * p.mt;
+    const int w_box = p.pair ? 128 : p.bn;
+    int rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, a_rows,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     // Weight tensor as stored: layout 0 is [K][N] (inner N), layout 1 is [N][K] (inner K).
@@ -455,9 +508,9 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     // dimension is the reduction: forward on [N][K], dX on [K][N].
     const bool inner_is_red = c.fwd ? (c.layout == REELS_W_IN_CONTIGUOUS) : (c.layout == REELS_W_OUT_CONTIGUOUS);
     const int orient = inner_is_red ? 0 : 1;
-    if (orient == 0) rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, p.bn,
+    if (orient == 0) rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, w_box,
                                   CU_TENSOR_MAP_SWIZZLE_NONE);
-    else rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, p.bn, 64,
+    else rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, w_box, 64,
                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
     const int64_t ldm = ld_tokens(c.M);
@@ -541,7 +594,15 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
         ev_stop = pr.second;
         t_prof.flops += 2.0 * (double)c.M * (double)c.Nout * (double)(c.Kred + c.r);
     }
-    launch_q8(dt, p.mt, p.bn, grid, st, ta, tw, te, a);
+    if (p.pair) {
+        const dim3 pgrid((unsigned)(2 * std::min<int64_t>(total_tiles, ds.pair_clusters)));
+        if (dt == REELS_BF16)
+            q8_gemm_pair_kernel<DT_BF16><<<pgrid, Q8_THREADS, Q8PairGeom::SMEM_BYTES, st>>>(ta, tw, te, a);
+        else
+            q8_gemm_pair_kernel<DT_F16><<<pgrid, Q8_THREADS, Q8PairGeom::SMEM_BYTES, st>>>(ta, tw, te, a);
+    } else {
+        launch_q8(dt, p.mt, p.bn, grid, st, ta, tw, te, a);
+    }
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {

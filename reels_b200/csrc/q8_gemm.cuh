@@ -88,9 +88,12 @@ struct Q8Geom {
 #ifndef REELS_Q8_S8
 #define REELS_Q8_S8 3
 #endif
-    static constexpr int SA = (MT == 2) ? (BN == 256 ? REELS_Q8_SA : 4) : (BN == 256 ? 4 : 6);
-    static constexpr int SB = (MT == 2) ? (BN == 256 ? REELS_Q8_SB : 3) : (BN == 256 ? 3 : 4);
-    static constexpr int S8 = (MT == 2 && BN == 256) ? REELS_Q8_S8 : (BN == 256 ? 4 : (MT == 2 ? 6 : 8));
+    // 128-row tiles serve few tokens (M < 256): the int8 weight then streams
+    // from HBM, so most of the budget goes to the W ring to keep ~128 KB of
+    // weight in flight per SM (Little's law at ~2 us DRAM latency).
+    static constexpr int SA = (MT == 2) ? (BN == 256 ? REELS_Q8_SA : 4) : 2;
+    static constexpr int SB = (MT == 2) ? (BN == 256 ? REELS_Q8_SB : 3) : (BN == 256 ? 2 : 3);
+    static constexpr int S8 = (MT == 2) ? (BN == 256 ? REELS_Q8_S8 : 6) : (BN == 256 ? 8 : 16);
     static constexpr int CPT = W_BYTES / 8 / Q8_NDT;  // 8-byte chunks per dequant thread
     static constexpr int A_OFF = 0;
     static constexpr int B_OFF = A_OFF + SA * A_BYTES;

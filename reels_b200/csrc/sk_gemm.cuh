@@ -20,12 +20,20 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
 
 // ------------------------------------------------------------ skinny gemm
 constexpr int SK_THREADS = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
-constexpr int SK_STAGES = 4;
 constexpr int SK_A_BYTES = 128 * 128;
-constexpr int SK_B_MAX = 256 * 128;
-constexpr int SK_STAGE_BYTES = SK_A_BYTES + SK_B_MAX;
-constexpr int SK_BAR_OFF = SK_STAGES * SK_STAGE_BYTES;
-constexpr int SK_SMEM_BYTES = SK_BAR_OFF + (2 * SK_STAGES + 1) * 8 + 16 + 1024;
+constexpr int SK_MAX_STAGES = 8;
+// Ring buffer for the stages; the stage count is chosen per launch from the
+// B tile size (rank): these kernels stream x or dy from HBM, so they keep as
+// many bytes in flight as the budget allows (8 stages up to rank 64).
+constexpr int SK_RING_BYTES = 200 * 1024;
+constexpr int SK_BAR_OFF = SK_RING_BYTES;
+constexpr int SK_SMEM_BYTES = SK_BAR_OFF + (2 * SK_MAX_STAGES + 1) * 8 + 16 + 1024;
+
+__host__ __device__ constexpr int sk_stage_bytes(int npad) { return SK_A_BYTES + npad * 128; }
+__host__ __device__ constexpr int sk_stages(int npad) {
+    return SK_RING_BYTES / sk_stage_bytes(npad) < SK_MAX_STAGES ? SK_RING_BYTES / sk_stage_bytes(npad)
+                                                                 : SK_MAX_STAGES;
+}
 
 struct SkArgs {
     int rows;          // rows of D
@@ -52,10 +60,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     const uint32_t raw_u32 = smem_u32(smem_raw);
     uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
     const uint32_t sbase = smem_u32(smem);
+    const int NS = sk_stages(args.npad);
+    const int STAGE = sk_stage_bytes(args.npad);  // multiple of 1024: A tile 16 KB + npad*128 B
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + SK_BAR_OFF);
-    uint64_t *empty = full + SK_STAGES;
-    uint64_t *acc_full = full + 2 * SK_STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SK_BAR_OFF + (2 * SK_STAGES + 1) * 8);
+    uint64_t *empty = full + SK_MAX_STAGES;
+    uint64_t *acc_full = full + 2 * SK_MAX_STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SK_BAR_OFF + (2 * SK_MAX_STAGES + 1) * 8);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -68,7 +78,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     const uint32_t tmem_cols = args.npad <= 32 ? 32u : (args.npad <= 64 ? 64u : (args.npad <= 128 ? 128u : 256u));
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < SK_STAGES; ++i) {
+        for (int i = 0; i < NS; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
@@ -93,13 +103,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             for (int it = 0; it < n_iter; ++it) {
-                const int s = it % SK_STAGES;
-                const uint32_t ph = (it / SK_STAGES) & 1;
+                const int s = it % NS;
+                const uint32_t ph = (it / NS) & 1;
                 if (!wait_bar(&empty[s], ph ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
                     aborted_here = true;
                     break;
                 }
-                uint8_t *a_dst = smem + s * SK_STAGE_BYTES;
+                uint8_t *a_dst = smem + s * STAGE;
                 uint8_t *b_dst = a_dst + SK_A_BYTES;
                 const int kb = kb0 + it;
                 mbar_arrive_expect_tx(&full[s], SK_A_BYTES + b_bytes);
@@ -117,14 +127,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             const int ab = (DT == DT_BF16) ? 1 : 0;
             const uint32_t id = idesc_f16(ab, args.a_mn, 0, 128, args.npad);
             for (int it = 0; it < n_iter; ++it) {
-                const int s = it % SK_STAGES;
-                const uint32_t ph = (it / SK_STAGES) & 1;
+                const int s = it % NS;
+                const uint32_t ph = (it / NS) & 1;
                 if (!wait_bar(&full[s], ph, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
                     aborted_here = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_base = sbase + s * SK_STAGE_BYTES;
+                const uint32_t a_base = sbase + s * STAGE;
                 const uint32_t b_base = a_base + SK_A_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk) {

@@ -1,0 +1,50 @@
+"""GPU parity of the pair-CTA (cta_group::2) q8 GEMM, which the planner only
+uses when REELS_Q8_TILE=pair forces it.  The override is read once per
+process, so the cases run in a child process."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = r"""
+import json, sys
+sys.path.insert(0, {root!r}); sys.path.insert(0, {tests!r})
+import torch
+import lora_case as lc
+from reels_b200 import lora_forward, lora_backward, saved_buffer, check_device_status
+out = []
+for (M, K, N, r, layout, dt) in {cases!r}:
+    c = lc.make_case(M, K, N, r, dtype=dt, layout=layout, seed=M + N)
+    tdt = lc.torch_dtype(torch, dt)
+    layer = lc.device_layer(torch, c)
+    x = torch.from_numpy(c.X).cuda().to(tdt); dy = torch.from_numpy(c.dY).cuda().to(tdt)
+    saved = saved_buffer(layer, x)
+    y = lora_forward(layer, x, saved=saved)
+    g = lora_backward(layer, x, dy, saved=saved)
+    check_device_status()
+    ref = lc.oracle_outputs(c)
+    got = (y.float().cpu().numpy(), g.dx.float().cpu().numpy(), g.A.t().contiguous().cpu().numpy(),
+           g.B.t().contiguous().cpu().numpy())
+    out.append([lc.rel_l2(a, b) for a, b in zip(got, ref)])
+print(json.dumps(out))
+"""
+
+CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1024, 512, 8, 0, "f16")]
+
+
+def test_pair_kernel_parity():
+    from reels_b200 import build
+    build.build()
+    env = dict(os.environ, REELS_Q8_TILE="pair")
+    code = CHILD.format(root=ROOT, tests=os.path.join(ROOT, "tests"), cases=CASES)
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    errs = json.loads(res.stdout.strip().splitlines()[-1])
+    for case, e in zip(CASES, errs):
+        assert max(e) <= 3e-3, (case, e)
