@@ -100,6 +100,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking check of a phase (no suspend): the cheap first probe of a wait.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Upper bound on a single wait: about two seconds at the B200 boost clock.
 // A pipeline stage normally completes in well under a microsecond.
 #ifndef REELS_WAIT_LIMIT_CYCLES
@@ -111,6 +124,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // CTA unwinds instead of serialising one timeout per stage.
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned *err, unsigned code) {
+    if (mbar_test_wait(bar, parity)) return true;
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (true) {

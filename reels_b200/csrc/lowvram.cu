@@ -16,6 +16,7 @@
 #include "aux_kernels.cuh"
 #include "q8_gemm.cuh"
 #include "q8_gemm_2sm.cuh"
+#include "q8ts_gemm.cuh"
 
 using namespace reels;
 
@@ -98,6 +99,19 @@ cudaError_t set_q8_attrs() {
     return set_q8_attr<DT, 2, 256>();
 }
 
+template <int DT>
+cudaError_t set_ts_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TsGeom<256>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 192>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 TsGeom<192>::SMEM_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 TsGeom<128>::SMEM_BYTES);
+    return e;
+}
+
 int bind_device(const void *ptr, DeviceState **out) {
     int dev = -1;
     cudaPointerAttributes attr;
@@ -126,6 +140,8 @@ int bind_device(const void *ptr, DeviceState **out) {
         REELS_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&st.quant_status), g_quant_status));
         REELS_CUDA(set_q8_attrs<DT_BF16>());
         REELS_CUDA(set_q8_attrs<DT_F16>());
+        REELS_CUDA(set_ts_attrs<DT_BF16>());
+        REELS_CUDA(set_ts_attrs<DT_F16>());
         REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         Q8PairGeom::SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -223,17 +239,24 @@ Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb) {
 struct Q8Plan {
     int mt = 1, bn = 256;
     bool pair = false;  // 2-CTA cluster kernel on 256x256 tiles
+    int ts = 0;         // > 0: weight-in-TMEM kernel, 128 output columns x ts tokens
     int64_t ntiles = 1, mtiles = 1;
     Split split;
 };
 
-// Tile shape and reduction split from a time model fitted to B200
-// measurements (bf16; microseconds): a 64-wide reduction block costs about
-// 1.18 (2x256 tiles), 0.85 (2x128), 1.0 (1x256) or 0.75 (1x128); a 2x256 tile
-// also pays ~3 us of epilogue its single accumulator cannot overlap.  The
-// kernel is persistent, so a CTA runs ceil(work units / SMs) units; a split
-// reduction adds the write and re-read of fp32 partials (~5 TB/s).
-Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters) {
+// Kernel, tile shape and reduction split from a time model fitted to B200
+// measurements (bf16; microseconds per 64-wide reduction block of one tile,
+// plus a per-tile epilogue cost the kernel cannot overlap):
+//   weight-in-TMEM kernel (q8ts_gemm.cuh), 128 output columns x bt tokens:
+//       bt 256: 0.49 + 1.1 per tile (single accumulator), bt 192: 0.44 + 0.4,
+//       bt 128: 0.48 + 0.4;
+//   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
+//       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
+// The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
+// split reduction adds the write and re-read of fp32 partials (~5 TB/s).
+// REELS_Q8_TILE ("MTxBN" or "pair") and REELS_Q8_TS (256, 192, 128, or 0 for
+// off) force a plan for measurements.
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters, bool allow_ts) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128") or "pair"
         if (!e) return 0;
@@ -242,36 +265,56 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
         if (sscanf(e, "%dx%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 128 || b == 256)) return a * 1000 + b;
         return 0;
     }();
+    static const int forced_ts = [] {
+        const char *e = getenv("REELS_Q8_TS");
+        if (!e) return -1;  // automatic
+        const int v = atoi(e);
+        return (v == 256 || v == 192 || v == 128) ? v : 0;
+    }();
+    struct Cand {
+        int mt, bn, ts;
+        double per_kb, epi;
+    };
+    const Cand cands[] = {
+        {0, 0, 256, 0.49, 1.1}, {0, 0, 192, 0.44, 0.4}, {0, 0, 128, 0.48, 0.4},
+        {2, 256, 0, 1.18, 4.0}, {2, 128, 0, 0.85, 1.5}, {1, 256, 0, 1.0, 1.5}, {1, 128, 0, 0.75, 1.5},
+    };
     const int64_t kb = cdiv(Kred, BK);
     double best = 1e300;
     Q8Plan bestp;
-    for (int mt = 1; mt <= 2; ++mt)
-        for (int bn = 128; bn <= 256; bn += 128) {
-            if (forced && forced != mt * 1000 + bn) continue;
-            if (!forced && mt == 2 && M < 256) continue;
-            const double per_kb = mt == 2 ? (bn == 256 ? 1.18 : 0.85) : (bn == 256 ? 1.0 : 0.75);
-            const double epi = (mt == 2 && bn == 256) ? 3.0 : 0.5;
-            const int64_t ntiles = cdiv(Nout, bn), mtiles = cdiv(M, 128 * mt);
-            const int64_t tiles = ntiles * mtiles;
-            for (int64_t want = 1; want <= std::max<int64_t>(1, kb / 4); want = want < 4 ? want + 1 : want * 2) {
-                Split sp;
-                sp.kb_per = (int)cdiv(kb, want);
-                sp.splits = (int)cdiv(kb, sp.kb_per);
-                if (want > 1 && sp.splits == 1) continue;
-                const double units = (double)cdiv(tiles * sp.splits, sms);
-                double cost = units * (sp.kb_per * per_kb + epi + 1.0);
-                if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
-                if (cost < best * 0.999) {
-                    best = cost;
-                    bestp.mt = mt;
-                    bestp.bn = bn;
-                    bestp.ntiles = ntiles;
-                    bestp.mtiles = mtiles;
-                    bestp.split = sp;
-                }
-                if (tiles >= sms) break;  // enough tiles: never split
-            }
+    for (const Cand &cd : cands) {
+        if (cd.ts) {
+            if (!allow_ts || forced || forced_ts == 0) continue;
+            if (forced_ts > 0 && forced_ts != cd.ts) continue;
+        } else {
+            if (forced_ts > 0) continue;
+            if (forced && forced != cd.mt * 1000 + cd.bn) continue;
+            if (!forced && cd.mt == 2 && M < 256) continue;
         }
+        const int64_t ntiles = cd.ts ? cdiv(Nout, 128) : cdiv(Nout, cd.bn);
+        const int64_t mtiles = cd.ts ? cdiv(M, cd.ts) : cdiv(M, 128 * cd.mt);
+        const int64_t tiles = ntiles * mtiles;
+        for (int64_t want = 1; want <= std::max<int64_t>(1, kb / 4); want = want < 4 ? want + 1 : want * 2) {
+            Split sp;
+            sp.kb_per = (int)cdiv(kb, want);
+            sp.splits = (int)cdiv(kb, sp.kb_per);
+            if (want > 1 && sp.splits == 1) continue;
+            const double units = (double)cdiv(tiles * sp.splits, sms);
+            double cost = units * (sp.kb_per * cd.per_kb + cd.epi);
+            if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
+            if (cost < best * 0.999) {
+                best = cost;
+                bestp = Q8Plan();
+                bestp.mt = cd.ts ? 1 : cd.mt;
+                bestp.bn = cd.ts ? 128 : cd.bn;
+                bestp.ts = cd.ts;
+                bestp.ntiles = ntiles;
+                bestp.mtiles = mtiles;
+                bestp.split = sp;
+            }
+            if (tiles >= sms) break;  // enough tiles: never split
+        }
+    }
     // The pair kernel (256x256 tiles on 2-CTA clusters) is correct but
     // measured slower than the single-CTA 2x256 plan on every BASELINE shape
     // (about 770 vs 920-1130 TFLOP/s forward), so it runs only when forced.
@@ -325,8 +368,11 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
         if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
     };
     auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
-        Q8Plan p = plan_q8(rows, cols, red, sms, 0);  // the pair plan never splits
-        if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
+        // the pair plan never splits; the TMEM-weight plan may fall back to the other
+        for (int ts = 0; ts < 2; ++ts) {
+            Q8Plan p = plan_q8(rows, cols, red, sms, 0, ts == 1);
+            if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
+        }
     };
     if (M > 0) {
         if (r > 0) sk_part(M, K);  // A*x (forward, or recompute in the backward)
@@ -443,6 +489,24 @@ __global__ void prep_ext_fwd_kernel(const T *__restrict__ B, const float *__rest
     }
 }
 
+// Forward LoRA operand of the TMEM-weight kernel, output-column major:
+// E[n][j] = B[j][n] * s (/ scale[n]), [N][rp].
+template <typename T>
+__global__ void prep_ext_fwd_rows_kernel(const T *__restrict__ B, const float *__restrict__ scales, float s,
+                                         int divide, int64_t r, int64_t rp, int64_t N, T *__restrict__ out) {
+    const int64_t total = rp * N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / rp, j = i % rp;
+        float v = 0.0f;
+        if (j < r) {
+            v = to_f32(B[j * N + n]) * s;
+            if (divide) v = v / scales[n];
+        }
+        out[i] = Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(v);
+    }
+}
+
 __global__ void prep_ext_dx_kernel(const uint16_t *__restrict__ A, int64_t K, int64_t r, int64_t rp,
                                    uint16_t *__restrict__ out) {
     const int64_t total = K * rp;
@@ -491,8 +555,147 @@ void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtenso
     }
 }
 
+template <int DT, int BT>
+void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &te,
+                 const CUtensorMap &tsc, const CUtensorMap &to, const TsArgs &a) {
+    q8ts_gemm_kernel<DT, BT><<<grid, TS_THREADS, TsGeom<BT>::SMEM_BYTES, st>>>(tx, tw, te, tsc, to, a);
+}
+
+// Profiling hook shared by both q8 launch paths: events around the GEMM.
+cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
+    if (!t_prof.on) return nullptr;
+    if (t_prof.used == t_prof.pool.size()) {
+        cudaEvent_t a, b;
+        if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) return nullptr;
+        t_prof.pool.emplace_back(a, b);
+    }
+    auto &pr = t_prof.pool[t_prof.used++];
+    cudaEventRecord(pr.first, st);
+    t_prof.flops += 2.0 * (double)c.M * (double)c.Nout * (double)(c.Kred + c.r);
+    return pr.second;
+}
+
+// The weight-in-TMEM kernel (q8ts_gemm.cuh).
+int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st,
+              const Q8Plan &p) {
+    const int bt = p.ts;
+    CUtensorMap tx, tw, te, tsc, to;
+    int rc = tmap_2d(&tx, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, bt,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t w_inner = c.layout == REELS_W_OUT_CONTIGUOUS ? c.N_w : c.K_w;
+    const uint64_t w_outer = c.layout == REELS_W_OUT_CONTIGUOUS ? c.K_w : c.N_w;
+    const bool inner_is_red = c.fwd ? (c.layout == REELS_W_IN_CONTIGUOUS) : (c.layout == REELS_W_OUT_CONTIGUOUS);
+    // Rows of output columns carry 64 reduction bytes (64B swizzle); rows of
+    // reduction indices carry 128 output-column bytes (128B swizzle).
+    if (inner_is_red)
+        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+    else
+        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 128, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const int64_t ldm = ld_tokens(c.M);
+    if (c.r > 0) {
+        rc = tmap_2d(&te, c.ext_act, tma_act_type(dt), c.M, c.r, (uint64_t)ldm * 2, 64, 64,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+        if (rc) return rc;
+    } else {
+        te = tx;
+    }
+    TsArgs a;
+    memset(&a, 0, sizeof a);
+    a.M = (int)c.M;
+    a.Nout = (int)c.Nout;
+    a.kb_total = (int)cdiv(c.Kred, BK);
+    a.kb_per_split = p.split.kb_per;
+    a.splits = p.split.splits;
+    a.ntiles = (int)p.ntiles;
+    a.mtiles = (int)p.mtiles;
+    a.w_rows_red = inner_is_red ? 0 : 1;
+    a.wscale = c.scales;
+    a.wscale_len = (int)c.N_w;
+    bool ext_divide = false;
+    if (c.fwd) {
+        // bf16: exact int8 in the MMA, scale per output column in the epilogue;
+        // fp16: scale in the dequant (keeps B*s in fp16 range).
+        if (dt == REELS_BF16) {
+            a.scale_mode = 0;
+            a.col_scale = c.scales;
+            ext_divide = true;
+        } else {
+            a.scale_mode = 1;
+        }
+    } else {
+        a.scale_mode = 2;  // dX: the scale sits on the reduction index
+    }
+    if (a.scale_mode == 2) {
+        rc = tmap_2d(&tsc, c.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c.N_w, 1, (uint64_t)round_up(c.N_w * 4, 16),
+                     64, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    } else {
+        tsc = tx;
+    }
+    a.r = (int)c.r;
+    if (c.r > 0) {
+        const int64_t rp = rank_pad(c.r);
+        a.ext_w = c.ext_buf;
+        a.ext_ld = (int)rp;
+        if (c.fwd) {
+            if (dt == REELS_BF16)
+                prep_ext_fwd_rows_kernel<__nv_bfloat16><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                    (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, c.r, rp, c.Nout,
+                    (__nv_bfloat16 *)c.ext_buf);
+            else
+                prep_ext_fwd_rows_kernel<__half><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                    (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
+        } else {
+            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp), 256, 0, st>>>((const uint16_t *)c.lora, c.Nout, c.r, rp,
+                                                                         (uint16_t *)c.ext_buf);
+        }
+        REELS_LAUNCHED();
+    }
+    a.bias = c.bias;
+    a.out = c.out;
+    a.ldo = c.Nout;
+    a.partial = reinterpret_cast<float *>(ws_base + wl.part);
+    a.epi_partial = p.split.splits > 1 ? 1 : 0;
+    a.err = ds.status;
+    if (!a.epi_partial) {
+        // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.
+        rc = tmap_2d(&to, c.out, tma_act_type(dt), c.Nout, c.M, (uint64_t)c.Nout * 2, 32, 32,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+        if (rc) return rc;
+    } else {
+        to = tx;
+    }
+    const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
+    const dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
+    cudaEvent_t ev_stop = prof_begin(st, c);
+    const int key = (dt == REELS_BF16 ? 1000 : 0) + bt;
+    switch (key) {
+        case 1256: launch_ts_t<DT_BF16, 256>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 1192: launch_ts_t<DT_BF16, 192>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 1128: launch_ts_t<DT_BF16, 128>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 256: launch_ts_t<DT_F16, 256>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 192: launch_ts_t<DT_F16, 192>(grid, st, tx, tw, te, tsc, to, a); break;
+        default: launch_ts_t<DT_F16, 128>(grid, st, tx, tw, te, tsc, to, a); break;
+    }
+    REELS_LAUNCHED();
+    if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
+    if (p.split.splits > 1) {
+        q8_reduce_kernel<<<launch_grid(c.M * c.Nout), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+                                                                    a.col_scale, c.bias, dt, c.out, c.Nout);
+        REELS_LAUNCHED();
+    }
+    return REELS_OK;
+}
+
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
-    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters);
+    // The TMEM-weight kernel loads the reduction scales by TMA (16-byte aligned base).
+    const bool ts_ok = aligned16(c.scales);
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters, ts_ok);
+    if (p.ts) return run_q8_ts(c, dt, ds, ws_base, wl, st, p);
     CUtensorMap ta, tw, te;
     // Per-CTA boxes: the pair kernel loads 128 token rows and 128 weight
     // columns per CTA of a 256x256 tile.
@@ -581,19 +784,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.err = ds.status;
     const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
     dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
-    cudaEvent_t ev_stop = nullptr;
-    if (t_prof.on) {
-        if (t_prof.used == t_prof.pool.size()) {
-            cudaEvent_t a, b;
-            REELS_CUDA(cudaEventCreate(&a));
-            REELS_CUDA(cudaEventCreate(&b));
-            t_prof.pool.emplace_back(a, b);
-        }
-        auto &pr = t_prof.pool[t_prof.used++];
-        REELS_CUDA(cudaEventRecord(pr.first, st));
-        ev_stop = pr.second;
-        t_prof.flops += 2.0 * (double)c.M * (double)c.Nout * (double)(c.Kred + c.r);
-    }
+    cudaEvent_t ev_stop = prof_begin(st, c);
     if (p.pair) {
         const dim3 pgrid((unsigned)(2 * std::min<int64_t>(total_tiles, ds.pair_clusters)));
         if (dt == REELS_BF16)

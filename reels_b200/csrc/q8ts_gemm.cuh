@@ -1,0 +1,690 @@
+// Persistent tcgen05 GEMM over an Int8 frozen weight with the dequantised
+// weight held in tensor memory (sm_100a).
+//
+// Same product as q8_gemm.cuh,
+//   D[M x Nout] = [act | ext_act] . [dequant(W) ; ext_w],
+// computed transposed: the tensor core's A operand is a 128-row slice of the
+// weight (128 output columns of D), written by the dequant warps straight
+// into TMEM with tcgen05.st, and its B operand is the activation tile (BT
+// tokens) that TMA leaves in shared memory.  The dequantised weight therefore
+// never touches shared memory: per 64-wide reduction block the SM's shared
+// memory sees the activation tile twice (TMA write, MMA read) and the int8
+// tile twice (TMA write, ldmatrix read), about 60% of the traffic of the
+// SMEM x SMEM kernel, whose 16-bit weight tile is written once and read by
+// both 128-row MMAs.  The accumulator holds D^T (lanes = output columns,
+// columns = tokens); the epilogue transposes through warp shuffles into
+// row-major D.
+//
+// Dequant fragment (both weight orientations): thread t of a warp working on
+// TMEM lane quarter q holds, for 16 reduction indices k0..k0+15, the four
+// bytes k0 + 4(t%4) .. +3 of lanes 32q + 8i + t/4 (i = 0..3).  Weight tiles
+// whose rows are output columns (64 reduction bytes per row, TMA 64B swizzle)
+// are read with ldmatrix.m8n8.x4.b16; tiles whose rows are reduction indices
+// (128 output-column bytes per row, TMA 128B swizzle) with
+// ldmatrix.m16n16.x2.trans.b8, which transposes the bytes on the way.  Each
+// byte quad becomes two bf16x2/f16x2 words, stored with tcgen05.st.16x256b
+// (thread t -> lane t/4 and t/4 + 8, columns 2(t%4), 2(t%4)+1), the operand
+// layout of a K-major TMEM A operand (lane = row, column c = elements 2c, 2c+1).
+//
+// Warp roles: 0 activation TMA, 1 MMA issue, 2 int8 (+ scale) TMA,
+// 3..10 dequant (two groups of four, one warp per TMEM lane quarter; the
+//          groups take alternate reduction blocks so two are in flight),
+// 11..18 epilogue (two per lane quarter, half of the tile's tokens each).
+#pragma once
+#include "q8_gemm.cuh"
+
+namespace reels {
+
+constexpr int TS_NDW = 8;  // dequant warps
+constexpr int TS_NG = 2;   // dequant groups (one warp per TMEM lane quarter each), alternate reduction blocks
+constexpr int TS_GW = TS_NDW / TS_NG;  // warps per group
+constexpr int TS_NEW = 8;  // epilogue warps
+constexpr int TS_THREADS = 32 * (3 + TS_NDW + TS_NEW);
+
+// TMEM (512 columns): NACC accumulators of BT columns and NA A-operand stages
+// of 32 columns (64 16-bit reduction elements).  BT = 256 leaves room for one
+// accumulator only; BT <= 192 double-buffers it so the epilogue overlaps the
+// next tile's MMAs.
+template <int BT>
+struct TsGeom {
+    static constexpr int NACC = BT == 256 ? 1 : 2;
+    static constexpr int NA = BT == 256 ? 8 : (BT == 192 ? 4 : 8);
+    static constexpr int X_BYTES = BT * 128;  // activation tile: BT rows x 64 K, SW128
+    static constexpr int W_BYTES = 128 * 64;  // int8 tile: 128 output columns x 64 K
+    static constexpr int SC_BYTES = 256;      // 64 fp32 reduction scales
+    static constexpr int EPI_BYTES = 4096;    // per epilogue warp: two 32 x 32 16-bit staging tiles
+#ifndef REELS_TS_SX
+#define REELS_TS_SX 0
+#endif
+#ifndef REELS_TS_S8
+#define REELS_TS_S8 0
+#endif
+    static constexpr int SX = REELS_TS_SX ? REELS_TS_SX : (BT == 256 ? 4 : (BT == 192 ? 4 : 6));
+    static constexpr int S8 = REELS_TS_S8 ? REELS_TS_S8 : (BT == 256 ? 6 : 8);
+    static constexpr int X_OFF = 0;
+    static constexpr int W_OFF = X_OFF + SX * X_BYTES;
+    static constexpr int SC_OFF = W_OFF + S8 * W_BYTES;
+    static constexpr int EPI_OFF = (SC_OFF + S8 * SC_BYTES + 1023) / 1024 * 1024;
+    static constexpr int BAR_OFF = EPI_OFF + TS_NEW * EPI_BYTES;
+    // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done
+    static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1;
+    static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
+    static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
+    static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
+    static_assert(NACC * BT + NA * 32 <= 512, "TMEM plan exceeds 512 columns");
+    // Reduction block ga uses barrier slot ga % NA: kb_full is completed by
+    // the activation TMA and the dequant group, kb_empty by the MMA commit
+    // once the block's MMAs are done.  The activation producer reuses X slot
+    // ga % SX after block ga - SX is consumed; with SX <= NA that block's
+    // kb_empty phase cannot have been overtaken, so its parity is unambiguous.
+    static_assert(SX <= NA, "activation ring deeper than the block barrier ring");
+
+    // Accumulator a starts at column 256 * a; A stages fill the columns left over.
+    static __device__ __forceinline__ uint32_t acc_col(int a) { return 256u * a; }
+    static __device__ __forceinline__ uint32_t a_col(int s) {
+        if constexpr (NACC == 1) return 256u + 32u * s;
+        else return (s < NA / 2) ? (uint32_t)BT + 32u * s : 256u + BT + 32u * (s - NA / 2);
+    }
+};
+
+struct TsArgs {
+    int M;             // rows of D (tokens)
+    int Nout;          // columns of D
+    int kb_total;      // main reduction blocks of 64
+    int kb_per_split;
+    int splits;
+    int ntiles, mtiles;
+    int w_rows_red;    // 1: int8 tile rows are reduction indices (transposed read)
+    int scale_mode;    // 0 none, 1 per output column (dequant), 2 per reduction index (dequant)
+    int wscale_len;
+    const float *wscale;
+    int r;             // LoRA rank (0: none)
+    int ext_ld;        // row pitch (elements) of ext_w, which is [Nout][rp]
+    const void *ext_w;
+    int epi_partial;
+    const float *col_scale;  // per output column, applied in the epilogue
+    const void *bias;
+    void *out;
+    long long ldo;
+    float *partial;    // [splits][M][Nout]
+    unsigned *err;
+};
+
+__device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_trans_b8(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// 16 lanes x 16 columns: thread t -> lanes t/4 (v[0..1], v[4..5]) and t/4 + 8
+// (v[2..3], v[6..7]), columns 2(t%4), 2(t%4)+1 and 8 + the same.
+__device__ __forceinline__ void tmem_st_16x256b_x2(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x2.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// TMA tile store from this CTA's shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void *tmap, uint32_t smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(x), "r"(y), "r"(smem_src)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 16 lanes x 32 columns: thread t gets lanes t/4 and t/4 + 8, columns
+// 8g + 2(t%4) and 8g + 2(t%4) + 1 for g = 0..3 (r[4g .. 4g+3]).
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+// Four 8x8 16-bit matrices from mma-fragment registers, each written
+// transposed (fragment row -> shared-memory column); threads 8i..8i+7 give
+// the row addresses of matrix i.
+__device__ __forceinline__ void stsm_x4_trans(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns; thread t gets lane (base + t).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Bounded wait executed by every lane of a warp (the warp stays converged);
+// the result is the same in all lanes.
+__device__ __forceinline__ bool wait_bar_all(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *err,
+                                             unsigned code) {
+    const bool ok = wait_bar(bar, parity, abort, err, code);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Four int8 (one 32-bit word, element 0 in the low byte) -> two 16-bit pairs.
+template <int DT, int SMODE>
+__device__ __forceinline__ void i8x4_convert(uint32_t v, const float *s, uint32_t &w0, uint32_t &w1) {
+    if constexpr (SMODE == 0) {
+        if constexpr (DT == DT_BF16) {
+            w0 = bytes01_to_bf16x2(v, 0x4140u);
+            w1 = bytes01_to_bf16x2(v, 0x4342u);
+        } else {
+            const uint32_t a = v ^ 0x80808080u;
+            w0 = bytes01_to_f16x2(a, 0x4140u);
+            w1 = bytes01_to_f16x2(a, 0x4342u);
+        }
+    } else {
+        const uint32_t a = v ^ 0x80808080u;
+        w0 = scaled_pair<DT>(a, 0, s[0], s[1]);
+        w1 = scaled_pair<DT>(a, 2, s[2], s[3]);
+    }
+}
+
+// One 64-wide reduction block of the weight into TMEM A stage `a_tm` (lane 0
+// address of the stage).  Warp q: lanes 32q..32q+31, all 64 reduction
+// indices.  `lane_s` are the per-lane scales of SMODE 1 (lanes 32q + 8i +
+// t/4); SMODE 2 reads the block's 64 reduction scales from `sc_base`.
+template <int DT, int ROWS_RED, int SMODE>
+__device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_base, uint32_t a_tm, int q, int lane,
+                                                 const float (&lane_s)[4]) {
+    uint32_t raw[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {  // 16-wide reduction chunk
+        if constexpr (ROWS_RED == 0) {
+            // rows = output columns (64 B, 64B swizzle): thread t addresses row 32q + t, chunk j
+            const uint32_t row = 32u * q + lane;
+            ldsm_x4_b16(w_base + row * 64u + ((j ^ ((row >> 1) & 3u)) << 4), raw[j]);
+        } else {
+            // rows = reduction indices (128 B, 128B swizzle): threads 0-15 chunk 2q, 16-31 chunk 2q+1
+            const uint32_t row = 16u * j + (lane & 15);
+            const uint32_t c = 2u * q + (lane >> 4);
+            ldsm_x2_trans_b8(w_base + row * 128u + ((c ^ (row & 7u)) << 4), raw[j]);
+        }
+    }
+    // raw[j][i]: lanes 32q + 8i + t/4, reduction 16j + 4(t%4) .. +3
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // reduction indices 32h .. 32h+31 = TMEM columns 16h .. 16h+15
+        float rs[2][4];
+        if constexpr (SMODE == 2) {
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const float4 s4 = *reinterpret_cast<const float4 *>(
+                    __cvta_shared_to_generic(sc_base + 4u * (16u * (2 * h + jj) + 4u * (lane & 3))));
+                rs[jj][0] = s4.x;
+                rs[jj][1] = s4.y;
+                rs[jj][2] = s4.z;
+                rs[jj][3] = s4.w;
+            }
+        }
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            uint32_t v[8];
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int i = 2 * half + u;
+                    float sc[4];
+                    if constexpr (SMODE == 1) sc[0] = sc[1] = sc[2] = sc[3] = lane_s[i];
+                    if constexpr (SMODE == 2) {
+                        sc[0] = rs[jj][0];
+                        sc[1] = rs[jj][1];
+                        sc[2] = rs[jj][2];
+                        sc[3] = rs[jj][3];
+                    }
+                    i8x4_convert<DT, SMODE>(raw[2 * h + jj][i], sc, v[4 * jj + 2 * u], v[4 * jj + 2 * u + 1]);
+                }
+            tmem_st_16x256b_x2(a_tm + ((uint32_t)(32 * q + 16 * half) << 16) + 16u * h, v);
+        }
+    }
+}
+
+
+struct TsTile {
+    int n0, m0, sp, kb0, n_main, n_ext;
+};
+
+// Tiles run output-column tile fastest, so the CTAs in flight share one
+// activation tile through L2 while the (small) weight stays resident there.
+template <int BT>
+__device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
+    TsTile c;
+    const int nt = t % a.ntiles;
+    const int rest = t / a.ntiles;
+    const int mt = rest % a.mtiles;
+    c.sp = rest / a.mtiles;
+    c.n0 = nt * 128;
+    c.m0 = mt * BT;
+    c.kb0 = c.sp * a.kb_per_split;
+    c.n_main = max(0, min(a.kb_total, c.kb0 + a.kb_per_split) - c.kb0);
+    c.n_ext = (c.sp == a.splits - 1 && a.r > 0) ? (a.r + 63) / 64 : 0;
+    return c;
+}
+
+template <int DT, int BT>
+__global__ void __launch_bounds__(TS_THREADS, 1)
+    q8ts_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmS,
+                     const __grid_constant__ CUtensorMap tmO, const TsArgs args) {
+    using G = TsGeom<BT>;
+    using E = Elem<DT>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+    const uint32_t sbase = smem_u32(smem);
+
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::BAR_OFF);
+    uint64_t *w_full = bars;
+    uint64_t *w_empty = w_full + G::S8;
+    uint64_t *kb_full = w_empty + G::S8;
+    uint64_t *kb_empty = kb_full + G::NA;
+    uint64_t *acc_full = kb_empty + G::NA;
+    uint64_t *acc_empty = acc_full + G::NACC;
+    uint64_t *mma_done = acc_empty + G::NACC;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + G::MISC_OFF);
+    volatile int *abort = reinterpret_cast<volatile int *>(smem + G::MISC_OFF + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int total_tiles = args.ntiles * args.mtiles * args.splits;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < G::S8; ++i) {
+            mbar_init(&w_full[i], 1);
+            mbar_init(&w_empty[i], TS_GW);
+        }
+        for (int i = 0; i < G::NA; ++i) {
+            mbar_init(&kb_full[i], 1 + TS_GW);  // activation TMA (expect_tx) + one dequant group
+            mbar_init(&kb_empty[i], 1);
+        }
+        for (int i = 0; i < G::NACC; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], TS_NEW);
+        }
+        mbar_init(mma_done, 1);
+        *abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+        if (args.r > 0) tma_prefetch_desc(&tmE);
+        if (args.scale_mode == 2) tma_prefetch_desc(&tmS);
+        if (!args.epi_partial) tma_prefetch_desc(&tmO);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool aborted_here = false;
+
+    // Producer and MMA warps run converged; one lane issues the TMA copies,
+    // MMAs and commits.
+    if (warp == 0) {
+        // ------------------------------------------------ activation producer
+        uint32_t gx = 0;
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT>(args, t);
+            for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
+                const int s = gx % G::SX;
+                if (gx >= (uint32_t)G::SX) {
+                    const uint32_t j = gx - G::SX;  // the block that last used this X slot
+                    if (!wait_bar_all(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
+                                      DEVERR_TIMEOUT_AB_EMPTY)) {
+                        aborted_here = true;
+                        break;
+                    }
+                }
+                if (lane == 0) {
+                    uint8_t *dst = smem + G::X_OFF + s * G::X_BYTES;
+                    uint64_t *full = &kb_full[gx % G::NA];
+                    mbar_arrive_expect_tx(full, G::X_BYTES);
+                    if (it < c.n_main) {
+                        tma_load_2d(dst, &tmX, (c.kb0 + it) * BK, c.m0, full);
+                    } else {
+                        // [64 ranks][BT tokens], tokens contiguous: BT/64 boxes of 64 x 64
+                        const int e = it - c.n_main;
+#pragma unroll
+                        for (int b = 0; b < BT / 64; ++b)
+                            tma_load_2d(dst + b * 8192, &tmE, c.m0 + 64 * b, 64 * e, full);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ int8 weight (+ scale) producer
+        uint32_t gw = 0;
+        const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT>(args, t);
+            for (int it = 0; it < c.n_main; ++it, ++gw) {
+                const int s = gw % G::S8;
+                if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
+                    aborted_here = true;
+                    break;
+                }
+                if (lane == 0) {
+                    uint8_t *dst = smem + G::W_OFF + s * G::W_BYTES;
+                    mbar_arrive_expect_tx(&w_full[s], bytes);
+                    const int kb = c.kb0 + it;
+                    if (args.w_rows_red == 0) tma_load_2d(dst, &tmW, kb * BK, c.n0, &w_full[s]);
+                    else tma_load_2d(dst, &tmW, c.n0, kb * BK, &w_full[s]);
+                    if (args.scale_mode == 2)
+                        tma_load_2d(smem + G::SC_OFF + s * G::SC_BYTES, &tmS, kb * BK, 0, &w_full[s]);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        // Lane 0 issues; the wait for block ga + 1 comes right after block
+        // ga's MMAs so its latency overlaps the queued tensor-core work.
+        const int ab = (DT == DT_BF16) ? 1 : 0;
+        const uint32_t id_main = idesc_f16(ab, 0, 0, 128, BT);
+        const uint32_t id_ext = idesc_f16(ab, 0, 1, 128, BT);
+        // Descriptors of X stage 0; a stage or K offset adds (bytes >> 4) to the address field.
+        const uint64_t dmain0 = sdesc_sw128(sbase + G::X_OFF, 16, 1024);
+        const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
+        uint32_t ga = 0, local = 0;
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
+            const TsTile c = ts_tile<BT>(args, t);
+            const int acc = local % G::NACC;
+            if (!wait_bar_all(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+                aborted_here = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d_tm = tmem + G::acc_col(acc);
+            const int n_iter = c.n_main + c.n_ext;
+            if (n_iter > 0 &&
+                !wait_bar_all(&kb_full[ga % G::NA], (ga / G::NA) & 1, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
+                aborted_here = true;
+                break;
+            }
+            for (int it = 0; it < n_iter; ++it, ++ga) {
+                tc_fence_after();
+                const int sx = ga % G::SX, sa = ga % G::NA;
+                const uint32_t a_tm = tmem + G::a_col(sa);
+                const uint64_t xoff = (uint64_t)((sx * G::X_BYTES) >> 4);
+                if (lane == 0) {
+                    if (it < c.n_main) {
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            mma_f16_ts(d_tm, a_tm + 8 * kk, dmain0 + xoff + (uint64_t)(kk * 2), id_main,
+                                       (it > 0 || kk > 0) ? 1u : 0u);
+                    } else {
+                        const int e = it - c.n_main;
+                        const int nk = (min(64, args.r - 64 * e) + 15) / 16;
+                        for (int kk = 0; kk < nk; ++kk)
+                            mma_f16_ts(d_tm, a_tm + 8 * kk, dext0 + xoff + (uint64_t)(kk * 128), id_ext,
+                                       (it > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+                __syncwarp();
+                bool ok = true;
+                if (it + 1 < n_iter)
+                    ok = wait_bar_all(&kb_full[(ga + 1) % G::NA], ((ga + 1) / G::NA) & 1, abort, args.err,
+                                      DEVERR_TIMEOUT_AB_FULL);
+                if (lane == 0) mma_commit(&kb_empty[sa]);
+                __syncwarp();
+                if (!ok) {
+                    aborted_here = true;
+                    break;
+                }
+            }
+            if (aborted_here) break;
+            if (lane == 0) mma_commit(&acc_full[acc]);
+            __syncwarp();
+        }
+        if (lane == 0) mma_commit(mma_done);
+        __syncwarp();
+    } else if (warp < 3 + TS_NDW) {
+        // ------------------------------------------------ dequant warps
+        const int q = warp & 3;               // TMEM lane quarter
+        const int g = (warp - 3) / TS_GW;     // group: reduction blocks with ga % TS_NG == g
+        uint32_t ga = 0, gw = 0;
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT>(args, t);
+            // Per-lane scales (lanes 32q + 8i + t/4) for SMODE 1.
+            float lane_s[4] = {0.f, 0.f, 0.f, 0.f};
+            if (args.scale_mode == 1) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int n = c.n0 + 32 * q + 8 * i + (lane >> 2);
+                    lane_s[i] = n < args.wscale_len ? __ldg(args.wscale + n) : 0.0f;
+                }
+            }
+            const int n_iter = c.n_main + c.n_ext;
+            for (int it = 0; it < n_iter; ++it, ++ga) {
+                const bool main_blk = it < c.n_main;
+                const uint32_t gw_this = gw;
+                if (main_blk) ++gw;
+                if ((int)(ga % TS_NG) != g) continue;
+                const int sw = gw_this % G::S8;
+                if (main_blk &&
+                    !wait_bar_all(&w_full[sw], (gw_this / G::S8) & 1, abort, args.err, DEVERR_TIMEOUT_W_FULL)) {
+                    aborted_here = true;
+                    break;
+                }
+                const int sa = ga % G::NA;
+                if (!wait_bar_all(&kb_empty[sa], ((ga / G::NA) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
+                    aborted_here = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_tm = tmem + G::a_col(sa);
+                if (main_blk) {
+                    const uint32_t w_base = sbase + G::W_OFF + sw * G::W_BYTES;
+                    const uint32_t sc_base = sbase + G::SC_OFF + sw * G::SC_BYTES;
+                    switch (args.w_rows_red * 3 + args.scale_mode) {
+                        case 0: ts_dequant_block<DT, 0, 0>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 1: ts_dequant_block<DT, 0, 1>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 2: ts_dequant_block<DT, 0, 2>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 3: ts_dequant_block<DT, 1, 0>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 4: ts_dequant_block<DT, 1, 1>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        default: ts_dequant_block<DT, 1, 2>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&w_empty[sw]);
+                } else {
+                    // LoRA block: rows n0 + lane of the prepared [Nout][rp] operand,
+                    // 16-bit pairs already in TMEM column order.
+                    const int e = it - c.n_main;
+                    const uint16_t *src = reinterpret_cast<const uint16_t *>(args.ext_w);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            uint32_t v[8];
+#pragma unroll
+                            for (int jj = 0; jj < 2; ++jj)
+#pragma unroll
+                                for (int u = 0; u < 2; ++u) {
+                                    const int n = c.n0 + 32 * q + 16 * half + 8 * u + (lane >> 2);
+                                    const int k = 64 * e + 16 * (2 * h + jj) + 4 * (lane & 3);
+                                    uint2 w = make_uint2(0, 0);
+                                    if (n < args.Nout)
+                                        w = __ldg(
+                                            reinterpret_cast<const uint2 *>(src + (long long)n * args.ext_ld + k));
+                                    v[4 * jj + 2 * u] = w.x;
+                                    v[4 * jj + 2 * u + 1] = w.y;
+                                }
+                            tmem_st_16x256b_x2(a_tm + ((uint32_t)(32 * q + 16 * half) << 16) + 16u * h, v);
+                        }
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&kb_full[sa]);
+            }
+        }
+    } else {
+        // ------------------------------------------------ epilogue warps
+        // 32 x 32 chunks of D^T (32 output columns of this warp's TMEM lane
+        // quarter x 32 tokens).  Split partials: fp32 straight from a
+        // thread-per-column load (a warp writes 128 contiguous bytes per
+        // token).  Otherwise the 16x256b load gives mma fragments (rows =
+        // columns of D, column pairs = tokens); after scale, bias and rounding
+        // stmatrix.trans writes them token-major into a 64B-swizzled staging
+        // tile that one TMA store copies to D.
+        const int ew = warp - (3 + TS_NDW);
+        const int q = warp & 3;
+        const int set = ew >> 2;
+        const uint32_t stage0 = sbase + G::EPI_OFF + ew * G::EPI_BYTES;
+        int buf = 0;
+        uint32_t local = 0;
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
+            const TsTile c = ts_tile<BT>(args, t);
+            const int acc = local % G::NACC;
+            if (!wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+                aborted_here = true;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t t_base = tmem + ((uint32_t)(32 * q) << 16) + G::acc_col(acc);
+            constexpr int NCH = BT / 64;  // 32-column chunks per epilogue set
+            if (args.epi_partial) {
+                const int n = c.n0 + 32 * q + lane;
+                const bool n_ok = n < args.Nout;
+                for (int ch = 0; ch < NCH; ++ch) {
+                    const int j0 = set * (BT / 2) + 32 * ch;
+                    uint32_t v[32];
+                    tmem_ld32(t_base + j0, v);
+                    tmem_wait_ld();
+                    if (ch == NCH - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    }
+                    const int m_base = c.m0 + j0;
+                    float *dst = args.partial + ((long long)c.sp * args.M + m_base) * args.Nout + n;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (n_ok && m_base + j < args.M) dst[(long long)j * args.Nout] = __uint_as_float(v[j]);
+                }
+                continue;
+            }
+            // Column scale and bias of the four output columns this thread holds:
+            // 32q + 16hh + 8k + t/4.
+            float cs[2][2], bs[2][2];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int n = c.n0 + 32 * q + 16 * hh + 8 * k + (lane >> 2);
+                    cs[hh][k] = 1.0f;
+                    bs[hh][k] = 0.0f;
+                    if (n < args.Nout) {
+                        if (args.col_scale) cs[hh][k] = __ldg(args.col_scale + n);
+                        if (args.bias) bs[hh][k] = E::to_f(reinterpret_cast<const typename E::T *>(args.bias)[n]);
+                    }
+                }
+            for (int ch = 0; ch < NCH; ++ch) {
+                const int j0 = set * (BT / 2) + 32 * ch;  // first token column of the chunk
+                uint32_t r[2][16];
+                tmem_ld_16x256b_x4(t_base + j0, r[0]);
+                tmem_ld_16x256b_x4(t_base + (16u << 16) + j0, r[1]);
+                tmem_wait_ld();
+                if (ch == NCH - 1) {
+                    // all of this warp's accumulator columns are in registers
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                }
+                const int m_base = c.m0 + j0;
+                // The staging tile this chunk reuses was last read by the TMA
+                // store issued two chunks ago.
+                if (lane == 0) bulk_wait_group_read<1>();
+                __syncwarp();
+                const uint32_t st_tile = stage0 + buf * 2048;
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    // matrix (column block nb = 2hh + k, token block g)
+                    uint32_t pm[4];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                        for (int k = 0; k < 2; ++k)
+                            pm[2 * hh + k] =
+                                E::pack2(fmaf(__uint_as_float(r[hh][4 * g + 2 * k]), cs[hh][k], bs[hh][k]),
+                                         fmaf(__uint_as_float(r[hh][4 * g + 2 * k + 1]), cs[hh][k], bs[hh][k]));
+                    // thread 8i + j: row (token) 8g + j of matrix i, 16-byte chunk i (64B swizzle)
+                    const uint32_t row = 8 * g + (lane & 7);
+                    const uint32_t nb = lane >> 3;
+                    stsm_x4_trans(st_tile + row * 64 + ((nb ^ ((row >> 1) & 3)) << 4), pm[0], pm[1], pm[2], pm[3]);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && m_base < args.M) {  // rows past M are clipped by the TMA unit
+                    tma_store_2d(&tmO, st_tile, c.n0 + 32 * q, m_base);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            }
+        }
+        // Stores must finish reading shared memory before the CTA exits.
+        if (lane == 0) bulk_wait_group<0>();
+        __syncwarp();
+    }
+
+    if (aborted_here && (warp == 0 || warp == 2)) {
+        for (int i = 0; i < 64; ++i) __nanosleep(2000);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        if (lane == 0) {
+            long long t0 = clock64();
+            while (!mbar_try_wait(mma_done, 0)) {
+                if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
+                    atomicOr(args.err, DEVERR_TIMEOUT_ACC);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace reels

@@ -1,6 +1,8 @@
-"""GPU parity of the pair-CTA (cta_group::2) q8 GEMM, which the planner only
-uses when REELS_Q8_TILE=pair forces it.  The override is read once per
-process, so the cases run in a child process."""
+"""GPU parity of q8 GEMM plans the planner does not pick for these shapes by
+itself: the pair-CTA (cta_group::2) SMEM x SMEM kernel (REELS_Q8_TILE=pair),
+the SMEM x SMEM kernel (REELS_Q8_TS=0) and each token tile of the
+weight-in-TMEM kernel (REELS_Q8_TS=256/192/128).  The overrides are read once
+per process, so each plan runs its cases in a child process."""
 import json
 import os
 import subprocess
@@ -35,13 +37,19 @@ for (M, K, N, r, layout, dt) in {cases!r}:
 print(json.dumps(out))
 """
 
-CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1024, 512, 8, 0, "f16")]
+CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1024, 512, 8, 0, "f16"),
+         (1000, 640, 1152, 32, 1, "f16"), (2048, 1536, 640, 32, 0, "bf16")]
 
 
-def test_pair_kernel_parity():
+@pytest.mark.parametrize("var,val", [("REELS_Q8_TILE", "pair"), ("REELS_Q8_TS", "0"), ("REELS_Q8_TS", "256"),
+                                     ("REELS_Q8_TS", "192"), ("REELS_Q8_TS", "128")])
+def test_forced_plan_parity(var, val):
     from reels_b200 import build
     build.build()
-    env = dict(os.environ, REELS_Q8_TILE="pair")
+    env = dict(os.environ)
+    env.pop("REELS_Q8_TILE", None)
+    env.pop("REELS_Q8_TS", None)
+    env[var] = val
     code = CHILD.format(root=ROOT, tests=os.path.join(ROOT, "tests"), cases=CASES)
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stderr[-2000:]
