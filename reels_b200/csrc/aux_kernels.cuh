@@ -143,10 +143,12 @@ __global__ void q8_reduce_kernel(const float *__restrict__ partial, int splits, 
 __global__ void sk_reduce_kernel(const float *__restrict__ partial, int splits, int64_t rows, int npad, int ncols,
                                  int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
                                  int64_t cs) {
+    // Consecutive threads take consecutive columns of one row, so the partial
+    // reads are contiguous.
     const int64_t total = rows * (int64_t)ncols;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i / rows, row = i % rows;
+        const int64_t row = i / ncols, j = i % ncols;
         float acc = 0.0f;
         for (int s = 0; s < splits; ++s) acc += partial[((int64_t)s * rows + row) * npad + j];
         if (epi == 0) {

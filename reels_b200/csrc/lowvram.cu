@@ -222,19 +222,36 @@ struct Split {
     int kb_per = 1;
 };
 
-// Spread the reduction over more CTAs when the output tiles alone do not
-// fill the machine; every split keeps at least `min_kb` blocks of 64.
-Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb) {
-    Split s;
+// Split of the reduction for the skinny kernels: the split count that
+// minimises (waves of CTAs) x (reduction blocks per CTA) plus the fp32
+// partial traffic, in units of one reduction block of one tile (16 KB of
+// 16-bit activations; a partial tile of 128 x npad fp32 is written once and
+// read once).  Each CTA runs one (tile, split) unit and the SK kernel is one
+// CTA per SM, so a count that spills a few CTAs into a second wave roughly
+// doubles the time.
+Split plan_split(int64_t tiles, int64_t kb, int sms, int64_t min_kb, int64_t npad) {
+    Split best;
     kb = std::max<int64_t>(kb, 1);
-    int64_t want = 1;
-    if (tiles < sms) want = cdiv(sms, tiles);
-    want = std::min<int64_t>(want, std::max<int64_t>(1, kb / min_kb));
-    want = std::max<int64_t>(want, 1);
-    s.kb_per = (int)cdiv(kb, want);
-    s.splits = (int)cdiv(kb, s.kb_per);
-    return s;
+    double best_cost = 1e300;
+    const int64_t max_want = std::max<int64_t>(1, kb / min_kb);
+    const double part_cost = 2.0 * 128.0 * (double)npad * 4.0 / 16384.0;  // per partial tile, in block units
+    for (int64_t want = 1; want <= max_want; ++want) {
+        Split s;
+        s.kb_per = (int)cdiv(kb, want);
+        s.splits = (int)cdiv(kb, s.kb_per);
+        if (want > 1 && s.splits != want) continue;
+        const double waves = (double)cdiv(tiles * s.splits, sms);
+        double cost = waves * s.kb_per;
+        if (s.splits > 1) cost += part_cost * (double)(tiles * s.splits) / sms + 2.0;
+        if (cost < best_cost * 0.999) {
+            best_cost = cost;
+            best = s;
+        }
+    }
+    return best;
 }
+
+int npad_of(int64_t r) { return (int)std::max<int64_t>(16, round_up(r, 16)); }
 
 struct Q8Plan {
     int mt = 1, bn = 256;
@@ -336,9 +353,10 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
     return bestp;
 }
 
-Split plan_sk(int64_t rows, int64_t red, int sms) { return plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4); }
+Split plan_sk(int64_t rows, int64_t red, int sms, int64_t r) {
+    return plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4, npad_of(r));
+}
 
-int npad_of(int64_t r) { return (int)std::max<int64_t>(16, round_up(r, 16)); }
 
 // Workspace layout shared by the forward and backward passes.
 struct Ws {
@@ -364,7 +382,7 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
     size_t part = 0;
     const int64_t np = npad_of(r);
     auto sk_part = [&](int64_t rows, int64_t red) {
-        Split s = plan_sk(rows, red, sms);
+        Split s = plan_sk(rows, red, sms, r);
         if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
     };
     auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
@@ -437,7 +455,7 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     rc = tmap_2d(&tb, c.bop, tma_act_type(dt), c.red, c.r, (uint64_t)c.bop_pitch * 2, 64, np,
                  CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    Split s = plan_sk(c.rows, c.red, ds.sms);
+    Split s = plan_sk(c.rows, c.red, ds.sms, c.r);
     SkArgs a;
     a.rows = (int)c.rows;
     a.kb_total = (int)cdiv(c.red, BK);

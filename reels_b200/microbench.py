@@ -4,9 +4,10 @@
     python -m reels_b200.microbench M K N [layout] [--reps R]
 
 Prints one JSON line: microseconds and TFLOP/s (2*M*N*K / time) per pass,
-CUDA-event timed on the launching stream after warm-up.  The tile shape
-follows the library's planner; the REELS_Q8_TILE environment variable
-("2x256", "2x128", "1x256", "1x128") forces one.
+CUDA-event timed on the launching stream after warm-up.  The kernel and tile
+shape follow the library's planner; REELS_Q8_TS (256, 192, 128, or 0 for the
+SMEM x SMEM kernel) and REELS_Q8_TILE ("2x256", "2x128", "1x256", "1x128",
+"pair") force one.
 """
 from __future__ import annotations
 
