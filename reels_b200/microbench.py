@@ -1,7 +1,7 @@
 """Time the q8 GEMM of the forward (_weight_mul) and of dX
 (_weight_transpose_mul) for one shape through the C ABI.
 
-    python -m reels_b200.microbench M K N [layout] [--reps R]
+    python -m reels_b200.microbench M K N [layout] [--reps R] [--once]
 
 Prints one JSON line: microseconds and TFLOP/s (2*M*N*K / time) per pass,
 CUDA-event timed on the launching stream after warm-up.  The kernel and tile
@@ -28,6 +28,8 @@ def main():
     ap.add_argument("layout", type=int, nargs="?", default=0)
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--dtype", default="bf16", choices=["bf16", "f16"])
+    ap.add_argument("--once", action="store_true",
+                    help="one forward and one dX launch, no timing (for a profiler capture)")
     a = ap.parse_args()
     native_build.build()
     L = nat.lib()
@@ -53,6 +55,13 @@ def main():
             dy.data_ptr(), q.data_ptr(), s.data_ptr(), layout, M, K, N, dt, dx.data_ptr(), ws.data_ptr(), wsn, st))
 
     out = {"M": M, "K": K, "N": N, "layout": layout, "dtype": a.dtype}
+    if a.once:
+        fwd()
+        bwd()
+        torch.cuda.synchronize(dev)
+        nat.check("device status", L.reels_lowvram_check_device_status(st))
+        print(json.dumps(out), flush=True)
+        return
     for name, fn in (("fwd", fwd), ("dx", bwd)):
         for _ in range(3):
             fn()
