@@ -365,15 +365,15 @@ def run_ours(args):
                        "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (about 5 GB of activations and gradients per step)"},
             "tflops": flops * world * args.steps / (ms / 1e3) / 1e12,
-            "roofline": {"bound": "tensor", "kernel": "q8_gemm_kernel (forward Y and dX)",
+            "roofline": {"bound": "tensor", "kernel": "q8ts_gemm_kernel (forward Y and dX)",
                          "achieved": q8_tflops, "peak": peak, "unit": "TFLOP/s",
                          "frac": (q8_tflops / peak) if q8_tflops else None,
                          "peak_source": f"bf16_tflops_sustained of {peak_kind}",
                          "launches": q8_n, "algorithmic_flops_per_launch": (q8_flops / q8_n) if q8_n else None,
                          "traffic": traffic,
                          "algorithmic_bytes_per_launch": alg_per_launch,
-                         "traffic_source": (f"ncu DRAM read+write of one launch of the same kernel on a smaller case "
-                                            f"({ratio_src}) as a fraction of its algorithmic bytes ({ratio:.3f}), "
+                         "traffic_source": (f"ncu DRAM read+write of the same kernel's launches on a smaller case "
+                                            f"({ratio_src}) as a fraction of their algorithmic bytes ({ratio:.3f}), "
                                             f"times this workload's algorithmic bytes per launch"
                                             if ratio is not None else None)},
             "cpu_baseline": cpu,
