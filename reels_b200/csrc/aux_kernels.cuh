@@ -111,52 +111,88 @@ __global__ void materialize_kernel(const int8_t *__restrict__ q, const float *__
     }
 }
 
-// A [K][r] -> At [r][K] (same element type, 2 bytes).
-__global__ void transpose_rank_kernel(const uint16_t *__restrict__ a, int64_t K, int r, uint16_t *__restrict__ at) {
-    const int64_t total = K * r;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t j = i / K, k = i % K;
+// A [K][r] -> At [r][K] (same element type, 2 bytes).  K * r < 2^31.
+__global__ void transpose_rank_kernel(const uint16_t *__restrict__ a, int K, int r, uint16_t *__restrict__ at) {
+    const int total = K * r;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int j = i / K, k = i - j * K;
         at[i] = a[k * r + j];
     }
 }
 
 // -------------------------------------------------- split-K reductions
-// Sum q8 partials [splits][M][Nout] and apply the output epilogue.
+// Sum q8 partials [splits][M][Nout] and apply the output epilogue.  Four
+// consecutive columns per thread (Nout is a multiple of 16 on the tensor-core
+// path), 16-byte loads, the split loop unrolled so its loads are in flight
+// together; the sum runs over s = 0 .. splits-1 in order.
 __global__ void q8_reduce_kernel(const float *__restrict__ partial, int splits, int64_t M, int64_t Nout,
                                  const float *__restrict__ col_scale, const void *bias, int dt, void *out,
                                  int64_t ldo) {
-    const int64_t total = M * Nout;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float acc = 0.0f;
-        for (int s = 0; s < splits; ++s) acc += partial[(int64_t)s * total + i];
-        const int64_t row = i / Nout, col = i % Nout;
-        if (col_scale) acc *= col_scale[col];
-        if (bias) acc += load_act(bias, col, dt);
-        store_act(out, row * ldo + col, dt, acc);
+    const int64_t total4 = M * Nout / 4;
+    const float4 *p4 = reinterpret_cast<const float4 *>(partial);
+    for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4;
+         i4 += (int64_t)gridDim.x * blockDim.x) {
+        float4 acc = __ldg(p4 + i4);
+#pragma unroll 4
+        for (int s = 1; s < splits; ++s) {
+            const float4 v = __ldg(p4 + (int64_t)s * total4 + i4);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const int64_t i = i4 * 4, row = i / Nout, col = i % Nout;
+        float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (col_scale) a[u] *= col_scale[col + u];
+            if (bias) a[u] += load_act(bias, col + u, dt);
+            store_act(out, row * ldo + col + u, dt, a[u]);
+        }
     }
 }
 
 // Sum skinny partials [splits][rows][npad] and apply epi 0 (transposed
 // store, act dtype) or epi 1 (fp32 accumulate into out[row*rs + j*cs]).
+// The outputs are few and the splits many, so the sum is latency-bound: four
+// threads share an output, thread t of the four adds the splits s = t mod 4
+// in order with eight loads in flight, and the four partial sums are
+// combined in a fixed order (deterministic from run to run).
 __global__ void sk_reduce_kernel(const float *__restrict__ partial, int splits, int64_t rows, int npad, int ncols,
                                  int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
                                  int64_t cs) {
-    // Consecutive threads take consecutive columns of one row, so the partial
-    // reads are contiguous.
     const int64_t total = rows * (int64_t)ncols;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = i / ncols, j = i % ncols;
+    const int lane = threadIdx.x & 31, sl = lane & 3;
+    const int64_t stride = rows * (int64_t)npad;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w * 8 < total; w += nw) {
+        const int64_t o = w * 8 + (lane >> 2);  // consecutive outputs: consecutive columns of a row
         float acc = 0.0f;
-        for (int s = 0; s < splits; ++s) acc += partial[((int64_t)s * rows + row) * npad + j];
-        if (epi == 0) {
-            store_act(out, j * ldo + row, dt, alpha * acc);
-        } else {
-            float *o = reinterpret_cast<float *>(out);
-            const int64_t idx = row * rs + j * cs;
-            o[idx] = (accumulate ? o[idx] : 0.0f) + alpha * acc;
+        int64_t row = 0, j = 0;
+        if (o < total) {
+            row = o / ncols;
+            j = o % ncols;
+            const float *p = partial + row * npad + j;
+            int s = sl;
+            for (; s + 28 < splits; s += 32) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (int64_t)(s + 4 * u) * stride);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc += v[u];
+            }
+            for (; s < splits; s += 4) acc += __ldg(p + (int64_t)s * stride);
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (sl == 0 && o < total) {
+            if (epi == 0) {
+                store_act(out, j * ldo + row, dt, alpha * acc);
+            } else {
+                float *o32 = reinterpret_cast<float *>(out);
+                const int64_t idx = row * rs + j * cs;
+                o32[idx] = (accumulate ? o32[idx] : 0.0f) + alpha * acc;
+            }
         }
     }
 }

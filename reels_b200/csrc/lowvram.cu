@@ -477,7 +477,7 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     else sk_gemm_kernel<DT_F16><<<grid, SK_THREADS, SK_SMEM_BYTES, st>>>(ta, tb, a);
     REELS_LAUNCHED();
     if (s.splits > 1) {
-        sk_reduce_kernel<<<launch_grid(c.rows * c.r), 256, 0, st>>>(a.partial, s.splits, c.rows, np, (int)c.r,
+        sk_reduce_kernel<<<launch_grid(c.rows * c.r * 4), 256, 0, st>>>(a.partial, s.splits, c.rows, np, (int)c.r,
                                                                     c.epi_final, c.alpha, c.accumulate, dt, c.out,
                                                                     c.ldo, c.rs, c.cs);
         REELS_LAUNCHED();
@@ -508,30 +508,53 @@ __global__ void prep_ext_fwd_kernel(const T *__restrict__ B, const float *__rest
 }
 
 // Forward LoRA operand of the TMEM-weight kernel, output-column major:
-// E[n][j] = B[j][n] * s (/ scale[n]), [N][rp].
+// E[n][j] = B[j][n] * s (/ scale[n]), [N][rp].  A block transposes a tile of
+// 32 columns x rp ranks through shared memory: B rows are read along n and E
+// rows written along j, both coalesced.
 template <typename T>
 __global__ void prep_ext_fwd_rows_kernel(const T *__restrict__ B, const float *__restrict__ scales, float s,
-                                         int divide, int64_t r, int64_t rp, int64_t N, T *__restrict__ out) {
-    const int64_t total = rp * N;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t n = i / rp, j = i % rp;
-        float v = 0.0f;
-        if (j < r) {
-            v = to_f32(B[j * N + n]) * s;
-            if (divide) v = v / scales[n];
+                                         int divide, int r, int rp, int N, T *__restrict__ out) {
+    __shared__ float tile[128][33];
+    const int n0 = blockIdx.x * 32;
+    for (int jb = 0; jb < rp; jb += 128) {
+        // load B[jb .. jb+127][n0 .. n0+31] (zero past r or N)
+        for (int e = threadIdx.x; e < 128 * 32; e += blockDim.x) {
+            const int jj = e >> 5, nn = e & 31;
+            const int j = jb + jj, n = n0 + nn;
+            float v = 0.0f;
+            if (j < r && n < N) {
+                v = to_f32(B[(int64_t)j * N + n]) * s;
+                if (divide) v = v / scales[n];
+            }
+            tile[jj][nn] = v;
         }
-        out[i] = Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(v);
+        __syncthreads();
+        const int jw = min(128, rp - jb);
+        for (int e = threadIdx.x; e < 32 * jw; e += blockDim.x) {
+            const int nn = e / jw, jj = e - nn * jw;
+            const int n = n0 + nn;
+            if (n < N) out[(int64_t)n * rp + jb + jj] = Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(tile[jj][nn]);
+        }
+        __syncthreads();
     }
 }
 
-__global__ void prep_ext_dx_kernel(const uint16_t *__restrict__ A, int64_t K, int64_t r, int64_t rp,
-                                   uint16_t *__restrict__ out) {
-    const int64_t total = K * rp;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t k = i / rp, j = i % rp;
-        out[i] = j < r ? A[k * r + j] : (uint16_t)0;
+// dX LoRA operand E[k][j] = A[k][j] (j < r), zero-padded to rp columns.
+// Eight columns per thread, one 16-byte store.
+__global__ void prep_ext_dx_kernel(const uint16_t *__restrict__ A, int K, int r, int rp, uint16_t *__restrict__ out) {
+    const int per_row = rp / 8;
+    const int total = K * per_row;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int k = i / per_row, j0 = (i - k * per_row) * 8;
+        uint16_t v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = (j0 + u < r) ? A[(int64_t)k * r + j0 + u] : (uint16_t)0;
+        uint4 w;
+        w.x = v[0] | ((uint32_t)v[1] << 16);
+        w.y = v[2] | ((uint32_t)v[3] << 16);
+        w.z = v[4] | ((uint32_t)v[5] << 16);
+        w.w = v[6] | ((uint32_t)v[7] << 16);
+        *reinterpret_cast<uint4 *>(out + (int64_t)k * rp + j0) = w;
     }
 }
 
@@ -661,15 +684,16 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
         a.ext_ld = (int)rp;
         if (c.fwd) {
             if (dt == REELS_BF16)
-                prep_ext_fwd_rows_kernel<__nv_bfloat16><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
-                    (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, c.r, rp, c.Nout,
-                    (__nv_bfloat16 *)c.ext_buf);
+                prep_ext_fwd_rows_kernel<__nv_bfloat16><<<(unsigned)cdiv(c.Nout, 32), 256, 0, st>>>(
+                    (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, (int)c.r, (int)rp,
+                    (int)c.Nout, (__nv_bfloat16 *)c.ext_buf);
             else
-                prep_ext_fwd_rows_kernel<__half><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
-                    (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
+                prep_ext_fwd_rows_kernel<__half><<<(unsigned)cdiv(c.Nout, 32), 256, 0, st>>>(
+                    (const __half *)c.lora, c.scales, c.ext_scale, 0, (int)c.r, (int)rp, (int)c.Nout,
+                    (__half *)c.ext_buf);
         } else {
-            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp), 256, 0, st>>>((const uint16_t *)c.lora, c.Nout, c.r, rp,
-                                                                         (uint16_t *)c.ext_buf);
+            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp / 8), 256, 0, st>>>(
+                (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
         }
         REELS_LAUNCHED();
     }
@@ -702,7 +726,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
-        q8_reduce_kernel<<<launch_grid(c.M * c.Nout), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+        q8_reduce_kernel<<<launch_grid(c.M * c.Nout / 4), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
                                                                     a.col_scale, c.bias, dt, c.out, c.Nout);
         REELS_LAUNCHED();
     }
@@ -788,8 +812,8 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
                     (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
         } else {
             a.ext_ld = (int)rp;
-            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp), 256, 0, st>>>((const uint16_t *)c.lora, c.Nout, c.r, rp,
-                                                                         (uint16_t *)c.ext_buf);
+            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp / 8), 256, 0, st>>>(
+                (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
         }
         REELS_LAUNCHED();
     }
@@ -815,7 +839,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
-        q8_reduce_kernel<<<launch_grid(c.M * c.Nout), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+        q8_reduce_kernel<<<launch_grid(c.M * c.Nout / 4), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
                                                                     a.col_scale, c.bias, dt, c.out, c.Nout);
         REELS_LAUNCHED();
     }
@@ -842,7 +866,7 @@ int check_ws(void *ws, size_t ws_bytes, const Ws &wl) {
 
 // A [K][r] -> At [r][K]
 int transpose_rank(const void *A, int64_t K, int64_t r, void *At, cudaStream_t st) {
-    transpose_rank_kernel<<<launch_grid(K * r), 256, 0, st>>>(reinterpret_cast<const uint16_t *>(A), K, (int)r,
+    transpose_rank_kernel<<<launch_grid(K * r), 256, 0, st>>>(reinterpret_cast<const uint16_t *>(A), (int)K, (int)r,
                                                               reinterpret_cast<uint16_t *>(At));
     REELS_LAUNCHED();
     return REELS_OK;
