@@ -99,17 +99,20 @@ cudaError_t set_q8_attrs() {
     return set_q8_attr<DT, 2, 256>();
 }
 
+template <int DT, int BT, int KB2>
+cudaError_t set_ts_attr() {
+    return cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                TsGeom<BT, KB2>::SMEM_BYTES);
+}
 template <int DT>
 cudaError_t set_ts_attrs() {
-    cudaError_t e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         TsGeom<256>::SMEM_BYTES);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 192>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 TsGeom<192>::SMEM_BYTES);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 TsGeom<128>::SMEM_BYTES);
-    return e;
+    cudaError_t e;
+    if ((e = set_ts_attr<DT, 256, 1>()) != cudaSuccess) return e;
+    if ((e = set_ts_attr<DT, 192, 1>()) != cudaSuccess) return e;
+    if ((e = set_ts_attr<DT, 128, 1>()) != cudaSuccess) return e;
+    if ((e = set_ts_attr<DT, 256, 2>()) != cudaSuccess) return e;
+    if ((e = set_ts_attr<DT, 192, 2>()) != cudaSuccess) return e;
+    return set_ts_attr<DT, 128, 2>();
 }
 
 int bind_device(const void *ptr, DeviceState **out) {
@@ -257,22 +260,27 @@ struct Q8Plan {
     int mt = 1, bn = 256;
     bool pair = false;  // 2-CTA cluster kernel on 256x256 tiles
     int ts = 0;         // > 0: weight-in-TMEM kernel, 128 output columns x ts tokens
+    int ts_kb2 = 1;     // its pipeline stages cover 64 * ts_kb2 reduction elements
     int64_t ntiles = 1, mtiles = 1;
     Split split;
 };
 
 // Kernel, tile shape and reduction split from a time model fitted to B200
-// measurements (bf16; microseconds per 64-wide reduction block of one tile,
-// plus a per-tile epilogue cost the kernel cannot overlap):
-//   weight-in-TMEM kernel (q8ts_gemm.cuh), 128 output columns x bt tokens:
-//       bt 256: 0.49 + 1.1 per tile (single accumulator), bt 192: 0.44 + 0.4,
-//       bt 128: 0.48 + 0.4;
+// measurements (bf16; microseconds per pipeline stage of one tile, plus a
+// per-tile epilogue cost the kernel cannot overlap):
+//   weight-in-TMEM kernel (q8ts_gemm.cuh), 128 output columns x bt tokens,
+//   stages of 64 reduction elements: bt 256: 0.49 + 1.1 per tile (single
+//       accumulator), bt 192: 0.44 + 0.4, bt 128: 0.48 + 0.4;
+//   stages of 128: bt 128: 0.60 + 0.4, bt 256: 1.07 + 1.1, bt 192: 1.02 + 0.4.
+//   The MMA warp's per-stage synchronisation costs about the same whatever
+//   the stage width, so 128-wide stages stream the weight twice as fast when
+//   there are few tokens; with many tokens the 256-token tiles win.
 //   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
 // split reduction adds the write and re-read of fp32 partials (~5 TB/s).
-// REELS_Q8_TILE ("MTxBN" or "pair") and REELS_Q8_TS (256, 192, 128, or 0 for
-// off) force a plan for measurements.
+// REELS_Q8_TILE ("MTxBN" or "pair") and REELS_Q8_TS (256, 192, 128; 2562,
+// 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements.
 Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters, bool allow_ts) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128") or "pair"
@@ -283,26 +291,28 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
         return 0;
     }();
     static const int forced_ts = [] {
-        const char *e = getenv("REELS_Q8_TS");
-        if (!e) return -1;  // automatic
+        const char *e = getenv("REELS_Q8_TS");  // 256, 192, 128 (64-wide stages), 2562, 1922, 1282 (128-wide), 0 = off
+        if (!e) return -1;                      // automatic
         const int v = atoi(e);
-        return (v == 256 || v == 192 || v == 128) ? v : 0;
+        return (v == 256 || v == 192 || v == 128 || v == 2562 || v == 1922 || v == 1282) ? v : 0;
     }();
     struct Cand {
-        int mt, bn, ts;
-        double per_kb, epi;
+        int mt, bn, ts, kb2;
+        double per_kb, epi;  // per_kb: per pipeline stage (64 * kb2 reduction elements)
     };
     const Cand cands[] = {
-        {0, 0, 256, 0.49, 1.1}, {0, 0, 192, 0.44, 0.4}, {0, 0, 128, 0.48, 0.4},
-        {2, 256, 0, 1.18, 4.0}, {2, 128, 0, 0.85, 1.5}, {1, 256, 0, 1.0, 1.5}, {1, 128, 0, 0.75, 1.5},
+        {0, 0, 256, 1, 0.49, 1.1}, {0, 0, 192, 1, 0.44, 0.4}, {0, 0, 128, 1, 0.48, 0.4}, {0, 0, 128, 2, 0.60, 0.4},
+        {0, 0, 256, 2, 1.07, 1.1}, {0, 0, 192, 2, 1.02, 0.4},
+        {2, 256, 0, 1, 1.18, 4.0}, {2, 128, 0, 1, 0.85, 1.5}, {1, 256, 0, 1, 1.0, 1.5}, {1, 128, 0, 1, 0.75, 1.5},
     };
-    const int64_t kb = cdiv(Kred, BK);
     double best = 1e300;
     Q8Plan bestp;
     for (const Cand &cd : cands) {
+        const int64_t kb = cdiv(Kred, BK * cd.kb2);
         if (cd.ts) {
             if (!allow_ts || forced || forced_ts == 0) continue;
-            if (forced_ts > 0 && forced_ts != cd.ts) continue;
+            if (forced_ts > 0 && forced_ts != cd.ts * 10 + cd.kb2 && forced_ts != cd.ts) continue;
+            if (forced_ts > 0 && forced_ts == cd.ts && cd.kb2 != 1) continue;
         } else {
             if (forced_ts > 0) continue;
             if (forced && forced != cd.mt * 1000 + cd.bn) continue;
@@ -325,6 +335,7 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
                 bestp.mt = cd.ts ? 1 : cd.mt;
                 bestp.bn = cd.ts ? 128 : cd.bn;
                 bestp.ts = cd.ts;
+                bestp.ts_kb2 = cd.kb2;
                 bestp.ntiles = ntiles;
                 bestp.mtiles = mtiles;
                 bestp.split = sp;
@@ -336,6 +347,7 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
     // measured slower than the single-CTA 2x256 plan on every BASELINE shape
     // (about 770 vs 920-1130 TFLOP/s forward), so it runs only when forced.
     if (pair_clusters > 0 && forced == 1) {
+        const int64_t kb = cdiv(Kred, BK);
         const int64_t ntiles = cdiv(Nout, 256), mtiles = cdiv(M, 256);
         const double units = (double)cdiv(ntiles * mtiles, pair_clusters);
         const double cost = units * (kb * 0.95 * 1.18 + 1.5);
@@ -363,7 +375,9 @@ struct Ws {
     size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, part = 0, total = 0;
 };
 
-int64_t rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 64); }
+// Rank padding of the prepared LoRA operands: a multiple of the widest
+// pipeline stage (128 reduction elements).
+int64_t rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 128); }
 
 Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int sms) {
     Ws w;
@@ -596,10 +610,10 @@ void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtenso
     }
 }
 
-template <int DT, int BT>
+template <int DT, int BT, int KB2>
 void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &te,
                  const CUtensorMap &tsc, const CUtensorMap &to, const TsArgs &a) {
-    q8ts_gemm_kernel<DT, BT><<<grid, TS_THREADS, TsGeom<BT>::SMEM_BYTES, st>>>(tx, tw, te, tsc, to, a);
+    q8ts_gemm_kernel<DT, BT, KB2><<<grid, TS_THREADS, TsGeom<BT, KB2>::SMEM_BYTES, st>>>(tx, tw, te, tsc, to, a);
 }
 
 // Profiling hook shared by both q8 launch paths: events around the GEMM.
@@ -620,6 +634,7 @@ cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
 int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st,
               const Q8Plan &p) {
     const int bt = p.ts;
+    const int sk = 64 * p.ts_kb2;  // reduction elements per pipeline stage
     CUtensorMap tx, tw, te, tsc, to;
     int rc = tmap_2d(&tx, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, bt,
                      CU_TENSOR_MAP_SWIZZLE_128B);
@@ -627,13 +642,14 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     const uint64_t w_inner = c.layout == REELS_W_OUT_CONTIGUOUS ? c.N_w : c.K_w;
     const uint64_t w_outer = c.layout == REELS_W_OUT_CONTIGUOUS ? c.K_w : c.N_w;
     const bool inner_is_red = c.fwd ? (c.layout == REELS_W_IN_CONTIGUOUS) : (c.layout == REELS_W_OUT_CONTIGUOUS);
-    // Rows of output columns carry 64 reduction bytes (64B swizzle); rows of
-    // reduction indices carry 128 output-column bytes (128B swizzle).
+    // Rows of output columns carry sk reduction bytes (64B swizzle for 64,
+    // 128B for 128); rows of reduction indices carry 128 output-column bytes
+    // (128B swizzle), sk of them.
     if (inner_is_red)
-        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 64, 128,
-                     CU_TENSOR_MAP_SWIZZLE_64B);
+        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, sk, 128,
+                     sk == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
     else
-        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 128, 64,
+        rc = tmap_2d(&tw, c.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_inner, w_outer, w_inner, 128, sk,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     const int64_t ldm = ld_tokens(c.M);
@@ -648,7 +664,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     memset(&a, 0, sizeof a);
     a.M = (int)c.M;
     a.Nout = (int)c.Nout;
-    a.kb_total = (int)cdiv(c.Kred, BK);
+    a.kb_total = (int)cdiv(c.Kred, sk);
     a.kb_per_split = p.split.kb_per;
     a.splits = p.split.splits;
     a.ntiles = (int)p.ntiles;
@@ -672,7 +688,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     }
     if (a.scale_mode == 2) {
         rc = tmap_2d(&tsc, c.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, c.N_w, 1, (uint64_t)round_up(c.N_w * 4, 16),
-                     64, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+                     sk, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     } else {
         tsc = tx;
@@ -714,14 +730,20 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
     const dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
     cudaEvent_t ev_stop = prof_begin(st, c);
-    const int key = (dt == REELS_BF16 ? 1000 : 0) + bt;
+    const int key = (dt == REELS_BF16 ? 10000 : 0) + bt * 10 + p.ts_kb2;
     switch (key) {
-        case 1256: launch_ts_t<DT_BF16, 256>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 1192: launch_ts_t<DT_BF16, 192>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 1128: launch_ts_t<DT_BF16, 128>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 256: launch_ts_t<DT_F16, 256>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 192: launch_ts_t<DT_F16, 192>(grid, st, tx, tw, te, tsc, to, a); break;
-        default: launch_ts_t<DT_F16, 128>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 12561: launch_ts_t<DT_BF16, 256, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 11921: launch_ts_t<DT_BF16, 192, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 11281: launch_ts_t<DT_BF16, 128, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 11282: launch_ts_t<DT_BF16, 128, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 12562: launch_ts_t<DT_BF16, 256, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 11922: launch_ts_t<DT_BF16, 192, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 2562: launch_ts_t<DT_F16, 256, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 1922: launch_ts_t<DT_F16, 192, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 2561: launch_ts_t<DT_F16, 256, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 1921: launch_ts_t<DT_F16, 192, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 1281: launch_ts_t<DT_F16, 128, 1>(grid, st, tx, tw, te, tsc, to, a); break;
+        default: launch_ts_t<DT_F16, 128, 2>(grid, st, tx, tw, te, tsc, to, a); break;
     }
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));

@@ -41,26 +41,32 @@ constexpr int TS_GW = TS_NDW / TS_NG;  // warps per group
 constexpr int TS_NEW = 8;  // epilogue warps
 constexpr int TS_THREADS = 32 * (3 + TS_NDW + TS_NEW);
 
+// A pipeline stage covers SK = 64*KB2 reduction elements: KB2 = 1 for the
+// 256- and 192-token tiles, 2 for 128-token tiles (the MMA warp's
+// per-stage synchronisation is then spread over twice the weight bytes,
+// which is what bounds weight streaming at small token counts).
 // TMEM (512 columns): NACC accumulators of BT columns and NA A-operand stages
-// of 32 columns (64 16-bit reduction elements).  BT = 256 leaves room for one
-// accumulator only; BT <= 192 double-buffers it so the epilogue overlaps the
-// next tile's MMAs.
-template <int BT>
+// of SK/2 columns.  BT = 256 leaves room for one accumulator only; BT <= 192
+// double-buffers it so the epilogue overlaps the next tile's MMAs.
+template <int BT, int KB2>
 struct TsGeom {
+    static constexpr int SK = 64 * KB2;
     static constexpr int NACC = BT == 256 ? 1 : 2;
-    static constexpr int NA = BT == 256 ? 8 : (BT == 192 ? 4 : 8);
-    static constexpr int X_BYTES = BT * 128;  // activation tile: BT rows x 64 K, SW128
-    static constexpr int W_BYTES = 128 * 64;  // int8 tile: 128 output columns x 64 K
-    static constexpr int SC_BYTES = 256;      // 64 fp32 reduction scales
-    static constexpr int EPI_BYTES = 4096;    // per epilogue warp: two 32 x 32 16-bit staging tiles
+    static constexpr int ACOLS = SK / 2;
+    static constexpr int NA = (BT == 192 ? 4 : 8) / KB2;
+    static constexpr int X_BYTES = KB2 * BT * 128;  // activation tile: KB2 SW128 atoms of BT rows x 64 K
+    static constexpr int W_BYTES = 128 * SK;        // int8 tile: 128 output columns x SK
+    static constexpr int SC_BYTES = 4 * SK;         // SK fp32 reduction scales
+    static constexpr int EPI_BYTES = 4096;          // per epilogue warp: two 32 x 32 16-bit staging tiles
 #ifndef REELS_TS_SX
 #define REELS_TS_SX 0
 #endif
 #ifndef REELS_TS_S8
 #define REELS_TS_S8 0
 #endif
-    static constexpr int SX = REELS_TS_SX ? REELS_TS_SX : (BT == 256 ? 4 : (BT == 192 ? 4 : 6));
-    static constexpr int S8 = REELS_TS_S8 ? REELS_TS_S8 : (BT == 256 ? 6 : 8);
+    static constexpr int SX = REELS_TS_SX ? REELS_TS_SX
+                                          : (KB2 == 2 ? (BT == 128 ? 4 : 2) : (BT == 128 ? 6 : 4));
+    static constexpr int S8 = REELS_TS_S8 ? REELS_TS_S8 : (KB2 == 2 ? 3 : (BT == 256 ? 6 : 8));
     static constexpr int X_OFF = 0;
     static constexpr int W_OFF = X_OFF + SX * X_BYTES;
     static constexpr int SC_OFF = W_OFF + S8 * W_BYTES;
@@ -71,19 +77,19 @@ struct TsGeom {
     static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
     static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
-    static_assert(NACC * BT + NA * 32 <= 512, "TMEM plan exceeds 512 columns");
-    // Reduction block ga uses barrier slot ga % NA: kb_full is completed by
-    // the activation TMA and the dequant group, kb_empty by the MMA commit
-    // once the block's MMAs are done.  The activation producer reuses X slot
-    // ga % SX after block ga - SX is consumed; with SX <= NA that block's
-    // kb_empty phase cannot have been overtaken, so its parity is unambiguous.
-    static_assert(SX <= NA, "activation ring deeper than the block barrier ring");
+    static_assert(NACC * BT + NA * ACOLS <= 512, "TMEM plan exceeds 512 columns");
+    // Stage ga uses barrier slot ga % NA: kb_full is completed by the
+    // activation TMA and the dequant group, kb_empty by the MMA commit once the
+    // stage's MMAs are done.  The activation producer reuses X slot ga % SX
+    // after stage ga - SX is consumed; with SX <= NA that stage's kb_empty
+    // phase cannot have been overtaken, so its parity is unambiguous.
+    static_assert(SX <= NA, "activation ring deeper than the stage barrier ring");
 
     // Accumulator a starts at column 256 * a; A stages fill the columns left over.
     static __device__ __forceinline__ uint32_t acc_col(int a) { return 256u * a; }
     static __device__ __forceinline__ uint32_t a_col(int s) {
-        if constexpr (NACC == 1) return 256u + 32u * s;
-        else return (s < NA / 2) ? (uint32_t)BT + 32u * s : 256u + BT + 32u * (s - NA / 2);
+        if constexpr (NACC == 1) return 256u + (uint32_t)ACOLS * s;
+        else return (s < NA / 2) ? (uint32_t)BT + ACOLS * s : 256u + BT + (uint32_t)ACOLS * (s - NA / 2);
     }
 };
 
@@ -214,25 +220,24 @@ __device__ __forceinline__ void i8x4_convert(uint32_t v, const float *s, uint32_
     }
 }
 
-// One 64-wide reduction block of the weight into TMEM A stage `a_tm` (lane 0
-// address of the stage).  Warp q: lanes 32q..32q+31, all 64 reduction
-// indices.  `lane_s` are the per-lane scales of SMODE 1 (lanes 32q + 8i +
-// t/4); SMODE 2 reads the block's 64 reduction scales from `sc_base`.
-template <int DT, int ROWS_RED, int SMODE>
-__device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_base, uint32_t a_tm, int q, int lane,
-                                                 const float (&lane_s)[4]) {
+// 64 reduction indices (sub-block h2 of the stage) into TMEM columns 32*h2 .. 32*h2 + 31.
+template <int DT, int ROWS_RED, int SMODE, int SK>
+__device__ __forceinline__ void ts_dequant_sub(uint32_t w_base, uint32_t sc_base, uint32_t a_tm, int q, int lane,
+                                               const float (&lane_s)[4], int h2) {
     uint32_t raw[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {  // 16-wide reduction chunk
+    for (int jl = 0; jl < 4; ++jl) {  // 16-wide reduction chunk j = 4*h2 + jl of the stage
+        const uint32_t j = 4u * h2 + jl;
         if constexpr (ROWS_RED == 0) {
-            // rows = output columns (64 B, 64B swizzle): thread t addresses row 32q + t, chunk j
+            // rows = output columns: thread t addresses row 32q + t, 16-byte chunk j
             const uint32_t row = 32u * q + lane;
-            ldsm_x4_b16(w_base + row * 64u + ((j ^ ((row >> 1) & 3u)) << 4), raw[j]);
+            if constexpr (SK == 64) ldsm_x4_b16(w_base + row * 64u + ((j ^ ((row >> 1) & 3u)) << 4), raw[jl]);
+            else ldsm_x4_b16(w_base + row * 128u + ((j ^ (row & 7u)) << 4), raw[jl]);
         } else {
-            // rows = reduction indices (128 B, 128B swizzle): threads 0-15 chunk 2q, 16-31 chunk 2q+1
+            // rows = reduction indices (128 B): threads 0-15 chunk 2q, 16-31 chunk 2q+1
             const uint32_t row = 16u * j + (lane & 15);
             const uint32_t c = 2u * q + (lane >> 4);
-            ldsm_x2_trans_b8(w_base + row * 128u + ((c ^ (row & 7u)) << 4), raw[j]);
+            ldsm_x2_trans_b8(w_base + row * 128u + ((c ^ (row & 7u)) << 4), raw[jl]);
         }
     }
     // raw[j][i]: lanes 32q + 8i + t/4, reduction 16j + 4(t%4) .. +3
@@ -243,7 +248,7 @@ __device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_ba
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
                 const float4 s4 = *reinterpret_cast<const float4 *>(
-                    __cvta_shared_to_generic(sc_base + 4u * (16u * (2 * h + jj) + 4u * (lane & 3))));
+                    __cvta_shared_to_generic(sc_base + 4u * (64u * h2 + 16u * (2 * h + jj) + 4u * (lane & 3))));
                 rs[jj][0] = s4.x;
                 rs[jj][1] = s4.y;
                 rs[jj][2] = s4.z;
@@ -268,9 +273,25 @@ __device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_ba
                     }
                     i8x4_convert<DT, SMODE>(raw[2 * h + jj][i], sc, v[4 * jj + 2 * u], v[4 * jj + 2 * u + 1]);
                 }
-            tmem_st_16x256b_x2(a_tm + ((uint32_t)(32 * q + 16 * half) << 16) + 16u * h, v);
+            tmem_st_16x256b_x2(a_tm + ((uint32_t)(32 * q + 16 * half) << 16) + 32u * h2 + 16u * h, v);
         }
     }
+}
+
+
+// One pipeline stage (SK reduction indices) of the weight into TMEM A stage
+// `a_tm` (lane 0 address of the stage), 64 indices (sub-block h2) at a time.
+// Warp q: lanes 32q..32q+31.  `lane_s` are the per-lane scales of SMODE 1
+// (lanes 32q + 8i + t/4); SMODE 2 reads the stage's reduction scales from
+// `sc_base`.  Tiles whose rows are output columns have SK-byte rows (64B
+// swizzle for 64, 128B swizzle for 128); tiles whose rows are reduction
+// indices have 128-byte rows (128B swizzle).
+template <int DT, int ROWS_RED, int SMODE, int SK>
+__device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_base, uint32_t a_tm, int q, int lane,
+                                                 const float (&lane_s)[4]) {
+#pragma unroll
+    for (int h2 = 0; h2 < SK / 64; ++h2)
+        ts_dequant_sub<DT, ROWS_RED, SMODE, SK>(w_base, sc_base, a_tm, q, lane, lane_s, h2);
 }
 
 
@@ -280,7 +301,7 @@ struct TsTile {
 
 // Tiles run output-column tile fastest, so the CTAs in flight share one
 // activation tile through L2 while the (small) weight stays resident there.
-template <int BT>
+template <int BT, int SK>
 __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
     TsTile c;
     const int nt = t % a.ntiles;
@@ -291,16 +312,16 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
     c.m0 = mt * BT;
     c.kb0 = c.sp * a.kb_per_split;
     c.n_main = max(0, min(a.kb_total, c.kb0 + a.kb_per_split) - c.kb0);
-    c.n_ext = (c.sp == a.splits - 1 && a.r > 0) ? (a.r + 63) / 64 : 0;
+    c.n_ext = (c.sp == a.splits - 1 && a.r > 0) ? (a.r + SK - 1) / SK : 0;
     return c;
 }
 
-template <int DT, int BT>
+template <int DT, int BT, int KB2>
 __global__ void __launch_bounds__(TS_THREADS, 1)
     q8ts_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmS,
                      const __grid_constant__ CUtensorMap tmO, const TsArgs args) {
-    using G = TsGeom<BT>;
+    using G = TsGeom<BT, KB2>;
     using E = Elem<DT>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -362,7 +383,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         // ------------------------------------------------ activation producer
         uint32_t gx = 0;
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT>(args, t);
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
                 const int s = gx % G::SX;
                 if (gx >= (uint32_t)G::SX) {
@@ -376,15 +397,23 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 if (lane == 0) {
                     uint8_t *dst = smem + G::X_OFF + s * G::X_BYTES;
                     uint64_t *full = &kb_full[gx % G::NA];
-                    mbar_arrive_expect_tx(full, G::X_BYTES);
                     if (it < c.n_main) {
-                        tma_load_2d(dst, &tmX, (c.kb0 + it) * BK, c.m0, full);
-                    } else {
-                        // [64 ranks][BT tokens], tokens contiguous: BT/64 boxes of 64 x 64
-                        const int e = it - c.n_main;
+                        // KB2 K-major atoms of [BT tokens][64 K]
+                        mbar_arrive_expect_tx(full, G::X_BYTES);
 #pragma unroll
-                        for (int b = 0; b < BT / 64; ++b)
-                            tma_load_2d(dst + b * 8192, &tmE, c.m0 + 64 * b, 64 * e, full);
+                        for (int a = 0; a < KB2; ++a)
+                            tma_load_2d(dst + a * BT * 128, &tmX, (c.kb0 + it) * G::SK + 64 * a, c.m0, full);
+                    } else {
+                        // rank atoms of [64 ranks][BT tokens], tokens contiguous (BT/64 boxes of 64 x 64);
+                        // atoms wholly past r are not loaded (the MMA does not read them)
+                        const int e = it - c.n_main;
+                        const int na = min(KB2, (args.r - G::SK * e + 63) / 64);
+                        mbar_arrive_expect_tx(full, na * BT * 128);
+                        for (int a = 0; a < na; ++a)
+#pragma unroll
+                            for (int b = 0; b < BT / 64; ++b)
+                                tma_load_2d(dst + a * BT * 128 + b * 8192, &tmE, c.m0 + 64 * b,
+                                            G::SK * e + 64 * a, full);
                     }
                 }
                 __syncwarp();
@@ -395,7 +424,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         uint32_t gw = 0;
         const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT>(args, t);
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main; ++it, ++gw) {
                 const int s = gw % G::S8;
                 if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
@@ -406,10 +435,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     uint8_t *dst = smem + G::W_OFF + s * G::W_BYTES;
                     mbar_arrive_expect_tx(&w_full[s], bytes);
                     const int kb = c.kb0 + it;
-                    if (args.w_rows_red == 0) tma_load_2d(dst, &tmW, kb * BK, c.n0, &w_full[s]);
-                    else tma_load_2d(dst, &tmW, c.n0, kb * BK, &w_full[s]);
+                    if (args.w_rows_red == 0) tma_load_2d(dst, &tmW, kb * G::SK, c.n0, &w_full[s]);
+                    else tma_load_2d(dst, &tmW, c.n0, kb * G::SK, &w_full[s]);
                     if (args.scale_mode == 2)
-                        tma_load_2d(smem + G::SC_OFF + s * G::SC_BYTES, &tmS, kb * BK, 0, &w_full[s]);
+                        tma_load_2d(smem + G::SC_OFF + s * G::SC_BYTES, &tmS, kb * G::SK, 0, &w_full[s]);
                 }
                 __syncwarp();
             }
@@ -426,7 +455,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
         uint32_t ga = 0, local = 0;
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
-            const TsTile c = ts_tile<BT>(args, t);
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
             if (!wait_bar_all(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
@@ -446,17 +475,21 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 const uint32_t a_tm = tmem + G::a_col(sa);
                 const uint64_t xoff = (uint64_t)((sx * G::X_BYTES) >> 4);
                 if (lane == 0) {
+                    // K step kk reads atom kk/4 of the stage (BT*128 bytes each):
+                    // 32 bytes per step inside a K-major atom, 2048 inside a rank atom.
                     if (it < c.n_main) {
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; ++kk)
-                            mma_f16_ts(d_tm, a_tm + 8 * kk, dmain0 + xoff + (uint64_t)(kk * 2), id_main,
-                                       (it > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < 4 * KB2; ++kk)
+                            mma_f16_ts(d_tm, a_tm + 8 * kk,
+                                       dmain0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 32) >> 4),
+                                       id_main, (it > 0 || kk > 0) ? 1u : 0u);
                     } else {
                         const int e = it - c.n_main;
-                        const int nk = (min(64, args.r - 64 * e) + 15) / 16;
+                        const int nk = (min(G::SK, args.r - G::SK * e) + 15) / 16;
                         for (int kk = 0; kk < nk; ++kk)
-                            mma_f16_ts(d_tm, a_tm + 8 * kk, dext0 + xoff + (uint64_t)(kk * 128), id_ext,
-                                       (it > 0 || kk > 0) ? 1u : 0u);
+                            mma_f16_ts(d_tm, a_tm + 8 * kk,
+                                       dext0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 2048) >> 4),
+                                       id_ext, (it > 0 || kk > 0) ? 1u : 0u);
                     }
                 }
                 __syncwarp();
@@ -483,7 +516,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int g = (warp - 3) / TS_GW;     // group: reduction blocks with ga % TS_NG == g
         uint32_t ga = 0, gw = 0;
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT>(args, t);
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             // Per-lane scales (lanes 32q + 8i + t/4) for SMODE 1.
             float lane_s[4] = {0.f, 0.f, 0.f, 0.f};
             if (args.scale_mode == 1) {
@@ -516,12 +549,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     const uint32_t w_base = sbase + G::W_OFF + sw * G::W_BYTES;
                     const uint32_t sc_base = sbase + G::SC_OFF + sw * G::SC_BYTES;
                     switch (args.w_rows_red * 3 + args.scale_mode) {
-                        case 0: ts_dequant_block<DT, 0, 0>(w_base, sc_base, a_tm, q, lane, lane_s); break;
-                        case 1: ts_dequant_block<DT, 0, 1>(w_base, sc_base, a_tm, q, lane, lane_s); break;
-                        case 2: ts_dequant_block<DT, 0, 2>(w_base, sc_base, a_tm, q, lane, lane_s); break;
-                        case 3: ts_dequant_block<DT, 1, 0>(w_base, sc_base, a_tm, q, lane, lane_s); break;
-                        case 4: ts_dequant_block<DT, 1, 1>(w_base, sc_base, a_tm, q, lane, lane_s); break;
-                        default: ts_dequant_block<DT, 1, 2>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 0: ts_dequant_block<DT, 0, 0, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 1: ts_dequant_block<DT, 0, 1, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 2: ts_dequant_block<DT, 0, 2, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 3: ts_dequant_block<DT, 1, 0, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        case 4: ts_dequant_block<DT, 1, 1, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
+                        default: ts_dequant_block<DT, 1, 2, G::SK>(w_base, sc_base, a_tm, q, lane, lane_s); break;
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&w_empty[sw]);
@@ -531,7 +564,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     const int e = it - c.n_main;
                     const uint16_t *src = reinterpret_cast<const uint16_t *>(args.ext_w);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h)
+                    for (int h = 0; h < 2 * KB2; ++h)
 #pragma unroll
                         for (int half = 0; half < 2; ++half) {
                             uint32_t v[8];
@@ -540,7 +573,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 #pragma unroll
                                 for (int u = 0; u < 2; ++u) {
                                     const int n = c.n0 + 32 * q + 16 * half + 8 * u + (lane >> 2);
-                                    const int k = 64 * e + 16 * (2 * h + jj) + 4 * (lane & 3);
+                                    const int k = G::SK * e + 16 * (2 * h + jj) + 4 * (lane & 3);
                                     uint2 w = make_uint2(0, 0);
                                     if (n < args.Nout)
                                         w = __ldg(
@@ -573,7 +606,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         int buf = 0;
         uint32_t local = 0;
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
-            const TsTile c = ts_tile<BT>(args, t);
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
             if (!wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
