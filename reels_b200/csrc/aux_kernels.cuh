@@ -112,7 +112,8 @@ __global__ void materialize_kernel(const int8_t *__restrict__ q, const float *__
 }
 
 // A [K][r] -> At [r][K] (same element type, 2 bytes).  K * r < 2^31.
-__global__ void transpose_rank_kernel(const uint16_t *__restrict__ a, int K, int r, uint16_t *__restrict__ at) {
+__global__ void transpose_rank_kernel(const uint16_t *a, int K, int r, uint16_t *__restrict__ at) {
+    griddep_wait();
     const int total = K * r;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
         const int j = i / K, k = i - j * K;
@@ -125,17 +126,18 @@ __global__ void transpose_rank_kernel(const uint16_t *__restrict__ a, int K, int
 // consecutive columns per thread (Nout is a multiple of 16 on the tensor-core
 // path), 16-byte loads, the split loop unrolled so its loads are in flight
 // together; the sum runs over s = 0 .. splits-1 in order.
-__global__ void q8_reduce_kernel(const float *__restrict__ partial, int splits, int64_t M, int64_t Nout,
-                                 const float *__restrict__ col_scale, const void *bias, int dt, void *out,
+__global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, int64_t Nout,
+                                 const float *col_scale, const void *bias, int dt, void *out,
                                  int64_t ldo) {
+    griddep_wait();
     const int64_t total4 = M * Nout / 4;
     const float4 *p4 = reinterpret_cast<const float4 *>(partial);
     for (int64_t i4 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i4 < total4;
          i4 += (int64_t)gridDim.x * blockDim.x) {
-        float4 acc = __ldg(p4 + i4);
+        float4 acc = __ldcg(p4 + i4);
 #pragma unroll 4
         for (int s = 1; s < splits; ++s) {
-            const float4 v = __ldg(p4 + (int64_t)s * total4 + i4);
+            const float4 v = __ldcg(p4 + (int64_t)s * total4 + i4);
             acc.x += v.x;
             acc.y += v.y;
             acc.z += v.z;
@@ -158,9 +160,10 @@ __global__ void q8_reduce_kernel(const float *__restrict__ partial, int splits, 
 // threads share an output, thread t of the four adds the splits s = t mod 4
 // in order with eight loads in flight, and the four partial sums are
 // combined in a fixed order (deterministic from run to run).
-__global__ void sk_reduce_kernel(const float *__restrict__ partial, int splits, int64_t rows, int npad, int ncols,
+__global__ void sk_reduce_kernel(const float *partial, int splits, int64_t rows, int npad, int ncols,
                                  int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
                                  int64_t cs) {
+    griddep_wait();
     const int64_t total = rows * (int64_t)ncols;
     const int lane = threadIdx.x & 31, sl = lane & 3;
     const int64_t stride = rows * (int64_t)npad;
@@ -177,11 +180,11 @@ __global__ void sk_reduce_kernel(const float *__restrict__ partial, int splits, 
             for (; s + 28 < splits; s += 32) {
                 float v[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldg(p + (int64_t)(s + 4 * u) * stride);
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (int64_t)(s + 4 * u) * stride);
 #pragma unroll
                 for (int u = 0; u < 8; ++u) acc += v[u];
             }
-            for (; s < splits; s += 4) acc += __ldg(p + (int64_t)s * stride);
+            for (; s < splits; s += 4) acc += __ldcg(p + (int64_t)s * stride);
         }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);

@@ -336,6 +336,17 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask
         : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization is queued early; griddep_wait() blocks until the previous
+// kernel in the stream has completed and its memory is visible, so every such
+// kernel calls it before its first global-memory access (read or write).
+// The kernels do not signal griddepcontrol.launch_dependents: with that early
+// trigger the dX GEMM on 128x192 tiles produced wrong results on B200 (parity
+// tests), a failure that waiting alone does not show and whose cause is not
+// established.  Data written by an earlier kernel is read through L2
+// (__ldcg), not through the SM's L1 or the read-only path.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 32-byte global stores (sm_100): one instruction per 16 bf16/fp16 or 8 fp32.
 __device__ __forceinline__ void st_global_v8(void *p, uint4 a, uint4 b) {
     asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w),

@@ -68,6 +68,29 @@ int ok(int path) {
         if (e_ != cudaSuccess) return fail_dev(std::string(#call) + ": " + cudaGetErrorString(e_));    \
     } while (0)
 
+// Launch with programmatic stream serialization (see griddep_wait in
+// common.cuh): the launch is queued ahead of the previous kernel's completion
+// and every kernel launched this way waits for that kernel before touching
+// global memory.  REELS_NO_PDL=1 launches everything in plain stream order.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    static const bool pdl = [] {
+        const char *e = getenv("REELS_NO_PDL");
+        return !(e && atoi(e) != 0);
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ------------------------------------------------------------ device state
 constexpr int kMaxDevices = 64;
 struct DeviceState {
@@ -487,11 +510,11 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.err = ds.status;
     a.epi = s.splits > 1 ? 2 : c.epi_final;
     dim3 grid((unsigned)cdiv(c.rows, 128), (unsigned)s.splits);
-    if (dt == REELS_BF16) sk_gemm_kernel<DT_BF16><<<grid, SK_THREADS, SK_SMEM_BYTES, st>>>(ta, tb, a);
-    else sk_gemm_kernel<DT_F16><<<grid, SK_THREADS, SK_SMEM_BYTES, st>>>(ta, tb, a);
+    if (dt == REELS_BF16) launch_pdl(sk_gemm_kernel<DT_BF16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
+    else launch_pdl(sk_gemm_kernel<DT_F16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     REELS_LAUNCHED();
     if (s.splits > 1) {
-        sk_reduce_kernel<<<launch_grid(c.rows * c.r * 4), 256, 0, st>>>(a.partial, s.splits, c.rows, np, (int)c.r,
+        launch_pdl(sk_reduce_kernel, dim3(launch_grid(c.rows * c.r * 4)), dim3(256), 0, st, a.partial, s.splits, c.rows, np, (int)c.r,
                                                                     c.epi_final, c.alpha, c.accumulate, dt, c.out,
                                                                     c.ldo, c.rs, c.cs);
         REELS_LAUNCHED();
@@ -506,8 +529,9 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
 //                     column scale is applied in the epilogue), [rp][N]
 //                     dX       E[k][j] = A[k][j],                  [K][rp]
 template <typename T>
-__global__ void prep_ext_fwd_kernel(const T *__restrict__ B, const float *__restrict__ scales, float s, int divide,
+__global__ void prep_ext_fwd_kernel(const T *B, const float *scales, float s, int divide,
                                     int64_t r, int64_t rp, int64_t N, T *__restrict__ out) {
+    griddep_wait();
     const int64_t total = rp * N;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -526,8 +550,9 @@ __global__ void prep_ext_fwd_kernel(const T *__restrict__ B, const float *__rest
 // 32 columns x rp ranks through shared memory: B rows are read along n and E
 // rows written along j, both coalesced.
 template <typename T>
-__global__ void prep_ext_fwd_rows_kernel(const T *__restrict__ B, const float *__restrict__ scales, float s,
+__global__ void prep_ext_fwd_rows_kernel(const T *B, const float *scales, float s,
                                          int divide, int r, int rp, int N, T *__restrict__ out) {
+    griddep_wait();
     __shared__ float tile[128][33];
     const int n0 = blockIdx.x * 32;
     for (int jb = 0; jb < rp; jb += 128) {
@@ -555,7 +580,8 @@ __global__ void prep_ext_fwd_rows_kernel(const T *__restrict__ B, const float *_
 
 // dX LoRA operand E[k][j] = A[k][j] (j < r), zero-padded to rp columns.
 // Eight columns per thread, one 16-byte store.
-__global__ void prep_ext_dx_kernel(const uint16_t *__restrict__ A, int K, int r, int rp, uint16_t *__restrict__ out) {
+__global__ void prep_ext_dx_kernel(const uint16_t *A, int K, int r, int rp, uint16_t *__restrict__ out) {
+    griddep_wait();
     const int per_row = rp / 8;
     const int total = K * per_row;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
@@ -592,7 +618,7 @@ struct Q8Call {
 template <int DT, int MT, int BN>
 void launch_q8_t(dim3 grid, cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tw, const CUtensorMap &te,
                  const Q8Args &a) {
-    q8_gemm_kernel<DT, MT, BN><<<grid, Q8_THREADS, Q8Geom<MT, BN>::SMEM_BYTES, st>>>(ta, tw, te, a);
+    launch_pdl(q8_gemm_kernel<DT, MT, BN>, dim3(grid), dim3(Q8_THREADS), Q8Geom<MT, BN>::SMEM_BYTES, st, ta, tw, te, a);
 }
 
 void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtensorMap &ta, const CUtensorMap &tw,
@@ -613,7 +639,7 @@ void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtenso
 template <int DT, int BT, int KB2>
 void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &te,
                  const CUtensorMap &tsc, const CUtensorMap &to, const TsArgs &a) {
-    q8ts_gemm_kernel<DT, BT, KB2><<<grid, TS_THREADS, TsGeom<BT, KB2>::SMEM_BYTES, st>>>(tx, tw, te, tsc, to, a);
+    launch_pdl(q8ts_gemm_kernel<DT, BT, KB2>, dim3(grid), dim3(TS_THREADS), TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, a);
 }
 
 // Profiling hook shared by both q8 launch paths: events around the GEMM.
@@ -700,15 +726,15 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
         a.ext_ld = (int)rp;
         if (c.fwd) {
             if (dt == REELS_BF16)
-                prep_ext_fwd_rows_kernel<__nv_bfloat16><<<(unsigned)cdiv(c.Nout, 32), 256, 0, st>>>(
+                launch_pdl(prep_ext_fwd_rows_kernel<__nv_bfloat16>, dim3((unsigned)cdiv(c.Nout, 32)), dim3(256), 0, st, 
                     (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, (int)c.r, (int)rp,
                     (int)c.Nout, (__nv_bfloat16 *)c.ext_buf);
             else
-                prep_ext_fwd_rows_kernel<__half><<<(unsigned)cdiv(c.Nout, 32), 256, 0, st>>>(
+                launch_pdl(prep_ext_fwd_rows_kernel<__half>, dim3((unsigned)cdiv(c.Nout, 32)), dim3(256), 0, st, 
                     (const __half *)c.lora, c.scales, c.ext_scale, 0, (int)c.r, (int)rp, (int)c.Nout,
                     (__half *)c.ext_buf);
         } else {
-            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp / 8), 256, 0, st>>>(
+            launch_pdl(prep_ext_dx_kernel, dim3(launch_grid(c.Nout * rp / 8)), dim3(256), 0, st, 
                 (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
         }
         REELS_LAUNCHED();
@@ -748,7 +774,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
-        q8_reduce_kernel<<<launch_grid(c.M * c.Nout / 4), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+        launch_pdl(q8_reduce_kernel, dim3(launch_grid(c.M * c.Nout / 4)), dim3(256), 0, st, a.partial, p.split.splits, c.M, c.Nout,
                                                                     a.col_scale, c.bias, dt, c.out, c.Nout);
         REELS_LAUNCHED();
     }
@@ -826,15 +852,15 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
         if (c.fwd) {
             a.ext_ld = (int)c.Nout;
             if (dt == REELS_BF16)
-                prep_ext_fwd_kernel<__nv_bfloat16><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                launch_pdl(prep_ext_fwd_kernel<__nv_bfloat16>, dim3(launch_grid(rp * c.Nout)), dim3(256), 0, st, 
                     (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, c.r, rp, c.Nout,
                     (__nv_bfloat16 *)c.ext_buf);
             else
-                prep_ext_fwd_kernel<__half><<<launch_grid(rp * c.Nout), 256, 0, st>>>(
+                launch_pdl(prep_ext_fwd_kernel<__half>, dim3(launch_grid(rp * c.Nout)), dim3(256), 0, st, 
                     (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
         } else {
             a.ext_ld = (int)rp;
-            prep_ext_dx_kernel<<<launch_grid(c.Nout * rp / 8), 256, 0, st>>>(
+            launch_pdl(prep_ext_dx_kernel, dim3(launch_grid(c.Nout * rp / 8)), dim3(256), 0, st, 
                 (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
         }
         REELS_LAUNCHED();
@@ -861,7 +887,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
-        q8_reduce_kernel<<<launch_grid(c.M * c.Nout / 4), 256, 0, st>>>(a.partial, p.split.splits, c.M, c.Nout,
+        launch_pdl(q8_reduce_kernel, dim3(launch_grid(c.M * c.Nout / 4)), dim3(256), 0, st, a.partial, p.split.splits, c.M, c.Nout,
                                                                     a.col_scale, c.bias, dt, c.out, c.Nout);
         REELS_LAUNCHED();
     }
@@ -888,7 +914,7 @@ int check_ws(void *ws, size_t ws_bytes, const Ws &wl) {
 
 // A [K][r] -> At [r][K]
 int transpose_rank(const void *A, int64_t K, int64_t r, void *At, cudaStream_t st) {
-    transpose_rank_kernel<<<launch_grid(K * r), 256, 0, st>>>(reinterpret_cast<const uint16_t *>(A), (int)K, (int)r,
+    launch_pdl(transpose_rank_kernel, dim3(launch_grid(K * r)), dim3(256), 0, st, reinterpret_cast<const uint16_t *>(A), (int)K, (int)r,
                                                               reinterpret_cast<uint16_t *>(At));
     REELS_LAUNCHED();
     return REELS_OK;

@@ -145,7 +145,7 @@ __device__ __forceinline__ void epilogue_store16(const Q8Args &args, const uint3
         const float4 *cs = reinterpret_cast<const float4 *>(args.col_scale + col);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float4 s4 = __ldg(cs + u);
+            const float4 s4 = cs[u];
             f[4 * u] *= s4.x;
             f[4 * u + 1] *= s4.y;
             f[4 * u + 2] *= s4.z;
@@ -187,7 +187,7 @@ __device__ __forceinline__ void epilogue_store16(const Q8Args &args, const uint3
 //   the staging coordinate in the weight (row y0 + row, column x0 + col).
 template <int DT, int BN, int ORIENT, int SMODE>
 __device__ __forceinline__ void dequant_stage(uint32_t w_base, uint32_t b_base, int ct, int x0, int y0,
-                                              const float *__restrict__ wscale, int wlen) {
+                                              const float *wscale, int wlen) {
     constexpr int CPT = BN * 8 / Q8_NDT;
     constexpr int BATCH = CPT < 4 ? CPT : 4;
     static_assert(CPT % BATCH == 0, "dequant chunks per thread must split into equal batches");
@@ -197,7 +197,7 @@ __device__ __forceinline__ void dequant_stage(uint32_t w_base, uint32_t b_base, 
     if constexpr (SMODE == 2) {
         const int gi = x0 + c8 * 8;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) cs[q] = (gi + q) < wlen ? __ldg(wscale + gi + q) : 0.0f;
+        for (int q = 0; q < 8; ++q) cs[q] = (gi + q) < wlen ? wscale[gi + q] : 0.0f;
     }
     // Batches of four chunks: four loads in flight, then convert and store.
 #pragma unroll
@@ -210,7 +210,7 @@ __device__ __forceinline__ void dequant_stage(uint32_t w_base, uint32_t b_base, 
 #pragma unroll
             for (int j = 0; j < BATCH; ++j) {
                 const int row = (ct + Q8_NDT * (jb + j)) / RC;
-                rs[j] = (y0 + row) < wlen ? __ldg(wscale + y0 + row) : 0.0f;
+                rs[j] = (y0 + row) < wlen ? wscale[y0 + row] : 0.0f;
             }
         }
 #pragma unroll
@@ -290,6 +290,7 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
 
     if (warp == 0) {
@@ -446,13 +447,13 @@ __global__ void __launch_bounds__(Q8_THREADS, 1)
                             const int n = c.n0 + cc * 8;
                             dst = b_base + (cc >> 3) * 8192 + sw128_off(jr, cc & 7);
                             if (n < args.Nout)
-                                o = __ldg(reinterpret_cast<const uint4 *>(src + (long long)(64 * e + jr) * args.ext_ld + n));
+                                o = __ldcg(reinterpret_cast<const uint4 *>(src + (long long)(64 * e + jr) * args.ext_ld + n));
                         } else {
                             const int row = i >> 3, cc = i & 7;
                             const int k = c.n0 + row;
                             dst = b_base + sw128_off(row, cc);
                             if (k < args.Nout)
-                                o = __ldg(reinterpret_cast<const uint4 *>(src + (long long)k * args.ext_ld + 64 * e + cc * 8));
+                                o = __ldcg(reinterpret_cast<const uint4 *>(src + (long long)k * args.ext_ld + 64 * e + cc * 8));
                         }
                         st_shared_v4(dst, o);
                     }

@@ -278,13 +278,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Q8_THREADS, 1)
                             const int n = ncol + cc * 8;
                             dst = b_base + (cc >> 3) * 8192 + sw128_off(jr, cc & 7);
                             if (n < args.Nout)
-                                o = __ldg(reinterpret_cast<const uint4 *>(src + (long long)(64 * e + jr) * args.ext_ld + n));
+                                o = __ldcg(reinterpret_cast<const uint4 *>(src + (long long)(64 * e + jr) * args.ext_ld + n));
                         } else {
                             const int row = i >> 3, cc = i & 7;
                             const int k = ncol + row;
                             dst = b_base + sw128_off(row, cc);
                             if (k < args.Nout)
-                                o = __ldg(reinterpret_cast<const uint4 *>(src + (long long)k * args.ext_ld + 64 * e + cc * 8));
+                                o = __ldcg(reinterpret_cast<const uint4 *>(src + (long long)k * args.ext_ld + 64 * e + cc * 8));
                         }
                         st_shared_v4(dst, o);
                     }

@@ -375,6 +375,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
 
     // Producer and MMA warps run converged; one lane issues the TMA copies,
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int n = c.n0 + 32 * q + 8 * i + (lane >> 2);
-                    lane_s[i] = n < args.wscale_len ? __ldg(args.wscale + n) : 0.0f;
+                    lane_s[i] = n < args.wscale_len ? args.wscale[n] : 0.0f;
                 }
             }
             const int n_iter = c.n_main + c.n_ext;
@@ -576,8 +577,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                                     const int k = G::SK * e + 16 * (2 * h + jj) + 4 * (lane & 3);
                                     uint2 w = make_uint2(0, 0);
                                     if (n < args.Nout)
-                                        w = __ldg(
-                                            reinterpret_cast<const uint2 *>(src + (long long)n * args.ext_ld + k));
+                                        w = __ldcg(reinterpret_cast<const uint2 *>(src + (long long)n * args.ext_ld + k));
                                     v[4 * jj + 2 * u] = w.x;
                                     v[4 * jj + 2 * u + 1] = w.y;
                                 }
@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     cs[hh][k] = 1.0f;
                     bs[hh][k] = 0.0f;
                     if (n < args.Nout) {
-                        if (args.col_scale) cs[hh][k] = __ldg(args.col_scale + n);
+                        if (args.col_scale) cs[hh][k] = args.col_scale[n];
                         if (args.bias) bs[hh][k] = E::to_f(reinterpret_cast<const typename E::T *>(args.bias)[n]);
                     }
                 }

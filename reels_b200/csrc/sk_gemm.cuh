@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
 
     if (warp == 0) {
