@@ -62,6 +62,11 @@ extern "C" {
 #define REELS_PASS_BACKWARD 1
 
 /* execution paths reported by reels_lowvram_last_path() */
+/* Activation fused into a linear's output (forward) or its input's gradient
+ * (backward). */
+#define REELS_ACT_NONE 0
+#define REELS_ACT_GELU_TANH 1 /* gelu_tanh, src/layers/linear.jl:61-68 */
+
 #define REELS_PATH_NONE 0
 #define REELS_PATH_TENSORCORE 1
 #define REELS_PATH_CUDACORE 2
@@ -178,6 +183,37 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
                           const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N, int64_t r,
                           float alpha, float grad_scale, int act_dtype, void *dx, float *dA, float *dB,
                           int accumulate, void *workspace, size_t ws_bytes, void *stream);
+
+/* A LoRA linear followed by an activation, the feed-forward input projection
+ * and its gelu_tanh of src/models/wan21/transformer.jl:289-291 (likewise
+ * ltx23/transformer.jl:308-310):
+ *   pre = round(lora_forward(x))         the linear's output ("hidden")
+ *   y   = round(act(float(pre)))         gelu_tanh, src/layers/linear.jl:61-68
+ * computed in one pass over the output tile.  `pre` (nullable, [M][N], the
+ * same element type) receives the linear's output, which the backward of
+ * the next linear needs (reels_q8lora_backward_act); inference passes NULL.
+ * act == REELS_ACT_NONE is reels_q8lora_forward.  Other arguments, results
+ * and the workspace are those of reels_q8lora_forward. */
+int reels_q8lora_forward_act(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                             const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                             float alpha, int act_dtype, int act, void *y, void *pre, void *saved, void *workspace,
+                             size_t ws_bytes, void *stream);
+
+/* reels_q8lora_backward for a linear whose input is an activation's output,
+ * x = act(pre_x) (the feed-forward output projection applied to
+ * gelu_tanh(hidden), transformer.jl:291): `dx` receives the gradient with
+ * respect to pre_x, the chain rule through the activation fused into the dx
+ * epilogue:
+ *   dx = round(round(dequant(q)' * dy + s * A' * g) * act'(float(pre_x)))
+ * which is Zygote's pullback of gelu_tanh (its derivative formed in fp32 and
+ * the gradient cast back to the element type).  dA and dB use `x` (the
+ * activation's output) as in reels_q8lora_backward.  pre_x [M][K] is required
+ * when dx is given. */
+int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                              const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
+                              int64_t r, float alpha, float grad_scale, int act_dtype, int act, const void *pre_x,
+                              void *dx, float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
+                              void *stream);
 
 #ifdef __cplusplus
 }

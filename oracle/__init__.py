@@ -8,8 +8,9 @@ Two restatements of the reference arithmetic live here:
 
 * ``reels_oracle.c`` (wrapped below): bit-exact quantiser
   (src/layers/quantization.jl:35-44), fp32/fp16/bf16 materialisation
-  (quantization.jl:54-64, src/models/interface.jl:13-25), and the forward /
-  backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation: the gold
+  (quantization.jl:54-64, src/models/interface.jl:13-25), the forward /
+  backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation, and
+  gelu_tanh with its derivative (src/layers/linear.jl:61-68): the gold
   standard the CUDA results are compared against.
 * ``numpy_port.py``: the reference CPU code path in fp32 through OpenBLAS
   (what Julia's LinearAlgebra calls), used as the timed CPU baseline.
@@ -55,6 +56,8 @@ def lib():
                                           _i64, _i64, _i64, _i64, ctypes.c_float, _f32p, vp]
         L.oracle_lora_backward.argtypes = [_f32p, _f32p, _i8p, _f32p, ctypes.c_int, _f32p, _f32p,
                                            _i64, _i64, _i64, _i64, ctypes.c_float, vp, vp, vp]
+        L.oracle_gelu_tanh.argtypes = [_f32p, _i64, _f32p]
+        L.oracle_gelu_tanh_grad.argtypes = [_f32p, _i64, _f32p]
         L.oracle_rel_l2.argtypes = [_f32p, _f32p, _i64]
         L.oracle_rel_l2.restype = ctypes.c_double
         _LIB = L
@@ -173,6 +176,22 @@ def lora_backward(X, dY, q, scales, layout, A, B, alpha):
     lib().oracle_lora_backward(X, dY, q, scales, layout, A, B, M, K, N, r, float(alpha),
                                dX.ctypes.data, dA.ctypes.data, dB.ctypes.data)
     return dX, dA, dB
+
+
+def gelu_tanh(h):
+    """gelu_tanh (src/layers/linear.jl:61-68) in fp32, elementwise."""
+    h = _c(h, np.float32)
+    out = np.empty_like(h)
+    lib().oracle_gelu_tanh(h.ravel(), h.size, out.ravel())
+    return out
+
+
+def gelu_tanh_grad(h):
+    """d gelu_tanh / dh in fp32, elementwise (the pullback's factor)."""
+    h = _c(h, np.float32)
+    out = np.empty_like(h)
+    lib().oracle_gelu_tanh_grad(h.ravel(), h.size, out.ravel())
+    return out
 
 
 def rel_l2(a, b) -> float:

@@ -228,6 +228,38 @@ void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, cons
     free(G);
 }
 
+/* gelu_tanh of src/layers/linear.jl:61-68, elementwise in fp32 as written
+ * there: cubic = x^3 (Julia's literal power, (x*x)*x), inner = x +
+ * 0.044715f*cubic, y = 0.5f*x*(1 + tanh(sqrt(Float32(2/pi))*inner)).  The
+ * caller rounds the input from and the output to the element type. */
+#define GELU_K0 0.7978845238685608f /* sqrt(Float32(2/pi)) rounded to fp32 */
+#define GELU_K1 0.044715f
+void oracle_gelu_tanh(const float *x, int64_t n, float *out)
+{
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = x[i];
+        const float cubic = (v * v) * v;
+        const float inner = v + GELU_K1 * cubic;
+        const float t = tanhf(GELU_K0 * inner);
+        out[i] = (0.5f * v) * (1.0f + t);
+    }
+}
+
+/* The derivative of gelu_tanh, the factor the pullback multiplies the
+ * incoming gradient by (chain rule through linear.jl:63-66, fp32):
+ *   0.5*(1 + t) + 0.5*x*(1 - t^2)*K0*(1 + 3*K1*x^2),  t = tanh(K0*inner). */
+void oracle_gelu_tanh_grad(const float *x, int64_t n, float *out)
+{
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = x[i];
+        const float x2 = v * v;
+        const float inner = v + GELU_K1 * (x2 * v);
+        const float t = tanhf(GELU_K0 * inner);
+        const float dinner = GELU_K0 * (1.0f + 3.0f * GELU_K1 * x2);
+        out[i] = 0.5f * (1.0f + t) + (0.5f * v) * (1.0f - t * t) * dinner;
+    }
+}
+
 /* Relative L2 error ||a - b|| / ||b|| in fp64 (the north-star metric). */
 double oracle_rel_l2(const float *a, const float *b, int64_t n)
 {

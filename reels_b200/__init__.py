@@ -7,6 +7,7 @@ package is the Python-side mirror of the reference's layer API
 """
 from .lowvram import (  # noqa: F401
     DenseLayer,
+    GeluFeedForwardFunction,
     LoRALinear,
     LoRALinearFunction,
     QuantizedMatrix,
@@ -14,6 +15,7 @@ from .lowvram import (  # noqa: F401
     linear,
     lora_backward,
     lora_forward,
+    lora_forward_gelu,
     materialize_weight,
     merged_weight,
     quantize_frozen_matrix,

@@ -18,6 +18,7 @@ F32, F16, BF16 = 0, 1, 2
 W_OUT_CONTIGUOUS, W_IN_CONTIGUOUS = 0, 1
 PASS_FORWARD, PASS_BACKWARD = 0, 1
 PATH_NONE, PATH_TENSORCORE, PATH_CUDACORE = 0, 1, 2
+ACT_NONE, ACT_GELU_TANH = 0, 1
 OK, EINVAL, EDEVICE = 0, -1, -2
 
 # Every symbol the header declares, with (restype, argtypes).
@@ -46,6 +47,10 @@ SIGNATURES = {
                                      _int, _vp, _vp, _vp, _int, _vp, _sz, _vp]),
     "reels_q8lora_forward_static_ws": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f,
                                               _int, _vp, _vp, _vp]),
+    "reels_q8lora_forward_act": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _int,
+                                        _int, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "reels_q8lora_backward_act": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _f,
+                                         _int, _int, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp]),
 }
 
 _lock = threading.Lock()

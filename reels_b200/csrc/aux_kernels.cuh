@@ -3,6 +3,7 @@
 // CUDA-core "generic" path that serves shapes and dtypes the tensor-core
 // path does not take (ragged feature sizes, fp32 activations).
 #pragma once
+#include "act.cuh"
 #include "common.cuh"
 
 namespace reels {
@@ -122,13 +123,30 @@ __global__ void transpose_rank_kernel(const uint16_t *a, int K, int r, uint16_t 
 }
 
 // -------------------------------------------------- split-K reductions
+// The output epilogue of one element: value v (column scale and bias applied),
+// optionally through gelu_tanh (writing the rounded pre-activation) or its
+// derivative (reading it); see act.cuh.
+__device__ __forceinline__ void epilogue_value(float v, int act, int dt, void *out, void *pre, int64_t idx) {
+    if (act == ACT_GELU_TANH) {
+        store_act(out, idx, dt, v);
+        const float h = load_act(out, idx, dt);  // the rounded pre-activation
+        if (pre) store_act(pre, idx, dt, h);
+        store_act(out, idx, dt, gelu_tanh_f32(h));
+    } else if (act == ACT_GELU_TANH_GRAD) {
+        store_act(out, idx, dt, v);
+        store_act(out, idx, dt, load_act(out, idx, dt) * gelu_tanh_grad_f32(load_act(pre, idx, dt)));
+    } else {
+        store_act(out, idx, dt, v);
+    }
+}
+
 // Sum q8 partials [splits][M][Nout] and apply the output epilogue.  Four
 // consecutive columns per thread (Nout is a multiple of 16 on the tensor-core
 // path), 16-byte loads, the split loop unrolled so its loads are in flight
 // together; the sum runs over s = 0 .. splits-1 in order.
 __global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, int64_t Nout,
                                  const float *col_scale, const void *bias, int dt, void *out,
-                                 int64_t ldo) {
+                                 int64_t ldo, int act, void *pre) {
     griddep_wait();
     const int64_t total4 = M * Nout / 4;
     const float4 *p4 = reinterpret_cast<const float4 *>(partial);
@@ -149,7 +167,7 @@ __global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, in
         for (int u = 0; u < 4; ++u) {
             if (col_scale) a[u] *= col_scale[col + u];
             if (bias) a[u] += load_act(bias, col + u, dt);
-            store_act(out, row * ldo + col + u, dt, a[u]);
+            epilogue_value(a[u], act, dt, out, pre, row * ldo + col + u);
         }
     }
 }
@@ -197,6 +215,19 @@ __global__ void sk_reduce_kernel(const float *partial, int splits, int64_t rows,
                 o32[idx] = (accumulate ? o32[idx] : 0.0f) + alpha * acc;
             }
         }
+    }
+}
+
+// The fused activation as a separate pass, for the kernels without it in
+// their epilogue: gelu reads the GEMM output from `pre` and writes `out`;
+// the gradient rescales `out` in place by gelu'(pre).
+__global__ void act_apply_kernel(int act, int dt, int64_t total, void *out, const void *pre) {
+    griddep_wait();
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float h = load_act(pre, i, dt);
+        if (act == ACT_GELU_TANH) store_act(out, i, dt, gelu_tanh_f32(h));
+        else store_act(out, i, dt, load_act(out, i, dt) * gelu_tanh_grad_f32(h));
     }
 }
 

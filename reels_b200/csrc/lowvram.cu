@@ -124,8 +124,14 @@ cudaError_t set_q8_attrs() {
 
 template <int DT, int BT, int KB2>
 cudaError_t set_ts_attr() {
-    return cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                TsGeom<BT, KB2>::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, TsGeom<BT, KB2>::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             TsGeom<BT, KB2>::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, TsGeom<BT, KB2>::SMEM_BYTES);
 }
 template <int DT>
 cudaError_t set_ts_attrs() {
@@ -304,7 +310,7 @@ struct Q8Plan {
 // split reduction adds the write and re-read of fp32 partials (~5 TB/s).
 // REELS_Q8_TILE ("MTxBN" or "pair") and REELS_Q8_TS (256, 192, 128; 2562,
 // 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements.
-Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters, bool allow_ts) {
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters, bool allow_ts, int act) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128") or "pair"
         if (!e) return 0;
@@ -350,7 +356,10 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
             sp.splits = (int)cdiv(kb, sp.kb_per);
             if (want > 1 && sp.splits == 1) continue;
             const double units = (double)cdiv(tiles * sp.splits, sms);
-            double cost = units * (sp.kb_per * cd.per_kb + cd.epi);
+            // A fused activation lengthens the epilogue; with one accumulator
+            // (256-token tiles) the MMAs wait for it.
+            const double act_epi = act == ACT_NONE || sp.splits > 1 ? 0.0 : (cd.ts == 256 ? 1.5 : 0.1);
+            double cost = units * (sp.kb_per * cd.per_kb + cd.epi + act_epi);
             if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
             if (cost < best * 0.999) {
                 best = cost;
@@ -423,11 +432,13 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
         if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
     };
     auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
-        // the pair plan never splits; the TMEM-weight plan may fall back to the other
-        for (int ts = 0; ts < 2; ++ts) {
-            Q8Plan p = plan_q8(rows, cols, red, sms, 0, ts == 1);
-            if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
-        }
+        // the pair plan never splits; the TMEM-weight plan may fall back to the
+        // other; a fused activation weighs the plans differently
+        for (int ts = 0; ts < 2; ++ts)
+            for (int act : {(int)ACT_NONE, (int)ACT_GELU_TANH}) {
+                Q8Plan p = plan_q8(rows, cols, red, sms, 0, ts == 1, act);
+                if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
+            }
     };
     if (M > 0) {
         if (r > 0) sk_part(M, K);  // A*x (forward, or recompute in the backward)
@@ -613,6 +624,8 @@ struct Q8Call {
     void *ext_buf;        // workspace for the prepared ext operand
     const void *bias;
     void *out;
+    int epi_act = ACT_NONE;  // fused output activation (act.cuh)
+    void *pre = nullptr;     // its rounded pre-activation [M][Nout]
 };
 
 template <int DT, int MT, int BN>
@@ -638,8 +651,19 @@ void launch_q8(int dt, int mt, int bn, dim3 grid, cudaStream_t st, const CUtenso
 
 template <int DT, int BT, int KB2>
 void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw, const CUtensorMap &te,
-                 const CUtensorMap &tsc, const CUtensorMap &to, const TsArgs &a) {
-    launch_pdl(q8ts_gemm_kernel<DT, BT, KB2>, dim3(grid), dim3(TS_THREADS), TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, a);
+                 const CUtensorMap &tsc, const CUtensorMap &to, const CUtensorMap &tp, const TsArgs &a) {
+    // The activation variant only when the kernel writes the output itself
+    // (split partials leave the activation to the reduce).
+    const int act = a.epi_partial ? ACT_NONE : a.epi_act;
+    if (act == ACT_GELU_TANH)
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH>, dim3(grid), dim3(TS_THREADS),
+                   TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, tp, a);
+    else if (act == ACT_GELU_TANH_GRAD)
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD>, dim3(grid), dim3(TS_THREADS),
+                   TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, tp, a);
+    else
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE>, dim3(grid), dim3(TS_THREADS), TsGeom<BT, KB2>::SMEM_BYTES,
+                   st, tx, tw, te, tsc, to, tp, a);
 }
 
 // Profiling hook shared by both q8 launch paths: events around the GEMM.
@@ -661,7 +685,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
               const Q8Plan &p) {
     const int bt = p.ts;
     const int sk = 64 * p.ts_kb2;  // reduction elements per pipeline stage
-    CUtensorMap tx, tw, te, tsc, to;
+    CUtensorMap tx, tw, te, tsc, to, tp;
     int rc = tmap_2d(&tx, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, bt,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -745,11 +769,19 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     a.partial = reinterpret_cast<float *>(ws_base + wl.part);
     a.epi_partial = p.split.splits > 1 ? 1 : 0;
     a.err = ds.status;
+    a.epi_act = c.epi_act;
+    a.pre = c.pre;
+    tp = tx;
     if (!a.epi_partial) {
         // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.
         rc = tmap_2d(&to, c.out, tma_act_type(dt), c.Nout, c.M, (uint64_t)c.Nout * 2, 32, 32,
                      CU_TENSOR_MAP_SWIZZLE_64B);
         if (rc) return rc;
+        if (c.epi_act != ACT_NONE && c.pre) {
+            rc = tmap_2d(&tp, c.pre, tma_act_type(dt), c.Nout, c.M, (uint64_t)c.Nout * 2, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B);
+            if (rc) return rc;
+        }
     } else {
         to = tx;
     }
@@ -758,24 +790,24 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     cudaEvent_t ev_stop = prof_begin(st, c);
     const int key = (dt == REELS_BF16 ? 10000 : 0) + bt * 10 + p.ts_kb2;
     switch (key) {
-        case 12561: launch_ts_t<DT_BF16, 256, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 11921: launch_ts_t<DT_BF16, 192, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 11281: launch_ts_t<DT_BF16, 128, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 11282: launch_ts_t<DT_BF16, 128, 2>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 12562: launch_ts_t<DT_BF16, 256, 2>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 11922: launch_ts_t<DT_BF16, 192, 2>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 2562: launch_ts_t<DT_F16, 256, 2>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 1922: launch_ts_t<DT_F16, 192, 2>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 2561: launch_ts_t<DT_F16, 256, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 1921: launch_ts_t<DT_F16, 192, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        case 1281: launch_ts_t<DT_F16, 128, 1>(grid, st, tx, tw, te, tsc, to, a); break;
-        default: launch_ts_t<DT_F16, 128, 2>(grid, st, tx, tw, te, tsc, to, a); break;
+        case 12561: launch_ts_t<DT_BF16, 256, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 11921: launch_ts_t<DT_BF16, 192, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 11281: launch_ts_t<DT_BF16, 128, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 11282: launch_ts_t<DT_BF16, 128, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 12562: launch_ts_t<DT_BF16, 256, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 11922: launch_ts_t<DT_BF16, 192, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 2562: launch_ts_t<DT_F16, 256, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 1922: launch_ts_t<DT_F16, 192, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 2561: launch_ts_t<DT_F16, 256, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 1921: launch_ts_t<DT_F16, 192, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        case 1281: launch_ts_t<DT_F16, 128, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+        default: launch_ts_t<DT_F16, 128, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
     }
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
         launch_pdl(q8_reduce_kernel, dim3(launch_grid(c.M * c.Nout / 4)), dim3(256), 0, st, a.partial, p.split.splits, c.M, c.Nout,
-                                                                    a.col_scale, c.bias, dt, c.out, c.Nout);
+                                                                    a.col_scale, c.bias, dt, c.out, c.Nout, c.epi_act, c.pre);
         REELS_LAUNCHED();
     }
     return REELS_OK;
@@ -784,8 +816,24 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
     // The TMEM-weight kernel loads the reduction scales by TMA (16-byte aligned base).
     const bool ts_ok = aligned16(c.scales);
-    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters, ts_ok);
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters, ts_ok, c.epi_act);
     if (p.ts) return run_q8_ts(c, dt, ds, ws_base, wl, st, p);
+    if (c.epi_act != ACT_NONE) {
+        // The SMEM-operand kernels have no activation epilogue: the GEMM
+        // writes the linear's output (gelu: into `pre` when given), then one
+        // elementwise pass applies the activation or its derivative.
+        Q8Call plain = c;
+        plain.epi_act = ACT_NONE;
+        plain.pre = nullptr;
+        if (c.epi_act == ACT_GELU_TANH && c.pre) plain.out = c.pre;
+        int rc = run_q8(plain, dt, ds, ws_base, wl, st);
+        if (rc) return rc;
+        const void *h = c.epi_act == ACT_GELU_TANH ? plain.out : c.pre;
+        launch_pdl(act_apply_kernel, dim3(launch_grid(c.M * c.Nout)), dim3(256), 0, st, c.epi_act, dt,
+                   c.M * c.Nout, c.out, h);
+        REELS_LAUNCHED();
+        return REELS_OK;
+    }
     CUtensorMap ta, tw, te;
     // Per-CTA boxes: the pair kernel loads 128 token rows and 128 weight
     // columns per CTA of a 256x256 tile.
@@ -888,7 +936,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
         launch_pdl(q8_reduce_kernel, dim3(launch_grid(c.M * c.Nout / 4)), dim3(256), 0, st, a.partial, p.split.splits, c.M, c.Nout,
-                                                                    a.col_scale, c.bias, dt, c.out, c.Nout);
+                                                                    a.col_scale, c.bias, dt, c.out, c.Nout, c.epi_act, c.pre);
         REELS_LAUNCHED();
     }
     return REELS_OK;
@@ -1069,12 +1117,15 @@ size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype) {
     return (size_t)r * ld_tokens(M) * esize(act_dtype);
 }
 
-int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
-                         const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
-                         int dt, void *y, void *saved, void *workspace, size_t ws_bytes, void *stream) {
+static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                               const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                               float alpha, int dt, int act, void *y, void *pre, void *saved, void *workspace,
+                               size_t ws_bytes, void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
     if (!x || !q || !scales || !y) return fail("null x, q, scales or y");
+    if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
+    if (pre == y) return fail("pre and y must be different buffers");
     if (r > 0 && (!A || !B)) return fail("null LoRA A or B");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
     if (M == 0) return ok(REELS_PATH_NONE);
@@ -1114,6 +1165,8 @@ int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, in
         c.ext_buf = ws + wl.ext;
         c.bias = bias;
         c.out = y;
+        c.epi_act = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH : ACT_NONE;
+        c.pre = act == REELS_ACT_NONE ? nullptr : pre;
         rc = run_q8(c, dt, *ds, ws, wl, st);
         if (rc) return rc;
         return ok(REELS_PATH_TENSORCORE);
@@ -1122,10 +1175,30 @@ int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, in
         gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(x, A, M, K, (int)r, dt, tbuf, ldm);
         REELS_LAUNCHED();
     }
+    void *lin = act != REELS_ACT_NONE && pre ? pre : y;  // the linear's output
     gen_forward_kernel<<<launch_grid(M * N), 256, 0, st>>>(x, q, scales, layout, bias, tbuf, ldm, B, M, K, N,
-                                                           (int)r, s, dt, y);
+                                                           (int)r, s, dt, lin);
     REELS_LAUNCHED();
+    if (act != REELS_ACT_NONE) {
+        act_apply_kernel<<<launch_grid(M * N), 256, 0, st>>>(ACT_GELU_TANH, dt, M * N, y, lin);
+        REELS_LAUNCHED();
+    }
     return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                         const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         int dt, void *y, void *saved, void *workspace, size_t ws_bytes, void *stream) {
+    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, dt, REELS_ACT_NONE, y, nullptr,
+                               saved, workspace, ws_bytes, stream);
+}
+
+int reels_q8lora_forward_act(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                             const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                             float alpha, int act_dtype, int act, void *y, void *pre, void *saved, void *workspace,
+                             size_t ws_bytes, void *stream) {
+    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, act_dtype, act, y, pre, saved,
+                               workspace, ws_bytes, stream);
 }
 
 int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int layout, const void *bias, int64_t M,
@@ -1135,13 +1208,17 @@ int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int
                                 nullptr, workspace, ws_bytes, stream);
 }
 
-int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
-                          const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N, int64_t r,
-                          float alpha, float grad_scale, int dt, void *dx, float *dA, float *dB, int accumulate,
-                          void *workspace, size_t ws_bytes, void *stream) {
+static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                                const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
+                                int64_t r, float alpha, float grad_scale, int dt, int act, const void *pre_x, void *dx,
+                                float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
+                                void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
     if (!dy || !q || !scales) return fail("null dy, q or scales");
+    if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
+    if (act != REELS_ACT_NONE && dx && !pre_x) return fail("null pre-activation of x");
+    if (act != REELS_ACT_NONE && dx && pre_x == dx) return fail("pre_x and dx must be different buffers");
     if (r > 0 && (!A || !B || !dA || !dB || !x)) return fail("null x, A, B, dA or dB with r > 0");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
     if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
@@ -1211,6 +1288,8 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
             c.ext_buf = ws + wl.ext;
             c.bias = nullptr;
             c.out = dx;
+            c.epi_act = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH_GRAD : ACT_NONE;
+            c.pre = act == REELS_ACT_NONE ? nullptr : const_cast<void *>(pre_x);
             rc = run_q8(c, dt, *ds, ws, wl, st);
             if (rc) return rc;
         }
@@ -1269,6 +1348,10 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
         gen_dx_kernel<<<launch_grid(M * K), 256, 0, st>>>(dy, q, scales, layout, gbuf, ldm, A, M, K, N, (int)r, dt,
                                                           dx);
         REELS_LAUNCHED();
+        if (act != REELS_ACT_NONE) {
+            act_apply_kernel<<<launch_grid(M * K), 256, 0, st>>>(ACT_GELU_TANH_GRAD, dt, M * K, dx, pre_x);
+            REELS_LAUNCHED();
+        }
     }
     if (r > 0) {
         gen_da_kernel<<<launch_grid(K * r), 256, 0, st>>>(gbuf, ldm, x, M, K, (int)r, grad_scale, accumulate, dt, dA);
@@ -1278,6 +1361,23 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
         REELS_LAUNCHED();
     }
     return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                          const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N, int64_t r,
+                          float alpha, float grad_scale, int dt, void *dx, float *dA, float *dB, int accumulate,
+                          void *workspace, size_t ws_bytes, void *stream) {
+    return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, dt,
+                                REELS_ACT_NONE, nullptr, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+}
+
+int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                              const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
+                              int64_t r, float alpha, float grad_scale, int act_dtype, int act, const void *pre_x,
+                              void *dx, float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
+                              void *stream) {
+    return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, act_dtype, act,
+                                pre_x, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
 }
 
 int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *scales, int layout, int64_t M,

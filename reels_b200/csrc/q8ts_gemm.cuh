@@ -31,6 +31,7 @@
 //          groups take alternate reduction blocks so two are in flight),
 // 11..18 epilogue (two per lane quarter, half of the tile's tokens each).
 #pragma once
+#include "act.cuh"
 #include "q8_gemm.cuh"
 
 namespace reels {
@@ -72,8 +73,8 @@ struct TsGeom {
     static constexpr int SC_OFF = W_OFF + S8 * W_BYTES;
     static constexpr int EPI_OFF = (SC_OFF + S8 * SC_BYTES + 1023) / 1024 * 1024;
     static constexpr int BAR_OFF = EPI_OFF + TS_NEW * EPI_BYTES;
-    // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done
-    static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1;
+    // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done, one pre-activation load per epilogue warp
+    static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1 + TS_NEW;
     static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
     static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
@@ -112,12 +113,21 @@ struct TsArgs {
     const void *bias;
     void *out;
     long long ldo;
+    int epi_act;       // EpiAct: gelu_tanh after the output, or its derivative (act.cuh)
+    void *pre;         // the rounded pre-activation [M][Nout]: written (gelu), read (gradient); nullable for gelu
     float *partial;    // [splits][M][Nout]
     unsigned *err;
 };
 
 __device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// Four 8x8 16-bit matrices read transposed into mma-fragment registers (the
+// inverse of stsm_x4_trans with the same addresses).
+__device__ __forceinline__ void ldsm_x4_trans_b16(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(addr));
 }
@@ -316,11 +326,12 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
     return c;
 }
 
-template <int DT, int BT, int KB2>
+template <int DT, int BT, int KB2, int ACT>
 __global__ void __launch_bounds__(TS_THREADS, 1)
     q8ts_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmS,
-                     const __grid_constant__ CUtensorMap tmO, const TsArgs args) {
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmP,
+                     const TsArgs args) {
     using G = TsGeom<BT, KB2>;
     using E = Elem<DT>;
     extern __shared__ uint8_t smem_raw[];
@@ -336,6 +347,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     uint64_t *acc_full = kb_empty + G::NA;
     uint64_t *acc_empty = acc_full + G::NACC;
     uint64_t *mma_done = acc_empty + G::NACC;
+    uint64_t *pre_bar = mma_done + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + G::MISC_OFF);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + G::MISC_OFF + 4);
 
@@ -357,6 +369,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             mbar_init(&acc_empty[i], TS_NEW);
         }
         mbar_init(mma_done, 1);
+        for (int i = 0; i < TS_NEW; ++i) mbar_init(&pre_bar[i], 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -366,6 +379,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         if (args.r > 0) tma_prefetch_desc(&tmE);
         if (args.scale_mode == 2) tma_prefetch_desc(&tmS);
         if (!args.epi_partial) tma_prefetch_desc(&tmO);
+        if (!args.epi_partial && args.epi_act != ACT_NONE && args.pre) tma_prefetch_desc(&tmP);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, 512);
@@ -604,10 +618,30 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int set = ew >> 2;
         const uint32_t stage0 = sbase + G::EPI_OFF + ew * G::EPI_BYTES;
         int buf = 0;
+        uint32_t pre_phase = 0;
+        bool pre_pending = false;  // a pre-activation load is in flight
         uint32_t local = 0;
+        // The activation is a compile-time variant: no branches in the
+        // per-element code, and ACT_NONE carries none of its registers.
+        constexpr int act = ACT;
+        const bool store_pre = act == ACT_GELU_TANH && args.pre != nullptr;
+        // Gradient: the pre-activation tile of a chunk is loaded (TMA, 32 x 32,
+        // 64B swizzle) into the second staging tile one chunk ahead; chunk 0's
+        // load is issued before the accumulator wait, under the MMAs.
+        auto load_pre = [&](const TsTile &c, int j0) {
+            fence_proxy_async_smem();  // earlier ldmatrix reads of the tile come first
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&pre_bar[ew], 2048);
+                tma_load_2d(reinterpret_cast<void *>(smem + (stage0 + 2048 - sbase)), &tmP, c.n0 + 32 * q,
+                            c.m0 + j0, &pre_bar[ew]);
+            }
+            pre_pending = true;
+        };
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
             const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
+            if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) load_pre(c, set * (BT / 2));
             if (!wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
                 break;
@@ -664,38 +698,89 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     if (lane == 0) mbar_arrive(&acc_empty[acc]);
                 }
                 const int m_base = c.m0 + j0;
-                // The staging tile this chunk reuses was last read by the TMA
-                // store issued two chunks ago.
-                if (lane == 0) bulk_wait_group_read<1>();
-                __syncwarp();
-                const uint32_t st_tile = stage0 + buf * 2048;
+                const bool rows_ok = m_base < args.M;  // rows past M are clipped by the TMA unit
+                uint32_t st_tile, pre_tile;
+                if (act == ACT_NONE) {
+                    // The staging tile this chunk reuses was last read by the TMA
+                    // store issued two chunks ago.
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+                    st_tile = stage0 + buf * 2048;
+                    pre_tile = st_tile;
+                    buf ^= 1;
+                } else {
+                    // Both staging tiles serve this chunk: the output and the
+                    // pre-activation (stored for gelu, loaded for its gradient).
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    __syncwarp();
+                    st_tile = stage0;
+                    pre_tile = stage0 + 2048;
+                }
+                uint32_t hp[4][4];  // gradient: the rounded pre-activation, in the accumulator's fragment layout
+                if (act == ACT_GELU_TANH_GRAD && rows_ok) {
+                    if (!wait_bar_all(&pre_bar[ew], pre_phase & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+                        aborted_here = true;
+                        break;
+                    }
+                    ++pre_phase;
+                    pre_pending = false;
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const uint32_t row = 8 * g + (lane & 7);
+                        ldsm_x4_trans_b16(pre_tile + row * 64 + (((lane >> 3) ^ ((row >> 1) & 3)) << 4), hp[g]);
+                    }
+                    if (ch + 1 < NCH && m_base + 32 < args.M) load_pre(c, j0 + 32);
+                }
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     // matrix (column block nb = 2hh + k, token block g)
-                    uint32_t pm[4];
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh)
-#pragma unroll
-                        for (int k = 0; k < 2; ++k)
-                            pm[2 * hh + k] =
-                                E::pack2(fmaf(__uint_as_float(r[hh][4 * g + 2 * k]), cs[hh][k], bs[hh][k]),
-                                         fmaf(__uint_as_float(r[hh][4 * g + 2 * k + 1]), cs[hh][k], bs[hh][k]));
+                    uint32_t pm[4], pp[4];
                     // thread 8i + j: row (token) 8g + j of matrix i, 16-byte chunk i (64B swizzle)
                     const uint32_t row = 8 * g + (lane & 7);
                     const uint32_t nb = lane >> 3;
-                    stsm_x4_trans(st_tile + row * 64 + ((nb ^ ((row >> 1) & 3)) << 4), pm[0], pm[1], pm[2], pm[3]);
+                    const uint32_t off = row * 64 + ((nb ^ ((row >> 1) & 3)) << 4);
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                        for (int k = 0; k < 2; ++k) {
+                            const float v0 = fmaf(__uint_as_float(r[hh][4 * g + 2 * k]), cs[hh][k], bs[hh][k]);
+                            const float v1 = fmaf(__uint_as_float(r[hh][4 * g + 2 * k + 1]), cs[hh][k], bs[hh][k]);
+                            const int i = 2 * hh + k;
+                            if (act == ACT_NONE) {
+                                pm[i] = E::pack2(v0, v1);
+                            } else if (act == ACT_GELU_TANH) {
+                                const float h0 = round_act<DT>(v0), h1 = round_act<DT>(v1);
+                                pp[i] = pack_rounded<DT>(h0, h1);
+                                pm[i] = E::pack2(gelu_tanh_f32(h0), gelu_tanh_f32(h1));
+                            } else {
+                                const uint32_t hw = hp[g][i];
+                                const float h0 = E::to_f(reinterpret_cast<const typename E::T *>(&hw)[0]);
+                                const float h1 = E::to_f(reinterpret_cast<const typename E::T *>(&hw)[1]);
+                                pm[i] = E::pack2(round_act<DT>(v0) * gelu_tanh_grad_f32(h0),
+                                                 round_act<DT>(v1) * gelu_tanh_grad_f32(h1));
+                            }
+                        }
+                    stsm_x4_trans(st_tile + off, pm[0], pm[1], pm[2], pm[3]);
+                    if (store_pre) stsm_x4_trans(pre_tile + off, pp[0], pp[1], pp[2], pp[3]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0 && m_base < args.M) {  // rows past M are clipped by the TMA unit
+                if (lane == 0 && rows_ok) {
                     tma_store_2d(&tmO, st_tile, c.n0 + 32 * q, m_base);
+                    if (store_pre) tma_store_2d(&tmP, pre_tile, c.n0 + 32 * q, m_base);
                     bulk_commit_group();
                 }
-                buf ^= 1;
+            }
+            if (aborted_here) break;
+        }
+        // Stores must finish reading shared memory before the CTA exits, and an
+        // abandoned pre-activation load must land (bounded wait).
+        if (lane == 0) bulk_wait_group<0>();
+        if (pre_pending) {
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&pre_bar[ew], pre_phase & 1) && clock64() - t0 < REELS_WAIT_LIMIT_CYCLES) {
             }
         }
-        // Stores must finish reading shared memory before the CTA exits.
-        if (lane == 0) bulk_wait_group<0>();
         __syncwarp();
     }
 

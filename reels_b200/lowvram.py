@@ -16,6 +16,9 @@ lora_forward                    :func:`lora_forward` (lora.jl:56-95)
 lora_backward                   :func:`lora_backward` (lora.jl:106-118)
 merged_weight                   :func:`merged_weight` (lora.jl:120-122)
 rrule(_weight_mul) / Zygote     :class:`LoRALinearFunction` (training/ad_rules.jl:70-80)
+_projection + gelu_tanh         :func:`lora_forward_gelu` (models/wan21/transformer.jl:289-291,
+                                layers/linear.jl:61-68)
+feed-forward pair               :class:`GeluFeedForwardFunction` (transformer.jl:287-292)
 ==============================  ===============================================
 
 Shapes: parameters keep the reference's logical shapes (weight (out, in),
@@ -293,6 +296,20 @@ def lora_forward(layer: LoRALinear, x: torch.Tensor, training: bool = False, dro
                  dropout_stream: int = 0, saved: Optional[torch.Tensor] = None) -> torch.Tensor:
     """lora_forward (lora.jl:56-95).  ``saved`` (optional uint8 buffer of
     reels_q8lora_saved_bytes) receives A*x for :func:`lora_backward`."""
+    return _lora_forward(layer, x, training, saved, nat.ACT_NONE, False)[0]
+
+
+def lora_forward_gelu(layer: LoRALinear, x: torch.Tensor, training: bool = False,
+                      saved: Optional[torch.Tensor] = None, keep_pre: bool = True):
+    """``gelu_tanh(lora_forward(layer, x))`` in one pass (the feed-forward
+    input projection and activation of transformer.jl:289-291).  Returns
+    ``(y, pre)``: y = gelu_tanh(pre), pre = the linear's output rounded to the
+    activation type (None unless ``keep_pre``; the backward of the next linear
+    needs it, see :func:`lora_backward`'s ``x_pre``)."""
+    return _lora_forward(layer, x, training, saved, nat.ACT_GELU_TANH, keep_pre)
+
+
+def _lora_forward(layer, x, training, saved, act, keep_pre):
     if training and layer.dropout > 0:
         raise NotImplementedError("LoRA dropout is not implemented on the native int8 path")
     N, K = layer.weight.shape
@@ -303,9 +320,18 @@ def lora_forward(layer: LoRALinear, x: torch.Tensor, training: bool = False, dro
     active_bias = layer.base_bias if (layer.train_bias and not layer.enabled) else layer.bias
     b = active_bias.contiguous().to(x.dtype) if active_bias is not None else None
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    pre = torch.empty((M, N), dtype=x.dtype, device=x.device) if keep_pre else None
     r = layer.rank if layer.enabled else 0
     ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_FORWARD)
-    if r > 0:
+    if act != nat.ACT_NONE:
+        A_mem = _colmajor(layer.A, x.dtype) if r > 0 else None
+        B_mem = _colmajor(layer.B, x.dtype) if r > 0 else None
+        code = nat.lib().reels_q8lora_forward_act(xf.data_ptr(), _wmem(layer.weight.values),
+                                                  layer.weight.scales.data_ptr(), layer.weight.layout,
+                                                  _ptr(A_mem), _ptr(B_mem), _ptr(b), M, K, N, r,
+                                                  float(layer.alpha) if r > 0 else 1.0, dt, act, y.data_ptr(), _ptr(pre),
+                                                  _ptr(saved), ws, wsn, _stream(x.device))
+    elif r > 0:
         A_mem = _colmajor(layer.A, x.dtype)   # [K][r]
         B_mem = _colmajor(layer.B, x.dtype)   # [r][N]
         code = nat.lib().reels_q8lora_forward(xf.data_ptr(), _wmem(layer.weight.values),
@@ -318,7 +344,8 @@ def lora_forward(layer: LoRALinear, x: torch.Tensor, training: bool = False, dro
                                              layer.weight.scales.data_ptr(), layer.weight.layout, _ptr(b), M, K,
                                              N, dt, y.data_ptr(), ws, wsn, _stream(x.device))
     nat.check("lora_forward", code)
-    return y.reshape(*x.shape[:-1], N)
+    shape = (*x.shape[:-1], N)
+    return y.reshape(shape), (pre.reshape(shape) if pre is not None else None)
 
 
 LoRAGradients = namedtuple("LoRAGradients", ["dx", "A", "B"])
@@ -326,12 +353,18 @@ LoRAGradients = namedtuple("LoRAGradients", ["dx", "A", "B"])
 
 def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: Optional[torch.Tensor] = None,
                   grad_scale: float = 1.0, dA_acc: Optional[torch.Tensor] = None,
-                  dB_acc: Optional[torch.Tensor] = None, need_dx: bool = True) -> LoRAGradients:
+                  dB_acc: Optional[torch.Tensor] = None, need_dx: bool = True,
+                  x_pre: Optional[torch.Tensor] = None) -> LoRAGradients:
     """lora_backward (lora.jl:106-118) -> (dx, A=dA, B=dB).
 
     dA/dB are fp32 with the logical shapes of A and B (column-major).  With
     ``dA_acc``/``dB_acc`` given (fp32 accumulators of that memory layout) the
-    gradients times ``grad_scale`` are added into them instead."""
+    gradients times ``grad_scale`` are added into them instead.
+
+    ``x_pre``: when the input is an activation's output, x = gelu_tanh(x_pre)
+    (the feed-forward output projection), the gradient is carried through the
+    activation in the same pass and ``dx`` is the gradient with respect to
+    ``x_pre`` (Zygote's pullback of gelu_tanh, linear.jl:61-68)."""
     if tuple(x.shape[:-1]) != tuple(dy.shape[:-1]):
         raise ValueError("LoRA input and output trailing dimensions differ")
     N, K = layer.weight.shape
@@ -353,11 +386,22 @@ def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: O
         dB_mem = torch.empty((r, N), dtype=torch.float32, device=x.device)
     dx = torch.empty((M, K), dtype=x.dtype, device=x.device) if need_dx else None
     ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_BACKWARD)
-    code = nat.lib().reels_q8lora_backward(xf.data_ptr(), dyf.data_ptr(), _wmem(layer.weight.values),
-                                           layer.weight.scales.data_ptr(), layer.weight.layout, A_mem.data_ptr(),
-                                           B_mem.data_ptr(), _ptr(saved), M, K, N, r, layer.alpha,
-                                           float(grad_scale), dt, _ptr(dx), dA_mem.data_ptr(), dB_mem.data_ptr(),
-                                           1 if accumulate else 0, ws, wsn, _stream(x.device))
+    if x_pre is not None:
+        if tuple(x_pre.shape) != tuple(x.shape) or x_pre.dtype != x.dtype:
+            raise ValueError("x_pre must have the shape and dtype of x")
+        xp = _flat(x_pre, K)
+        code = nat.lib().reels_q8lora_backward_act(
+            xf.data_ptr(), dyf.data_ptr(), _wmem(layer.weight.values), layer.weight.scales.data_ptr(),
+            layer.weight.layout, A_mem.data_ptr(), B_mem.data_ptr(), _ptr(saved), M, K, N, r, layer.alpha,
+            float(grad_scale), dt, nat.ACT_GELU_TANH, xp.data_ptr(), _ptr(dx), dA_mem.data_ptr(),
+            dB_mem.data_ptr(), 1 if accumulate else 0, ws, wsn, _stream(x.device))
+    else:
+        code = nat.lib().reels_q8lora_backward(xf.data_ptr(), dyf.data_ptr(), _wmem(layer.weight.values),
+                                               layer.weight.scales.data_ptr(), layer.weight.layout,
+                                               A_mem.data_ptr(), B_mem.data_ptr(), _ptr(saved), M, K, N, r,
+                                               layer.alpha, float(grad_scale), dt, _ptr(dx), dA_mem.data_ptr(),
+                                               dB_mem.data_ptr(), 1 if accumulate else 0, ws, wsn,
+                                               _stream(x.device))
     nat.check("lora_backward", code)
     return LoRAGradients(dx.reshape(x.shape) if dx is not None else None, dA_mem.t(), dB_mem.t())
 
@@ -401,3 +445,29 @@ class LoRALinearFunction(torch.autograd.Function):
         x, saved = ctx.saved_tensors
         g = lora_backward(ctx.layer, x, dy.contiguous(), saved=saved)
         return g.dx, g.A.to(ctx.layer.A.dtype), g.B.to(ctx.layer.B.dtype), None
+
+
+class GeluFeedForwardFunction(torch.autograd.Function):
+    """The feed-forward pair of the Wan block, ``ffn_out(gelu_tanh(ffn_in(x)))``
+    (transformer.jl:287-292), with gelu_tanh fused into ffn_in's output tile
+    and its derivative into ffn_out's dx tile.  Gradients flow to x and to
+    both adapters' A and B."""
+
+    @staticmethod
+    def forward(ctx, x, A_in, B_in, A_out, B_out, ffn_in, ffn_out):
+        saved_in = saved_buffer(ffn_in, x)
+        act, hidden = lora_forward_gelu(ffn_in, x, saved=saved_in)
+        saved_out = saved_buffer(ffn_out, act)
+        y = lora_forward(ffn_out, act, saved=saved_out)
+        ctx.layers = (ffn_in, ffn_out)
+        ctx.save_for_backward(x, act, hidden, saved_in, saved_out)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, act, hidden, saved_in, saved_out = ctx.saved_tensors
+        ffn_in, ffn_out = ctx.layers
+        g_out = lora_backward(ffn_out, act, dy.contiguous(), saved=saved_out, x_pre=hidden)
+        g_in = lora_backward(ffn_in, x, g_out.dx, saved=saved_in)
+        return (g_in.dx, g_in.A.to(ffn_in.A.dtype), g_in.B.to(ffn_in.B.dtype), g_out.A.to(ffn_out.A.dtype),
+                g_out.B.to(ffn_out.B.dtype), None, None)

@@ -85,6 +85,20 @@ def test_backward_rejects_null_gradients(lib):
     assert "dA" in _err(lib)
 
 
+def test_activation_entry_points_reject_bad_arguments(lib):
+    p = ctypes.c_void_p(0x1000)
+    q = ctypes.c_void_p(0x2000)
+    fwd = lambda act, y, pre: lib.reels_q8lora_forward_act(p, p, p, 0, p, p, None, 4, 16, 16, 2, 2.0, nat.BF16,
+                                                            act, y, pre, None, None, 0, None)
+    assert fwd(7, p, q) == nat.EINVAL and "activation" in _err(lib)
+    assert fwd(nat.ACT_GELU_TANH, p, p) == nat.EINVAL and "different" in _err(lib)
+    bwd = lambda act, pre_x, dx: lib.reels_q8lora_backward_act(p, p, p, p, 0, p, p, None, 4, 16, 16, 2, 2.0, 1.0,
+                                                                nat.BF16, act, pre_x, dx, p, p, 0, None, 0, None)
+    assert bwd(3, q, p) == nat.EINVAL and "activation" in _err(lib)
+    assert bwd(nat.ACT_GELU_TANH, None, p) == nat.EINVAL and "pre-activation" in _err(lib)
+    assert bwd(nat.ACT_GELU_TANH, p, p) == nat.EINVAL and "different" in _err(lib)
+
+
 def test_quantize_rejects_bad_arguments(lib):
     p = ctypes.c_void_p(0x1000)
     assert lib.reels_q8_quantize(None, nat.F32, 0, 4, 4, p, p, None) == nat.EINVAL

@@ -185,3 +185,25 @@ def test_oracle_reproduces_committed_fixtures(path):
     assert np.array_equal(Y, f["Y"])
     dX, dA, dB = oracle.lora_backward(f["X"], f["dY"], q, s, meta["layout"], f["A"], f["B"], meta["alpha"])
     assert np.array_equal(dX, f["dX"]) and np.array_equal(dA, f["dA"]) and np.array_equal(dB, f["dB"])
+
+
+def test_gelu_tanh_known_answers():
+    """gelu_tanh (src/layers/linear.jl:61-68): fixed points and the published
+    values of the tanh approximation, in fp32."""
+    x = np.array([0.0, 1.0, -1.0, 2.0, -3.0, 0.5, 10.0, -10.0], np.float32)
+    y = oracle.gelu_tanh(x)
+    expect = [0.0, 0.8411920, -0.1588080, 1.9545977, -0.0036374, 0.3457140, 10.0, 0.0]
+    assert np.allclose(y, expect, rtol=2e-6, atol=2e-7)
+    # odd part: gelu(x) - gelu(-x) = x
+    z = np.linspace(-6, 6, 1001, dtype=np.float32)
+    assert np.allclose(oracle.gelu_tanh(z) - oracle.gelu_tanh(-z), z, atol=2e-6)
+
+
+def test_gelu_tanh_grad_matches_finite_differences():
+    z = np.linspace(-8, 8, 4001)
+    k0, k1 = np.sqrt(2 / np.pi), 0.044715
+    f = lambda v: 0.5 * v * (1 + np.tanh(k0 * (v + k1 * v ** 3)))
+    h = 1e-5
+    fd = (f(z + h) - f(z - h)) / (2 * h)
+    got = oracle.gelu_tanh_grad(z.astype(np.float32))
+    assert np.max(np.abs(got - fd)) < 2e-6
