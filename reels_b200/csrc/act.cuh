@@ -56,16 +56,32 @@ __device__ __forceinline__ float gelu_logistic(float x) {
 
 __device__ __forceinline__ float gelu_tanh_f32(float x) { return x * gelu_logistic(x); }
 
+// gelu'(x) = s + 2 x s (1 - s) sqrt(2/pi) (1 + 3 * 0.044715 x^2)
+//          = s (1 + (1 - s) x (2 sqrt(2/pi) + 6 * 0.044715 sqrt(2/pi) x^2))
 __device__ __forceinline__ float gelu_tanh_grad_f32(float x) {
+    constexpr float kA = 2.0f * kGeluK0, kB = 6.0f * kGeluK1 * kGeluK0;
     const float s = gelu_logistic(x);
-    const float dinner = kGeluK0 * fmaf(3.0f * kGeluK1, x * x, 1.0f);
-    return fmaf(2.0f * x * s * (1.0f - s), dinner, s);
+    const float w = x * fmaf(kB, x * x, kA);
+    return s * fmaf(1.0f - s, w, 1.0f);
 }
 
 // The value an element takes after rounding to the activation dtype.
 template <int DT>
 __device__ __forceinline__ float round_act(float x) {
     return Elem<DT>::to_f(Elem<DT>::from_f(x));
+}
+
+// The two values of a packed pair (low half first), without taking the
+// register's address.
+template <int DT>
+__device__ __forceinline__ void unpack2(uint32_t w, float &a, float &b) {
+    if constexpr (DT == DT_BF16) {
+        a = __uint_as_float(w << 16);
+        b = __uint_as_float(w & 0xffff0000u);
+    } else {
+        a = __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+        b = __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+    }
 }
 
 // Two values already rounded to DT as one packed pair (a in the low half).

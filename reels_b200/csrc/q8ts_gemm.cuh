@@ -626,8 +626,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         constexpr int act = ACT;
         const bool store_pre = act == ACT_GELU_TANH && args.pre != nullptr;
         // Gradient: the pre-activation tile of a chunk is loaded (TMA, 32 x 32,
-        // 64B swizzle) into the second staging tile one chunk ahead; chunk 0's
-        // load is issued before the accumulator wait, under the MMAs.
+        // 64B swizzle) into the second staging tile while the chunk before it
+        // is computed, once that chunk has read its own; chunk 0's load and an
+        // L2 prefetch of the tile's other chunks are issued before the
+        // accumulator wait, under the MMAs.
         auto load_pre = [&](const TsTile &c, int j0) {
             fence_proxy_async_smem();  // earlier ldmatrix reads of the tile come first
             __syncwarp();
@@ -641,7 +643,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
             const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
-            if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) load_pre(c, set * (BT / 2));
+            if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) {
+                if (lane == 0)
+                    for (int ch = 1; ch < BT / 64; ++ch)
+                        if (c.m0 + set * (BT / 2) + 32 * ch < args.M)
+                            tma_prefetch_l2_2d(&tmP, c.n0 + 32 * q, c.m0 + set * (BT / 2) + 32 * ch);
+                load_pre(c, set * (BT / 2));
+            }
             if (!wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
                 break;
@@ -716,7 +724,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     st_tile = stage0;
                     pre_tile = stage0 + 2048;
                 }
-                uint32_t hp[4][4];  // gradient: the rounded pre-activation, in the accumulator's fragment layout
                 if (act == ACT_GELU_TANH_GRAD && rows_ok) {
                     if (!wait_bar_all(&pre_bar[ew], pre_phase & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                         aborted_here = true;
@@ -724,12 +731,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     }
                     ++pre_phase;
                     pre_pending = false;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const uint32_t row = 8 * g + (lane & 7);
-                        ldsm_x4_trans_b16(pre_tile + row * 64 + (((lane >> 3) ^ ((row >> 1) & 3)) << 4), hp[g]);
-                    }
-                    if (ch + 1 < NCH && m_base + 32 < args.M) load_pre(c, j0 + 32);
                 }
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
@@ -739,6 +740,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     const uint32_t row = 8 * g + (lane & 7);
                     const uint32_t nb = lane >> 3;
                     const uint32_t off = row * 64 + ((nb ^ ((row >> 1) & 3)) << 4);
+                    uint32_t hp[4];  // gradient: the rounded pre-activation, in the accumulator's fragment layout
+                    if (act == ACT_GELU_TANH_GRAD) {
+                        ldsm_x4_trans_b16(pre_tile + off, hp);
+                        // the last read of this chunk's pre-activation tile: the next chunk's may load
+                        if (g == 3 && rows_ok && ch + 1 < NCH && m_base + 32 < args.M) load_pre(c, j0 + 32);
+                    }
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh)
 #pragma unroll
@@ -753,9 +760,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                                 pp[i] = pack_rounded<DT>(h0, h1);
                                 pm[i] = E::pack2(gelu_tanh_f32(h0), gelu_tanh_f32(h1));
                             } else {
-                                const uint32_t hw = hp[g][i];
-                                const float h0 = E::to_f(reinterpret_cast<const typename E::T *>(&hw)[0]);
-                                const float h1 = E::to_f(reinterpret_cast<const typename E::T *>(&hw)[1]);
+                                float h0, h1;
+                                unpack2<DT>(hp[i], h0, h1);
                                 pm[i] = E::pack2(round_act<DT>(v0) * gelu_tanh_grad_f32(h0),
                                                  round_act<DT>(v1) * gelu_tanh_grad_f32(h1));
                             }
