@@ -215,6 +215,58 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
                               void *dx, float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
                               void *stream);
 
+/* ---------------------------------------------------------------------
+ * The optimizer step after the gradient all-reduce (src/training/
+ * wan_runner.jl:213-227 and AdamW update!, src/training/optimizer.jl:48-73),
+ * over all adapter tensors in two launches and without a host round trip:
+ *   reels_grad_norm_sq   sum of g^2 over every tensor (the clip's norm^2)
+ *   reels_adamw_update   clip by max_norm / norm when norm > max_norm, then
+ *                        AdamW with fp32 master weights; the model's copy
+ *                        of each parameter is rewritten from its master.
+ * One descriptor per parameter tensor; the tensors may differ in length
+ * and element type. */
+typedef struct reels_opt_tensor {
+    void *param;         /* [n] the model's copy, element type param_dtype   */
+    const float *grad;   /* [n] fp32 gradient (all-reduced)                  */
+    float *m;            /* [n] fp32 first moment                            */
+    float *v;            /* [n] fp32 second moment                           */
+    float *master;       /* [n] fp32 master weight                           */
+    int64_t n;
+    int param_dtype;     /* REELS_F32, REELS_F16 or REELS_BF16               */
+    int decay;           /* 0: excluded from weight decay (weight_decay_mask) */
+} reels_opt_tensor;
+
+/* Bytes of the optimizer workspace for `count` descriptors: the descriptor
+ * table (kept between steps) and the norm's partial sums. */
+size_t reels_opt_workspace_bytes(int count);
+
+/* Validate the descriptors and store them in `workspace` (device memory,
+ * 256-byte aligned, reels_opt_workspace_bytes(count) bytes), which then
+ * stands for this set of tensors in the calls below until it is prepared
+ * again.  Done once per set of tensors, not per step: it synchronises
+ * `stream` after the copy so `tensors` may be released on return. */
+int reels_opt_prepare(const reels_opt_tensor *tensors, int count, void *workspace, size_t ws_bytes, void *stream);
+
+/* *sumsq (device fp32) = sum over the prepared tensors of (grad_scale*g)^2,
+ * the norm_squared of wan_runner.jl:215 (grad_scale: a factor applied first,
+ * e.g. the 1/gradient_accumulation of wan_runner.jl:212).  Accumulated in
+ * fp64 in a fixed order, then rounded: the same inputs give the same bits. */
+int reels_grad_norm_sq(void *workspace, float grad_scale, float *sumsq, void *stream);
+
+/* AdamW step `update!` (optimizer.jl:48-73) for every prepared tensor:
+ *   g  = grad_scale * grad; if sumsq is given: norm = sqrt(*sumsq), and when
+ *        norm > max_norm, g = g * (max_norm / norm)   (wan_runner.jl:218-221)
+ *   m  = beta1 m + (1 - beta1) g ;  v = beta2 v + (1 - beta2) g^2
+ *   master -= lr ((m / correction1) / (sqrt(v / correction2) + eps)
+ *                 + decay * weight_decay * master)
+ *   param  = master rounded to param_dtype
+ * correction1/2 are 1 - beta1^step and 1 - beta2^step of the step being
+ * taken (the caller counts steps).  Each operation is rounded once in fp32,
+ * with no fused multiply-add, as the reference's broadcasts evaluate it. */
+int reels_adamw_update(void *workspace, float lr, float beta1, float beta2, float eps, float weight_decay,
+                       float correction1, float correction2, float grad_scale, const float *sumsq, float max_norm,
+                       void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,9 +9,11 @@ Two restatements of the reference arithmetic live here:
 * ``reels_oracle.c`` (wrapped below): bit-exact quantiser
   (src/layers/quantization.jl:35-44), fp32/fp16/bf16 materialisation
   (quantization.jl:54-64, src/models/interface.jl:13-25), the forward /
-  backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation, and
-  gelu_tanh with its derivative (src/layers/linear.jl:61-68): the gold
-  standard the CUDA results are compared against.
+  backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation,
+  gelu_tanh with its derivative (src/layers/linear.jl:61-68), and the AdamW
+  step with the gradient-norm clip (src/training/optimizer.jl:48-73,
+  wan_runner.jl:213-221): the gold standard the CUDA results are compared
+  against.
 * ``numpy_port.py``: the reference CPU code path in fp32 through OpenBLAS
   (what Julia's LinearAlgebra calls), used as the timed CPU baseline.
 
@@ -58,6 +60,10 @@ def lib():
                                            _i64, _i64, _i64, _i64, ctypes.c_float, vp, vp, vp]
         L.oracle_gelu_tanh.argtypes = [_f32p, _i64, _f32p]
         L.oracle_gelu_tanh_grad.argtypes = [_f32p, _i64, _f32p]
+        f = ctypes.c_float
+        L.oracle_adamw_update.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, f, f, f, f, f, f, f, f, ctypes.c_int, f]
+        L.oracle_sumsq.argtypes = [_f32p, _i64, ctypes.c_float]
+        L.oracle_sumsq.restype = ctypes.c_double
         L.oracle_rel_l2.argtypes = [_f32p, _f32p, _i64]
         L.oracle_rel_l2.restype = ctypes.c_double
         _LIB = L
@@ -192,6 +198,25 @@ def gelu_tanh_grad(h):
     out = np.empty_like(h)
     lib().oracle_gelu_tanh_grad(h.ravel(), h.size, out.ravel())
     return out
+
+
+def adamw_update(g, m, v, w, lr, beta1, beta2, eps, decay, c1, c2, grad_scale=1.0, clip_scale=None):
+    """update! (src/training/optimizer.jl:63-71) on copies of m, v, w (fp32),
+    with the gradient clipped by ``clip_scale`` first when given
+    (wan_runner.jl:218-221).  Returns the new (m, v, w)."""
+    g = _c(g, np.float32).ravel()
+    m = np.array(m, np.float32).ravel()
+    v = np.array(v, np.float32).ravel()
+    w = np.array(w, np.float32).ravel()
+    lib().oracle_adamw_update(g, m, v, w, g.size, lr, beta1, beta2, eps, decay, c1, c2, grad_scale,
+                              0 if clip_scale is None else 1, 0.0 if clip_scale is None else clip_scale)
+    return m, v, w
+
+
+def sumsq(grads, grad_scale=1.0) -> float:
+    """Sum over every array of (grad_scale*g)^2, in fp64."""
+    return float(sum(lib().oracle_sumsq(_c(g, np.float32).ravel(), np.asarray(g).size, grad_scale)
+                     for g in grads))
 
 
 def rel_l2(a, b) -> float:

@@ -260,6 +260,51 @@ void oracle_gelu_tanh_grad(const float *x, int64_t n, float *out)
     }
 }
 
+/* update! of src/training/optimizer.jl:63-71 over one tensor, with the clip
+ * of src/training/wan_runner.jl:218-221 applied to the gradient first when
+ * `clip` is set.  fp32 throughout, each operation rounded once (this file is
+ * built with -ffp-contract=off, and Julia's broadcasts do not fuse):
+ *   g = gs*g; g = g*clip_scale; m = b1*m + (1-b1)*g; v = b2*v + (1-b2)*g*g
+ *   w = w - lr*((m/c1)/(sqrt(v/c2) + eps) + decay*w)
+ * The model's copy of the parameter is w rounded to its element type, which
+ * the caller does. */
+void oracle_adamw_update(const float *g, float *m, float *v, float *w, int64_t n, float lr, float b1, float b2,
+                         float eps, float decay, float c1, float c2, float gs, int clip, float clip_scale)
+{
+    const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
+    for (int64_t i = 0; i < n; ++i) {
+        float gi = g[i];
+        if (gs != 1.0f) gi = gi * gs;
+        if (clip) gi = gi * clip_scale;
+        const float mi = b1 * m[i] + omb1 * gi;
+        const float g2 = gi * gi;
+        const float vi = b2 * v[i] + omb2 * g2;
+        const float t1 = mi / c1;
+        const float t2 = vi / c2;
+        const float t3 = sqrtf(t2);
+        const float t4 = t3 + eps;
+        const float t5 = t1 / t4;
+        const float t6 = decay * w[i];
+        const float t7 = t5 + t6;
+        const float t8 = lr * t7;
+        m[i] = mi;
+        v[i] = vi;
+        w[i] = w[i] - t8;
+    }
+}
+
+/* sum of (gs*g)^2 in fp64: the reference's norm_squared (wan_runner.jl:215)
+ * without its fp32 summation-order dependence. */
+double oracle_sumsq(const float *g, int64_t n, float gs)
+{
+    double s = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        const float a = g[i] * gs;
+        s += (double)a * (double)a;
+    }
+    return s;
+}
+
 /* Relative L2 error ||a - b|| / ||b|| in fp64 (the north-star metric). */
 double oracle_rel_l2(const float *a, const float *b, int64_t n)
 {

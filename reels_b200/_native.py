@@ -21,6 +21,13 @@ PATH_NONE, PATH_TENSORCORE, PATH_CUDACORE = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH = 0, 1
 OK, EINVAL, EDEVICE = 0, -1, -2
 
+class OptTensor(ctypes.Structure):
+    """reels_opt_tensor: one parameter tensor of the optimizer step."""
+    _fields_ = [("param", ctypes.c_void_p), ("grad", ctypes.c_void_p), ("m", ctypes.c_void_p),
+                ("v", ctypes.c_void_p), ("master", ctypes.c_void_p), ("n", ctypes.c_int64),
+                ("param_dtype", ctypes.c_int), ("decay", ctypes.c_int)]
+
+
 # Every symbol the header declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -51,6 +58,10 @@ SIGNATURES = {
                                         _int, _vp, _vp, _vp, _vp, _sz, _vp]),
     "reels_q8lora_backward_act": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _f,
                                          _int, _int, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp]),
+    "reels_opt_workspace_bytes": (_sz, [_int]),
+    "reels_opt_prepare": (_int, [ctypes.POINTER(OptTensor), _int, _vp, _sz, _vp]),
+    "reels_grad_norm_sq": (_int, [_vp, _f, _vp, _vp]),
+    "reels_adamw_update": (_int, [_vp, _f, _f, _f, _f, _f, _f, _f, _f, _vp, _f, _vp]),
 }
 
 _lock = threading.Lock()

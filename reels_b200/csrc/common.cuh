@@ -25,6 +25,7 @@ enum DevErr : unsigned {
     DEVERR_TIMEOUT_W_EMPTY = 8u,
     DEVERR_TIMEOUT_ACC = 16u,
     DEVERR_NONFINITE_WEIGHT = 256u,
+    DEVERR_OPT_TABLE = 512u,  // an optimizer workspace that was not prepared
 };
 
 // ---------------------------------------------------------------- elements

@@ -16,6 +16,7 @@
 #include "aux_kernels.cuh"
 #include "q8_gemm.cuh"
 #include "q8_gemm_2sm.cuh"
+#include "optim.cuh"
 #include "q8ts_gemm.cuh"
 
 using namespace reels;
@@ -1035,7 +1036,9 @@ int reels_lowvram_check_device_status(void *stream) {
     if (h) {
         REELS_CUDA(cudaMemcpy(ds->status, &zero, 4, cudaMemcpyHostToDevice));
         char buf[128];
-        snprintf(buf, sizeof buf, "device status 0x%x: a pipeline wait timed out", h);
+        snprintf(buf, sizeof buf, "device status 0x%x: %s", h,
+                 (h & DEVERR_OPT_TABLE) ? "an optimizer call on a workspace that reels_opt_prepare did not set up"
+                                        : "a pipeline wait timed out");
         return fail_dev(buf);
     }
     t_last_error.clear();
@@ -1378,6 +1381,106 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
                               void *stream) {
     return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, act_dtype, act,
                                 pre_x, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+}
+
+size_t reels_opt_workspace_bytes(int count) {
+    if (count < 0) return 0;
+    return opt_table_end(count);
+}
+
+int reels_opt_prepare(const reels_opt_tensor *tensors, int count, void *workspace, size_t ws_bytes, void *stream) {
+    if (count < 0) return fail("negative tensor count");
+    if (count > 0 && !tensors) return fail("null tensor table");
+    if (!workspace) return fail("null optimizer workspace");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("optimizer workspace must be 256-byte aligned");
+    if (ws_bytes < reels_opt_workspace_bytes(count))
+        return fail("optimizer workspace too small: need " + std::to_string(reels_opt_workspace_bytes(count)) +
+                    " bytes, got " + std::to_string(ws_bytes));
+    // header and table (the partials in between are scratch: not copied)
+    std::vector<char> host(opt_table_end(count), 0);
+    OptHeader *h = reinterpret_cast<OptHeader *>(host.data());
+    OptEntry *tab = reinterpret_cast<OptEntry *>(host.data() + OPT_TABLE_OFF);
+    int64_t chunks = 0;
+    for (int i = 0; i < count; ++i) {
+        const reels_opt_tensor &t = tensors[i];
+        if (t.n < 0) return fail("tensor " + std::to_string(i) + ": negative length");
+        if (t.param_dtype != REELS_F32 && t.param_dtype != REELS_F16 && t.param_dtype != REELS_BF16)
+            return fail("tensor " + std::to_string(i) + ": unknown param_dtype");
+        if (t.n > 0 && (!t.param || !t.grad || !t.m || !t.v || !t.master))
+            return fail("tensor " + std::to_string(i) + ": null pointer");
+        tab[i].t = t;
+        tab[i].chunk0 = chunks;
+        const size_t pal = t.param_dtype == REELS_F32 ? 16 : 8;
+        tab[i].vec = aligned16(t.grad) && aligned16(t.m) && aligned16(t.v) && aligned16(t.master) &&
+                     (reinterpret_cast<uintptr_t>(t.param) % pal) == 0;
+        chunks += (t.n + OPT_CHUNK - 1) / OPT_CHUNK;
+    }
+    h->magic = OPT_MAGIC;
+    h->count = count;
+    h->total_chunks = chunks;
+    DeviceState *ds;
+    int rc = bind_device(workspace, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char *dws = reinterpret_cast<char *>(workspace);
+    REELS_CUDA(cudaMemcpyAsync(dws, host.data(), sizeof(OptHeader), cudaMemcpyHostToDevice, st));
+    if (count > 0)
+        REELS_CUDA(cudaMemcpyAsync(dws + OPT_TABLE_OFF, host.data() + OPT_TABLE_OFF, host.size() - OPT_TABLE_OFF,
+                                   cudaMemcpyHostToDevice, st));
+    REELS_CUDA(cudaStreamSynchronize(st));
+    return ok(REELS_PATH_CUDACORE);
+}
+
+static int opt_blocks(const DeviceState &ds) { return std::min(OPT_MAX_BLOCKS, 4 * ds.sms); }
+
+int reels_grad_norm_sq(void *workspace, float grad_scale, float *sumsq, void *stream) {
+    if (!workspace || !sumsq) return fail("null workspace or sumsq");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("optimizer workspace must be 256-byte aligned");
+    if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
+    DeviceState *ds;
+    int rc = bind_device(workspace, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const char *ws = reinterpret_cast<const char *>(workspace);
+    double *partials = reinterpret_cast<double *>(reinterpret_cast<char *>(workspace) + OPT_PARTIALS_OFF);
+    const int nb = opt_blocks(*ds);
+    launch_pdl(grad_sumsq_kernel, dim3(nb), dim3(OPT_THREADS), 0, st, ws, grad_scale, partials, ds->status);
+    REELS_LAUNCHED();
+    launch_pdl(grad_sumsq_final_kernel, dim3(1), dim3(OPT_MAX_BLOCKS), 0, st, (const double *)partials, nb, sumsq);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_adamw_update(void *workspace, float lr, float beta1, float beta2, float eps, float weight_decay,
+                       float correction1, float correction2, float grad_scale, const float *sumsq, float max_norm,
+                       void *stream) {
+    if (!workspace) return fail("null optimizer workspace");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("optimizer workspace must be 256-byte aligned");
+    for (float f : {lr, beta1, beta2, eps, weight_decay, correction1, correction2, grad_scale})
+        if (!std::isfinite(f)) return fail("optimizer hyperparameters must be finite");
+    if (!(correction1 > 0.0f) || !(correction2 > 0.0f)) return fail("bias corrections must be positive");
+    if (sumsq && !(max_norm > 0.0f)) return fail("max_norm must be positive when clipping");
+    DeviceState *ds;
+    int rc = bind_device(workspace, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    AdamArgs a;
+    a.lr = lr;
+    a.beta1 = beta1;
+    a.beta2 = beta2;
+    a.omb1 = 1.0f - beta1;  // (1f0 - opt.beta1), rounded in fp32 as the reference forms it
+    a.omb2 = 1.0f - beta2;
+    a.eps = eps;
+    a.wd = weight_decay;
+    a.c1 = correction1;
+    a.c2 = correction2;
+    a.gs = grad_scale;
+    a.max_norm = max_norm;
+    a.sumsq = sumsq;
+    launch_pdl(adamw_kernel, dim3(opt_blocks(*ds)), dim3(OPT_THREADS), 0, st, (const char *)workspace, a,
+               ds->status);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
 }
 
 int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *scales, int layout, int64_t M,
