@@ -60,6 +60,7 @@ extern "C" {
 /* which pass a workspace query is for */
 #define REELS_PASS_FORWARD 0
 #define REELS_PASS_BACKWARD 1
+#define REELS_PASS_DROPOUT 2 /* or-ed into the pass: room for the dropped-out input */
 
 /* execution paths reported by reels_lowvram_last_path() */
 /* Activation fused into a linear's output (forward) or its input's gradient
@@ -214,6 +215,36 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
                               int64_t r, float alpha, float grad_scale, int act_dtype, int act, const void *pre_x,
                               void *dx, float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
                               void *stream);
+
+/* lora_forward with LoRA dropout (lora.jl:71-85, training with dropout > 0):
+ * the adapter's input is z = x * keep / (1 - dropout) (rounded to act_dtype),
+ * the frozen weight still multiplies x:
+ *   y = dequant(q) * x (+ bias) + (alpha / r) * B * (A * z)
+ * keep = (u >= dropout) with u a uniform Float32 per element of x drawn from
+ * a counter-based generator keyed by seed xor (stream_id * 0x9e3779b97f4a7c15)
+ * (the reference's _dropout_seed, lora.jl:41-43) and indexed by the element's
+ * linear position; see reels_dropout_mask.  The workspace comes from
+ * reels_q8lora_workspace_bytes(..., REELS_PASS_FORWARD | REELS_PASS_DROPOUT).
+ * `saved` receives A * z. */
+int reels_q8lora_forward_dropout(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                                 const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                                 float alpha, int act_dtype, float dropout, uint64_t seed, uint64_t stream_id, void *y,
+                                 void *saved, void *workspace, size_t ws_bytes, void *stream);
+
+/* The gradients of reels_q8lora_forward_dropout with the same seed and
+ * stream_id (the mask is recomputed, not stored):
+ *   dx = dequant(q)' * dy + keep * (s * A' * (B' * dy)) / (1 - dropout)
+ *   dA = s * (B' * dy) * z'      dB = s * dy * (A * z)'
+ * Workspace: REELS_PASS_BACKWARD | REELS_PASS_DROPOUT. */
+int reels_q8lora_backward_dropout(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                                  const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
+                                  int64_t r, float alpha, float grad_scale, int act_dtype, float dropout, uint64_t seed,
+                                  uint64_t stream_id, void *dx, float *dA, float *dB, int accumulate, void *workspace,
+                                  size_t ws_bytes, void *stream);
+
+/* The dropout mask itself: keep[i] = 1 where element i of the adapter input
+ * is kept, 0 where dropped, for i < n (n = M * K, i = token * K + feature). */
+int reels_dropout_mask(int64_t n, float dropout, uint64_t seed, uint64_t stream_id, uint8_t *keep, void *stream);
 
 /* ---------------------------------------------------------------------
  * The optimizer step after the gradient all-reduce (src/training/

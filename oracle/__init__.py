@@ -10,7 +10,8 @@ Two restatements of the reference arithmetic live here:
   (src/layers/quantization.jl:35-44), fp32/fp16/bf16 materialisation
   (quantization.jl:54-64, src/models/interface.jl:13-25), the forward /
   backward of lora.jl:56-95 / lora.jl:106-118 with fp64 accumulation,
-  gelu_tanh with its derivative (src/layers/linear.jl:61-68), and the AdamW
+  gelu_tanh with its derivative (src/layers/linear.jl:61-68), the LoRA
+  dropout forms of both with the library's counter-based mask, and the AdamW
   step with the gradient-norm clip (src/training/optimizer.jl:48-73,
   wan_runner.jl:213-221): the gold standard the CUDA results are compared
   against.
@@ -64,6 +65,12 @@ def lib():
         L.oracle_adamw_update.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, f, f, f, f, f, f, f, f, ctypes.c_int, f]
         L.oracle_sumsq.argtypes = [_f32p, _i64, ctypes.c_float]
         L.oracle_sumsq.restype = ctypes.c_double
+        L.oracle_lora_forward_z.argtypes = [_f32p, vp, _i8p, _f32p, ctypes.c_int, _f32p, _f32p, vp,
+                                            _i64, _i64, _i64, _i64, ctypes.c_float, _f32p, vp]
+        L.oracle_lora_backward_z.argtypes = [_f32p, vp, vp, _f32p, _i8p, _f32p, ctypes.c_int, _f32p, _f32p,
+                                             _i64, _i64, _i64, _i64, ctypes.c_float, vp, vp, vp]
+        L.oracle_dropout_keep.argtypes = [_i64, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64,
+                                          np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")]
         L.oracle_rel_l2.argtypes = [_f32p, _f32p, _i64]
         L.oracle_rel_l2.restype = ctypes.c_double
         _LIB = L
@@ -217,6 +224,40 @@ def sumsq(grads, grad_scale=1.0) -> float:
     """Sum over every array of (grad_scale*g)^2, in fp64."""
     return float(sum(lib().oracle_sumsq(_c(g, np.float32).ravel(), np.asarray(g).size, grad_scale)
                      for g in grads))
+
+
+def dropout_keep(n, p, seed, stream=0):
+    """The library's LoRA dropout mask (uint8, 1 = kept) for n elements."""
+    keep = np.empty(n, np.uint8)
+    lib().oracle_dropout_keep(n, p, seed & 0xFFFFFFFFFFFFFFFF, stream & 0xFFFFFFFFFFFFFFFF, keep)
+    return keep
+
+
+def lora_dropout(X, Z, dY, q, scales, layout, A, B, alpha, dscale, bias=None):
+    """Forward and backward with LoRA dropout (lora.jl:71-85): the adapter's
+    input is Z, its part of dX is scaled per element by dscale.  Returns
+    (Y, dX, dA, dB), fp64 accumulation."""
+    X = _c(X, np.float32)
+    Z = _c(Z, np.float32)
+    dY = _c(dY, np.float32)
+    A = _c(A, np.float32)
+    B = _c(B, np.float32)
+    q = _c(q, np.int8)
+    scales = _c(scales, np.float32)
+    dscale = _c(dscale, np.float32)
+    M, K = X.shape
+    r = A.shape[1]
+    N = scales.shape[0]
+    Y = np.empty((M, N), np.float32)
+    b = _c(bias, np.float32) if bias is not None else None
+    lib().oracle_lora_forward_z(X, Z.ctypes.data, q, scales, layout, A, B, b.ctypes.data if b is not None else None,
+                                M, K, N, r, float(alpha), Y, None)
+    dX = np.empty((M, K), np.float32)
+    dA = np.empty((K, r), np.float32)
+    dB = np.empty((r, N), np.float32)
+    lib().oracle_lora_backward_z(X, Z.ctypes.data, dscale.ctypes.data, dY, q, scales, layout, A, B, M, K, N, r,
+                                 float(alpha), dX.ctypes.data, dA.ctypes.data, dB.ctypes.data)
+    return Y, dX, dA, dB
 
 
 def rel_l2(a, b) -> float:

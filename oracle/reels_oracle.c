@@ -133,10 +133,12 @@ void oracle_bf16_materialise_array(const int8_t *q, const float *scales, int lay
  * Inputs are fp32 (bf16/fp16 inputs are widened exactly by the caller);
  * accumulation is fp64, the result is rounded once to fp32.
  * T_out (nullable) receives T as [M][r]. */
-void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, int layout,
-                         const float *A, const float *B, const float *bias,
-                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
-                         float *Y, float *T_out)
+/* Z (nullable): the adapter's input when it differs from X (LoRA dropout,
+ * lora.jl:71-85): T = A * Z, the frozen weight still multiplies X. */
+void oracle_lora_forward_z(const float *X, const float *Z, const int8_t *q, const float *scales, int layout,
+                           const float *A, const float *B, const float *bias,
+                           int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                           float *Y, float *T_out)
 {
     double s = r > 0 ? (double)(alpha / (float)r) : 0.0;  /* r = 0: no adapter */
     double *T = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
@@ -145,9 +147,10 @@ void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, i
     #pragma omp parallel for schedule(static)
     for (int64_t m = 0; m < M; ++m) {
         const float *x = X + m * K;
+        const float *z = (Z ? Z : X) + m * K;
         for (int64_t j = 0; j < r; ++j) {
             double acc = 0.0;
-            for (int64_t k = 0; k < K; ++k) acc += (double)x[k] * (double)A[k * r + j];
+            for (int64_t k = 0; k < K; ++k) acc += (double)z[k] * (double)A[k * r + j];
             T[m * r + j] = acc;
             if (T_out) T_out[m * r + j] = (float)acc;
         }
@@ -165,6 +168,14 @@ void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, i
     free(T);
 }
 
+void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, int layout,
+                         const float *A, const float *B, const float *bias,
+                         int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                         float *Y, float *T_out)
+{
+    oracle_lora_forward_z(X, NULL, q, scales, layout, A, B, bias, M, K, N, r, alpha, Y, T_out);
+}
+
 /* Backward, lora.jl:106-118 (identical to Zygote's pullback of lora_forward
  * through the rrule at ad_rules.jl:70-80):
  *   ax = A * x
@@ -172,11 +183,15 @@ void oracle_lora_forward(const float *X, const int8_t *q, const float *scales, i
  *   dB = s * dy * ax'                 -> [r][N] here (Julia (out, r))
  *   dx = Wdq' * dy + s * A' * (B' * dy)
  * fp64 accumulation, fp32 results.  Any of dX, dA, dB may be NULL. */
-void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, const float *scales, int layout,
-                          const float *A, const float *B,
-                          int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
-                          float *dX, float *dA, float *dB)
+/* With LoRA dropout the adapter saw Z = X * keep / (1 - p): T = A * Z,
+ * dA = s * G * Z', and the adapter's part of dX is scaled per element by
+ * dscale = keep / (1 - p) ([M][K]).  Z and dscale NULL: no dropout. */
+void oracle_lora_backward_z(const float *X, const float *Z, const float *dscale, const float *dY, const int8_t *q,
+                            const float *scales, int layout, const float *A, const float *B,
+                            int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                            float *dX, float *dA, float *dB)
 {
+    if (!Z) Z = X;
     double s = r > 0 ? (double)(alpha / (float)r) : 0.0;  /* r = 0: no adapter */
     double *G = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
     double *T = (double *)malloc(sizeof(double) * (size_t)(M * (r > 0 ? r : 1)));
@@ -187,7 +202,7 @@ void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, cons
         for (int64_t j = 0; j < r; ++j) {
             double g = 0.0, t = 0.0;
             for (int64_t n = 0; n < N; ++n) g += (double)dY[m * N + n] * (double)B[j * N + n];
-            for (int64_t k = 0; k < K; ++k) t += (double)X[m * K + k] * (double)A[k * r + j];
+            for (int64_t k = 0; k < K; ++k) t += (double)Z[m * K + k] * (double)A[k * r + j];
             G[m * r + j] = g;
             T[m * r + j] = t;
         }
@@ -201,6 +216,7 @@ void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, cons
                     acc += (double)dY[m * N + n] * (double)Wd[OIDX_W(layout, n, k, N, K)];
                 double lora = 0.0;
                 for (int64_t j = 0; j < r; ++j) lora += (double)A[k * r + j] * G[m * r + j];
+                if (dscale) lora *= (double)dscale[m * K + k];
                 dX[m * K + k] = (float)(acc + s * lora);
             }
         }
@@ -210,7 +226,7 @@ void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, cons
         for (int64_t k = 0; k < K; ++k)
             for (int64_t j = 0; j < r; ++j) {
                 double acc = 0.0;
-                for (int64_t m = 0; m < M; ++m) acc += G[m * r + j] * (double)X[m * K + k];
+                for (int64_t m = 0; m < M; ++m) acc += G[m * r + j] * (double)Z[m * K + k];
                 dA[k * r + j] = (float)(s * acc);
             }
     }
@@ -226,6 +242,33 @@ void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, cons
     free(Wd);
     free(T);
     free(G);
+}
+
+void oracle_lora_backward(const float *X, const float *dY, const int8_t *q, const float *scales, int layout,
+                          const float *A, const float *B,
+                          int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
+                          float *dX, float *dA, float *dB)
+{
+    oracle_lora_backward_z(X, NULL, NULL, dY, q, scales, layout, A, B, M, K, N, r, alpha, dX, dA, dB);
+}
+
+/* The LoRA dropout mask of the library (its counter-based generator,
+ * restated): key = seed xor (stream * 0x9e3779b97f4a7c15) (lora.jl:41-43);
+ * for element i, z = key + (i + 1) * 0x9e3779b97f4a7c15 through the SplitMix64
+ * output function (Steele, Lea, Flood 2014); u = (z >> 40) * 2^-24 in fp32;
+ * keep = u >= p. */
+void oracle_dropout_keep(int64_t n, float p, uint64_t seed, uint64_t stream, uint8_t *keep)
+{
+    const uint64_t golden = 0x9e3779b97f4a7c15ull;
+    const uint64_t key = seed ^ (stream * golden);
+    for (int64_t i = 0; i < n; ++i) {
+        uint64_t z = key + ((uint64_t)i + 1) * golden;
+        z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+        z ^= z >> 31;
+        const float u = (float)(uint32_t)(z >> 40) * 0x1p-24f;
+        keep[i] = u >= p ? 1 : 0;
+    }
 }
 
 /* gelu_tanh of src/layers/linear.jl:61-68, elementwise in fp32 as written

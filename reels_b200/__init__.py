@@ -12,6 +12,7 @@ from .lowvram import (  # noqa: F401
     LoRALinearFunction,
     QuantizedMatrix,
     check_device_status,
+    dropout_mask,
     linear,
     lora_backward,
     lora_forward,

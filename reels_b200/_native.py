@@ -16,7 +16,7 @@ LIB_NAME = "libreels_lowvram.so"
 
 F32, F16, BF16 = 0, 1, 2
 W_OUT_CONTIGUOUS, W_IN_CONTIGUOUS = 0, 1
-PASS_FORWARD, PASS_BACKWARD = 0, 1
+PASS_FORWARD, PASS_BACKWARD, PASS_DROPOUT = 0, 1, 2
 PATH_NONE, PATH_TENSORCORE, PATH_CUDACORE = 0, 1, 2
 ACT_NONE, ACT_GELU_TANH = 0, 1
 OK, EINVAL, EDEVICE = 0, -1, -2
@@ -58,6 +58,12 @@ SIGNATURES = {
                                         _int, _vp, _vp, _vp, _vp, _sz, _vp]),
     "reels_q8lora_backward_act": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _f,
                                          _int, _int, _vp, _vp, _vp, _vp, _int, _vp, _sz, _vp]),
+    "reels_q8lora_forward_dropout": (_int, [_vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f, _int,
+                                            _f, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _vp, _sz, _vp]),
+    "reels_q8lora_backward_dropout": (_int, [_vp, _vp, _vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f,
+                                             _f, _int, _f, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _vp, _int, _vp,
+                                             _sz, _vp]),
+    "reels_dropout_mask": (_int, [_i64, _f, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp]),
     "reels_opt_workspace_bytes": (_sz, [_int]),
     "reels_opt_prepare": (_int, [ctypes.POINTER(OptTensor), _int, _vp, _sz, _vp]),
     "reels_grad_norm_sq": (_int, [_vp, _f, _vp, _vp]),

@@ -59,6 +59,12 @@ __device__ __forceinline__ float load_act(const void *p, int64_t i, int dt) {
     if (dt == DT_F16) return __half2float(reinterpret_cast<const __half *>(p)[i]);
     return reinterpret_cast<const float *>(p)[i];
 }
+// v rounded to the element type dt (kept in fp32 form).
+__device__ __forceinline__ float round_dt(float v, int dt) {
+    if (dt == DT_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+    if (dt == DT_F16) return __half2float(__float2half_rn(v));
+    return v;
+}
 __device__ __forceinline__ void store_act(void *p, int64_t i, int dt, float v) {
     if (dt == DT_BF16) reinterpret_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
     else if (dt == DT_F16) reinterpret_cast<__half *>(p)[i] = __float2half_rn(v);

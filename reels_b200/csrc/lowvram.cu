@@ -16,6 +16,7 @@
 #include "aux_kernels.cuh"
 #include "q8_gemm.cuh"
 #include "q8_gemm_2sm.cuh"
+#include "dropout.cuh"
 #include "optim.cuh"
 #include "q8ts_gemm.cuh"
 
@@ -405,15 +406,17 @@ Split plan_sk(int64_t rows, int64_t red, int sms, int64_t r) {
 
 // Workspace layout shared by the forward and backward passes.
 struct Ws {
-    size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, part = 0, total = 0;
+    size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, zbuf = 0, part = 0, total = 0;
 };
 
 // Rank padding of the prepared LoRA operands: a multiple of the widest
 // pipeline stage (128 reduction elements).
 int64_t rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 128); }
 
-Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int sms) {
+Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags, int sms) {
     Ws w;
+    const int pass = pass_flags & 1;
+    const bool dropout = (pass_flags & REELS_PASS_DROPOUT) && r > 0;
     const int64_t ldm = ld_tokens(M);
     size_t off = 0;
     const size_t at_bytes = r > 0 ? align256((size_t)r * K * 2) : 0;
@@ -426,6 +429,8 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass, int s
     if (pass == REELS_PASS_BACKWARD) off += tg_bytes;
     w.ext = off;
     if (r > 0) off += align256((size_t)rank_pad(r) * std::max(N, K) * 2);
+    w.zbuf = off;  // the dropped-out adapter input z [M][K]
+    if (dropout) off += align256((size_t)M * K * esize(dt));
     size_t part = 0;
     const int64_t np = npad_of(r);
     auto sk_part = [&](int64_t rows, int64_t red) {
@@ -1120,10 +1125,23 @@ size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype) {
     return (size_t)r * ld_tokens(M) * esize(act_dtype);
 }
 
+static int check_dropout(float dropout, int64_t M) {
+    if (!(dropout >= 0.0f && dropout < 1.0f)) return fail("dropout must be in [0, 1)");
+    if (dropout > 0.0f && cdiv(M, DROP_TOK) > 65535) return fail("too many tokens for the dropout kernels");
+    return REELS_OK;
+}
+
+// z = dropout(x) into the workspace (lora.jl:71-83)
+static int launch_dropout_input(const void *x, int64_t n, int dt, float p, uint64_t key, void *z, cudaStream_t st) {
+    launch_pdl(dropout_input_kernel, dim3(launch_grid(n)), dim3(256), 0, st, x, n, dt, p, key, z);
+    REELS_LAUNCHED();
+    return REELS_OK;
+}
+
 static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
                                const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
-                               float alpha, int dt, int act, void *y, void *pre, void *saved, void *workspace,
-                               size_t ws_bytes, void *stream) {
+                               float alpha, int dt, int act, float dropout, uint64_t key, void *y, void *pre,
+                               void *saved, void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
     if (!x || !q || !scales || !y) return fail("null x, q, scales or y");
@@ -1131,11 +1149,14 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
     if (pre == y) return fail("pre and y must be different buffers");
     if (r > 0 && (!A || !B)) return fail("null LoRA A or B");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
+    rc = check_dropout(dropout, M);
+    if (rc) return rc;
     if (M == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
     rc = bind_device(x, &ds);
     if (rc) return rc;
-    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_FORWARD, ds->sms);
+    const bool drop = dropout > 0.0f && r > 0;
+    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_FORWARD | (drop ? REELS_PASS_DROPOUT : 0), ds->sms);
     rc = check_ws(workspace, ws_bytes, wl);
     if (rc) return rc;
     if (saved && !aligned16(saved)) return fail("saved buffer must be 16-byte aligned");
@@ -1144,10 +1165,17 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
     const float s = r > 0 ? alpha / (float)r : 0.0f;
     const int64_t ldm = ld_tokens(M);
     void *tbuf = r > 0 ? (saved ? saved : ws + wl.tbuf) : nullptr;
+    // The adapter's input: x, or with dropout z = x * keep / (1 - p).
+    const void *ax = x;
+    if (drop) {
+        rc = launch_dropout_input(x, M * K, dt, dropout, key, ws + wl.zbuf, st);
+        if (rc) return rc;
+        ax = ws + wl.zbuf;
+    }
 
     if (tc_eligible(K, N, dt, {x, q, y, B, saved})) {
         if (r > 0) {
-            rc = rank_down_tc(x, A, M, K, r, dt, tbuf, ws + wl.at, *ds, ws, wl, st);
+            rc = rank_down_tc(ax, A, M, K, r, dt, tbuf, ws + wl.at, *ds, ws, wl, st);
             if (rc) return rc;
         }
         Q8Call c{};
@@ -1175,7 +1203,7 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
         return ok(REELS_PATH_TENSORCORE);
     }
     if (r > 0) {
-        gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(x, A, M, K, (int)r, dt, tbuf, ldm);
+        gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(ax, A, M, K, (int)r, dt, tbuf, ldm);
         REELS_LAUNCHED();
     }
     void *lin = act != REELS_ACT_NONE && pre ? pre : y;  // the linear's output
@@ -1192,16 +1220,24 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
 int reels_q8lora_forward(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
                          const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r, float alpha,
                          int dt, void *y, void *saved, void *workspace, size_t ws_bytes, void *stream) {
-    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, dt, REELS_ACT_NONE, y, nullptr,
-                               saved, workspace, ws_bytes, stream);
+    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, dt, REELS_ACT_NONE, 0.0f, 0, y,
+                               nullptr, saved, workspace, ws_bytes, stream);
 }
 
 int reels_q8lora_forward_act(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
                              const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
                              float alpha, int act_dtype, int act, void *y, void *pre, void *saved, void *workspace,
                              size_t ws_bytes, void *stream) {
-    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, act_dtype, act, y, pre, saved,
-                               workspace, ws_bytes, stream);
+    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, act_dtype, act, 0.0f, 0, y, pre,
+                               saved, workspace, ws_bytes, stream);
+}
+
+int reels_q8lora_forward_dropout(const void *x, const int8_t *q, const float *scales, int layout, const void *A,
+                                 const void *B, const void *bias, int64_t M, int64_t K, int64_t N, int64_t r,
+                                 float alpha, int act_dtype, float dropout, uint64_t seed, uint64_t stream_id, void *y,
+                                 void *saved, void *workspace, size_t ws_bytes, void *stream) {
+    return q8lora_forward_impl(x, q, scales, layout, A, B, bias, M, K, N, r, alpha, act_dtype, REELS_ACT_NONE,
+                               dropout, dropout_key(seed, stream_id), y, nullptr, saved, workspace, ws_bytes, stream);
 }
 
 int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int layout, const void *bias, int64_t M,
@@ -1213,15 +1249,18 @@ int reels_q8_weight_mul(const void *x, const int8_t *q, const float *scales, int
 
 static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
                                 const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
-                                int64_t r, float alpha, float grad_scale, int dt, int act, const void *pre_x, void *dx,
-                                float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
-                                void *stream) {
+                                int64_t r, float alpha, float grad_scale, int dt, int act, const void *pre_x,
+                                float dropout, uint64_t key, void *dx, float *dA, float *dB, int accumulate,
+                                void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
     if (!dy || !q || !scales) return fail("null dy, q or scales");
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
     if (act != REELS_ACT_NONE && dx && !pre_x) return fail("null pre-activation of x");
     if (act != REELS_ACT_NONE && dx && pre_x == dx) return fail("pre_x and dx must be different buffers");
+    rc = check_dropout(dropout, M);
+    if (rc) return rc;
+    if (dropout > 0.0f && act != REELS_ACT_NONE) return fail("dropout is not combined with a fused activation");
     if (r > 0 && (!A || !B || !dA || !dB || !x)) return fail("null x, A, B, dA or dB with r > 0");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
     if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
@@ -1238,7 +1277,8 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
         }
         return ok(REELS_PATH_NONE);
     }
-    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_BACKWARD, ds->sms);
+    const bool drop = dropout > 0.0f && r > 0;
+    const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_BACKWARD | (drop ? REELS_PASS_DROPOUT : 0), ds->sms);
     rc = check_ws(workspace, ws_bytes, wl);
     if (rc) return rc;
     if (saved && !aligned16(saved)) return fail("saved buffer must be 16-byte aligned");
@@ -1247,11 +1287,36 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
     const int64_t ldm = ld_tokens(M);
     const void *tbuf = r > 0 ? (saved ? saved : (const void *)(ws + wl.tbuf)) : nullptr;
     void *gbuf = r > 0 ? (void *)(ws + wl.gbuf) : nullptr;
+    // The adapter's input of the forward: x, or with dropout z, recomputed
+    // from the same key (the mask is a function of the key and the index).
+    const void *ax = x;
+    if (drop) {
+        rc = launch_dropout_input(x, M * K, dt, dropout, key, ws + wl.zbuf, st);
+        if (rc) return rc;
+        ax = ws + wl.zbuf;
+    }
+    // With dropout the adapter's part of dx is masked, so the dx GEMM takes
+    // the frozen weight alone and dropout_dx_kernel adds that part.
+    auto add_dropout_dx = [&]() -> int {
+        const size_t smem = sizeof(float) * (size_t)r * DROP_TOK;
+        const dim3 grid((unsigned)cdiv(K, 256), (unsigned)cdiv(M, DROP_TOK));
+        if (dt == REELS_BF16)
+            launch_pdl(dropout_dx_kernel<DT_BF16>, grid, dim3(256), smem, st, A, (const void *)gbuf, ldm, M, K, (int)r,
+                       dropout, key, dx);
+        else if (dt == REELS_F16)
+            launch_pdl(dropout_dx_kernel<DT_F16>, grid, dim3(256), smem, st, A, (const void *)gbuf, ldm, M, K, (int)r,
+                       dropout, key, dx);
+        else
+            launch_pdl(dropout_dx_kernel<DT_F32>, grid, dim3(256), smem, st, A, (const void *)gbuf, ldm, M, K, (int)r,
+                       dropout, key, dx);
+        REELS_LAUNCHED();
+        return REELS_OK;
+    };
 
     if (tc_eligible(K, N, dt, {x, dy, q, dx, B, saved})) {
         if (r > 0) {
             if (!saved) {
-                rc = rank_down_tc(x, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st);
+                rc = rank_down_tc(ax, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st);
                 if (rc) return rc;
             }
             // g' = s * (B' * dy), stored [r][ldm]
@@ -1284,7 +1349,7 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             c.layout = layout;
             c.N_w = N;
             c.K_w = K;
-            c.r = r;
+            c.r = drop ? 0 : r;
             c.ext_act = gbuf;
             c.lora = A;
             c.ext_scale = 1.0f;
@@ -1295,11 +1360,15 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             c.pre = act == REELS_ACT_NONE ? nullptr : const_cast<void *>(pre_x);
             rc = run_q8(c, dt, *ds, ws, wl, st);
             if (rc) return rc;
+            if (drop) {
+                rc = add_dropout_dx();
+                if (rc) return rc;
+            }
         }
         if (r > 0) {
-            // dA[k][j] = grad_scale * sum_m g'[j][m] x[m][k]
+            // dA[k][j] = grad_scale * sum_m g'[j][m] z[m][k]  (z = x without dropout)
             SkCall da{};
-            da.act = x;
+            da.act = ax;
             da.act_inner = K;
             da.act_outer = M;
             da.a_mn = true;
@@ -1341,23 +1410,27 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
 
     if (r > 0) {
         if (!saved) {
-            gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(x, A, M, K, (int)r, dt, ws + wl.tbuf, ldm);
+            gen_rank_down_kernel<<<launch_grid(M * r), 256, 0, st>>>(ax, A, M, K, (int)r, dt, ws + wl.tbuf, ldm);
             REELS_LAUNCHED();
         }
         gen_rank_grad_kernel<<<launch_grid(M * r), 256, 0, st>>>(dy, B, M, N, (int)r, s, dt, gbuf, ldm);
         REELS_LAUNCHED();
     }
     if (dx) {
-        gen_dx_kernel<<<launch_grid(M * K), 256, 0, st>>>(dy, q, scales, layout, gbuf, ldm, A, M, K, N, (int)r, dt,
-                                                          dx);
+        gen_dx_kernel<<<launch_grid(M * K), 256, 0, st>>>(dy, q, scales, layout, gbuf, ldm, A, M, K, N,
+                                                          drop ? 0 : (int)r, dt, dx);
         REELS_LAUNCHED();
+        if (drop) {
+            rc = add_dropout_dx();
+            if (rc) return rc;
+        }
         if (act != REELS_ACT_NONE) {
             act_apply_kernel<<<launch_grid(M * K), 256, 0, st>>>(ACT_GELU_TANH_GRAD, dt, M * K, dx, pre_x);
             REELS_LAUNCHED();
         }
     }
     if (r > 0) {
-        gen_da_kernel<<<launch_grid(K * r), 256, 0, st>>>(gbuf, ldm, x, M, K, (int)r, grad_scale, accumulate, dt, dA);
+        gen_da_kernel<<<launch_grid(K * r), 256, 0, st>>>(gbuf, ldm, ax, M, K, (int)r, grad_scale, accumulate, dt, dA);
         REELS_LAUNCHED();
         gen_db_kernel<<<launch_grid(N * r), 256, 0, st>>>(dy, tbuf, ldm, M, N, (int)r, grad_scale * s, accumulate, dt,
                                                           dB);
@@ -1371,7 +1444,31 @@ int reels_q8lora_backward(const void *x, const void *dy, const int8_t *q, const 
                           float alpha, float grad_scale, int dt, void *dx, float *dA, float *dB, int accumulate,
                           void *workspace, size_t ws_bytes, void *stream) {
     return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, dt,
-                                REELS_ACT_NONE, nullptr, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+                                REELS_ACT_NONE, nullptr, 0.0f, 0, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+}
+
+int reels_q8lora_backward_dropout(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
+                                  const void *A, const void *B, const void *saved, int64_t M, int64_t K, int64_t N,
+                                  int64_t r, float alpha, float grad_scale, int act_dtype, float dropout, uint64_t seed,
+                                  uint64_t stream_id, void *dx, float *dA, float *dB, int accumulate, void *workspace,
+                                  size_t ws_bytes, void *stream) {
+    return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, act_dtype,
+                                REELS_ACT_NONE, nullptr, dropout, dropout_key(seed, stream_id), dx, dA, dB, accumulate,
+                                workspace, ws_bytes, stream);
+}
+
+int reels_dropout_mask(int64_t n, float dropout, uint64_t seed, uint64_t stream_id, uint8_t *keep, void *stream) {
+    if (n < 0) return fail("negative length");
+    if (!(dropout >= 0.0f && dropout < 1.0f)) return fail("dropout must be in [0, 1)");
+    if (n == 0) return ok(REELS_PATH_NONE);
+    if (!keep) return fail("null mask");
+    DeviceState *ds;
+    int rc = bind_device(keep, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dropout_mask_kernel<<<launch_grid(n), 256, 0, st>>>(n, dropout, dropout_key(seed, stream_id), keep);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
 }
 
 int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, const float *scales, int layout,
@@ -1380,7 +1477,7 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
                               void *dx, float *dA, float *dB, int accumulate, void *workspace, size_t ws_bytes,
                               void *stream) {
     return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, act_dtype, act,
-                                pre_x, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+                                pre_x, 0.0f, 0, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
 }
 
 size_t reels_opt_workspace_bytes(int count) {

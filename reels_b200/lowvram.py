@@ -295,8 +295,53 @@ def _colmajor(t: torch.Tensor, dtype) -> torch.Tensor:
 def lora_forward(layer: LoRALinear, x: torch.Tensor, training: bool = False, dropout_seed=None,
                  dropout_stream: int = 0, saved: Optional[torch.Tensor] = None) -> torch.Tensor:
     """lora_forward (lora.jl:56-95).  ``saved`` (optional uint8 buffer of
-    reels_q8lora_saved_bytes) receives A*x for :func:`lora_backward`."""
-    return _lora_forward(layer, x, training, saved, nat.ACT_NONE, False)[0]
+    reels_q8lora_saved_bytes) receives A*x for :func:`lora_backward`.
+
+    With ``training`` and ``layer.dropout > 0`` the adapter sees the dropped
+    out input (lora.jl:71-85).  The mask is a function of ``dropout_seed``
+    and ``dropout_stream`` (the reference's _dropout_seed); the backward
+    recomputes it from the same pair.  ``dropout_seed=None`` draws a seed
+    from torch's default generator, as the reference then uses its global
+    RNG; pass an explicit seed to be able to call :func:`lora_backward`."""
+    if training and layer.dropout > 0 and layer.enabled:
+        if dropout_seed is None:
+            dropout_seed = int(torch.randint(0, 2 ** 63 - 1, (1,)).item())
+        return _lora_forward_dropout(layer, x, saved, int(dropout_seed), int(dropout_stream))
+    return _lora_forward(layer, x, False, saved, nat.ACT_NONE, False)[0]
+
+
+def _u64(v: int) -> int:
+    return int(v) & 0xFFFFFFFFFFFFFFFF
+
+
+def _lora_forward_dropout(layer, x, saved, seed, stream):
+    N, K = layer.weight.shape
+    _require_cuda(x, layer.weight.values)
+    xf = _flat(x, K)
+    M = xf.shape[0]
+    dt = _dt(x.dtype)
+    b = layer.bias.contiguous().to(x.dtype) if layer.bias is not None else None
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    r = layer.rank
+    ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_FORWARD | nat.PASS_DROPOUT)
+    A_mem = _colmajor(layer.A, x.dtype)
+    B_mem = _colmajor(layer.B, x.dtype)
+    code = nat.lib().reels_q8lora_forward_dropout(
+        xf.data_ptr(), _wmem(layer.weight.values), layer.weight.scales.data_ptr(), layer.weight.layout,
+        A_mem.data_ptr(), B_mem.data_ptr(), _ptr(b), M, K, N, r, layer.alpha, dt, float(layer.dropout), _u64(seed),
+        _u64(stream), y.data_ptr(), _ptr(saved), ws, wsn, _stream(x.device))
+    nat.check("lora_forward", code)
+    return y.reshape(*x.shape[:-1], N)
+
+
+def dropout_mask(n: int, dropout: float, seed: int, stream: int = 0, device=None) -> torch.Tensor:
+    """The keep mask (uint8, 1 = kept) of the first ``n`` elements of an
+    adapter input for (seed, stream): the mask lora_forward applies."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    keep = torch.empty(max(n, 1), dtype=torch.uint8, device=dev)
+    nat.check("dropout_mask", nat.lib().reels_dropout_mask(n, float(dropout), _u64(seed), _u64(stream),
+                                                           keep.data_ptr(), _stream(dev)))
+    return keep[:n]
 
 
 def lora_forward_gelu(layer: LoRALinear, x: torch.Tensor, training: bool = False,
@@ -310,8 +355,8 @@ def lora_forward_gelu(layer: LoRALinear, x: torch.Tensor, training: bool = False
 
 
 def _lora_forward(layer, x, training, saved, act, keep_pre):
-    if training and layer.dropout > 0:
-        raise NotImplementedError("LoRA dropout is not implemented on the native int8 path")
+    if training and layer.dropout > 0 and layer.enabled:
+        raise NotImplementedError("LoRA dropout is not combined with the fused activation")
     N, K = layer.weight.shape
     _require_cuda(x, layer.weight.values)
     xf = _flat(x, K)
@@ -354,7 +399,8 @@ LoRAGradients = namedtuple("LoRAGradients", ["dx", "A", "B"])
 def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: Optional[torch.Tensor] = None,
                   grad_scale: float = 1.0, dA_acc: Optional[torch.Tensor] = None,
                   dB_acc: Optional[torch.Tensor] = None, need_dx: bool = True,
-                  x_pre: Optional[torch.Tensor] = None) -> LoRAGradients:
+                  x_pre: Optional[torch.Tensor] = None, dropout_seed: Optional[int] = None,
+                  dropout_stream: int = 0) -> LoRAGradients:
     """lora_backward (lora.jl:106-118) -> (dx, A=dA, B=dB).
 
     dA/dB are fp32 with the logical shapes of A and B (column-major).  With
@@ -364,7 +410,10 @@ def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: O
     ``x_pre``: when the input is an activation's output, x = gelu_tanh(x_pre)
     (the feed-forward output projection), the gradient is carried through the
     activation in the same pass and ``dx`` is the gradient with respect to
-    ``x_pre`` (Zygote's pullback of gelu_tanh, linear.jl:61-68)."""
+    ``x_pre`` (Zygote's pullback of gelu_tanh, linear.jl:61-68).
+
+    ``dropout_seed``: the gradients of a training forward with LoRA dropout
+    (``layer.dropout > 0``) run with that seed and ``dropout_stream``."""
     if tuple(x.shape[:-1]) != tuple(dy.shape[:-1]):
         raise ValueError("LoRA input and output trailing dimensions differ")
     N, K = layer.weight.shape
@@ -386,7 +435,17 @@ def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: O
         dB_mem = torch.empty((r, N), dtype=torch.float32, device=x.device)
     dx = torch.empty((M, K), dtype=x.dtype, device=x.device) if need_dx else None
     ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_BACKWARD)
-    if x_pre is not None:
+    drop = dropout_seed is not None and layer.dropout > 0
+    if drop and x_pre is not None:
+        raise ValueError("dropout is not combined with a fused activation")
+    if drop:
+        ws, wsn = _workspace(x.device, M, K, N, r, dt, nat.PASS_BACKWARD | nat.PASS_DROPOUT)
+        code = nat.lib().reels_q8lora_backward_dropout(
+            xf.data_ptr(), dyf.data_ptr(), _wmem(layer.weight.values), layer.weight.scales.data_ptr(),
+            layer.weight.layout, A_mem.data_ptr(), B_mem.data_ptr(), _ptr(saved), M, K, N, r, layer.alpha,
+            float(grad_scale), dt, float(layer.dropout), _u64(dropout_seed), _u64(dropout_stream), _ptr(dx),
+            dA_mem.data_ptr(), dB_mem.data_ptr(), 1 if accumulate else 0, ws, wsn, _stream(x.device))
+    elif x_pre is not None:
         if tuple(x_pre.shape) != tuple(x.shape) or x_pre.dtype != x.dtype:
             raise ValueError("x_pre must have the shape and dtype of x")
         xp = _flat(x_pre, K)
@@ -433,18 +492,24 @@ class LoRALinearFunction(torch.autograd.Function):
     (ad_rules.jl:70-80) plus Zygote's adjoints of B*(A*x)."""
 
     @staticmethod
-    def forward(ctx, x, A, B, layer):
+    def forward(ctx, x, A, B, layer, training=False, dropout_seed=None, dropout_stream=0):
         saved = saved_buffer(layer, x)
-        y = lora_forward(layer, x, saved=saved)
+        drop = training and layer.dropout > 0 and layer.enabled
+        if drop and dropout_seed is None:
+            dropout_seed = int(torch.randint(0, 2 ** 63 - 1, (1,)).item())
+        y = lora_forward(layer, x, training=training, dropout_seed=dropout_seed, dropout_stream=dropout_stream,
+                         saved=saved)
         ctx.layer = layer
+        ctx.dropout = (dropout_seed, dropout_stream) if drop else (None, 0)
         ctx.save_for_backward(x, saved)
         return y
 
     @staticmethod
     def backward(ctx, dy):
         x, saved = ctx.saved_tensors
-        g = lora_backward(ctx.layer, x, dy.contiguous(), saved=saved)
-        return g.dx, g.A.to(ctx.layer.A.dtype), g.B.to(ctx.layer.B.dtype), None
+        seed, stream = ctx.dropout
+        g = lora_backward(ctx.layer, x, dy.contiguous(), saved=saved, dropout_seed=seed, dropout_stream=stream)
+        return g.dx, g.A.to(ctx.layer.A.dtype), g.B.to(ctx.layer.B.dtype), None, None, None, None
 
 
 class GeluFeedForwardFunction(torch.autograd.Function):

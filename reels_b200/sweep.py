@@ -2,6 +2,7 @@
 
     python -m reels_b200.sweep [--N 13824 --K 5120] [--tokens 128,512,...]
                                [--ranks 8,64] [--dtype f16] [--loss-scale 1024]
+                               [--dropout P]
 
 Defaults are the bandwidth-bound sweep on the Wan-2.1-14B FFN up-projection
 (W 13824 x 5120, int8 per output row; fp16 activations; dY carries a static
@@ -21,6 +22,11 @@ dW is not computed, the weight is frozen), 4*M*N*K, and the six rank-r
 products (T, the adapter term of Y, G, that of dX, dA, dB), 2*M*r*(3K + 3N).  Algorithmic bytes:
 what must cross HBM at least once per pass -- forward: x, W (int8 + scales),
 y; backward: dy, W, x (for dA), dx; the rank-r tensors are counted too.
+
+--dropout P runs the training forward and backward with LoRA dropout
+(reels_q8lora_forward_dropout / _backward_dropout): the same algorithmic
+FLOPs and bytes, plus the dropped-out input's pass and the masked adapter
+part of dx, which the figures then include as overhead.
 """
 from __future__ import annotations
 
@@ -55,6 +61,7 @@ def main():
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     ap.add_argument("--loss-scale", type=float, default=1024.0)
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--dropout", type=float, default=0.0)
     a = ap.parse_args()
     native_build.build()
     L = nat.lib()
@@ -81,15 +88,27 @@ def main():
             dx = torch.empty((M, K), device=dev, dtype=tdt)
             saved = torch.empty((max(L.reels_q8lora_saved_bytes(M, r, dt), 16),), dtype=torch.uint8, device=dev)
             grad = torch.zeros((r * (K + N),), dtype=torch.float32, device=dev)
-            wsn = max(L.reels_q8lora_workspace_bytes(M, K, N, r, dt, p) for p in (0, 1))
+            flag = nat.PASS_DROPOUT if a.dropout > 0 else 0
+            wsn = max(L.reels_q8lora_workspace_bytes(M, K, N, r, dt, p | flag) for p in (0, 1))
             ws = torch.empty((max(wsn, 256),), dtype=torch.uint8, device=dev)
 
             def fwd():
+                if a.dropout > 0:
+                    nat.check("forward", L.reels_q8lora_forward_dropout(
+                        x.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(), None, M, K, N, r,
+                        alpha, dt, a.dropout, 1, 0, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, st))
+                    return
                 nat.check("forward", L.reels_q8lora_forward(
                     x.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(), None, M, K, N, r, alpha,
                     dt, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, st))
 
             def bwd():
+                if a.dropout > 0:
+                    nat.check("backward", L.reels_q8lora_backward_dropout(
+                        x.data_ptr(), dy.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(),
+                        saved.data_ptr(), M, K, N, r, alpha, 1.0 / a.loss_scale, dt, a.dropout, 1, 0, dx.data_ptr(),
+                        grad.data_ptr(), grad.data_ptr() + 4 * K * r, 0, ws.data_ptr(), wsn, st))
+                    return
                 nat.check("backward", L.reels_q8lora_backward(
                     x.data_ptr(), dy.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(),
                     saved.data_ptr(), M, K, N, r, alpha, 1.0 / a.loss_scale, dt, dx.data_ptr(), grad.data_ptr(),
@@ -118,6 +137,7 @@ def main():
             tfl = flops / (us * 1e-6) / 1e12
             print(json.dumps({
                 "shape": f"W {N}x{K}", "tokens": M, "rank": r, "dtype": a.dtype, "loss_scale": a.loss_scale,
+                "dropout": a.dropout,
                 "us_fwd": round(res["fwd"], 1), "us_bwd": round(res["bwd"], 1), "us": round(us, 1),
                 "tflops": round(tfl, 1), "tensor_frac": round(tfl / tf_peak, 3),
                 "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3),
