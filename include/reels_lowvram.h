@@ -246,6 +246,51 @@ int reels_q8lora_backward_dropout(const void *x, const void *dy, const int8_t *q
  * is kept, 0 where dropped, for i < n (n = M * K, i = token * K + feature). */
 int reels_dropout_mask(int64_t n, float dropout, uint64_t seed, uint64_t stream_id, uint8_t *keep, void *stream);
 
+/* The linears' input producer of the Wan block,
+ *   out = mixed_affine(layernorm(x; epsilon, ln_weight, ln_bias), scale, shift)
+ * (src/layers/linear.jl:26-36,49-59, called at
+ * src/models/wan21/transformer.jl:287-289), one pass per row of x [M][K]:
+ * mean and variance in fp32, y = (x - mean) / sqrt(var + epsilon)
+ * (* ln_weight) (+ ln_bias) rounded to act_dtype, then
+ * round(y * (1 + scale[b]) + shift[b]) with b = token / tokens_per_sample.
+ * scale and shift are [batch][K] (the per-sample modulation, AdaLN); any of
+ * scale, shift, ln_weight, ln_bias may be NULL.  K <= 16384. */
+int reels_layernorm_modulate(const void *x, int64_t M, int64_t K, int64_t tokens_per_sample, const void *scale,
+                             const void *shift, const void *ln_weight, const void *ln_bias, float epsilon,
+                             int act_dtype, void *out, void *stream);
+
+/* Workspace of reels_layernorm_modulate_backward when the parameter
+ * gradients are requested. */
+size_t reels_layernorm_modulate_workspace_bytes(int64_t M, int64_t K, int64_t tokens_per_sample);
+
+/* Its pullback for dout [M][K]: dx (required), and optionally the modulation's
+ * parameter gradients (modulation.jl:13-22) as fp32 [batch][K]:
+ *   dscale[b] = sum over the sample's tokens of dout * ln,  dshift[b] = sum dout
+ * (overwritten, or added with accumulate = 1), in a fixed summation order.
+ * The LayerNorm's own weight and bias receive no gradient (frozen). */
+int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M, int64_t K,
+                                      int64_t tokens_per_sample, const void *scale, const void *ln_weight,
+                                      const void *ln_bias, float epsilon, int act_dtype, void *dx, float *dscale,
+                                      float *dshift, int accumulate, void *workspace, size_t ws_bytes, void *stream);
+
+/* The gated residual after a block's output projection (transformer.jl:272,
+ * 293): out = mixed_add(x, mixed_mul(y, gate[b])) = round(x + round(y * gate[b]))
+ * per element of [M][N], b = token / tokens_per_sample, gate [batch][N].
+ * out may be x (the residual stream updated in place). */
+int reels_gated_residual(const void *x, const void *y, const void *gate, int64_t M, int64_t N,
+                         int64_t tokens_per_sample, int act_dtype, void *out, void *stream);
+
+/* Workspace of reels_gated_residual_backward when dgate is requested. */
+size_t reels_gated_residual_workspace_bytes(int64_t M, int64_t N, int64_t tokens_per_sample);
+
+/* Its pullback for dout: the residual's gradient is dout itself; dy (nullable)
+ * = round(dout * gate[b]); dgate (nullable, fp32 [batch][N], overwritten or
+ * with accumulate = 1 added) = the sample's sum of dout * y, in a fixed
+ * order. */
+int reels_gated_residual_backward(const void *dout, const void *y, const void *gate, int64_t M, int64_t N,
+                                  int64_t tokens_per_sample, int act_dtype, void *dy, float *dgate, int accumulate,
+                                  void *workspace, size_t ws_bytes, void *stream);
+
 /* ---------------------------------------------------------------------
  * The optimizer step after the gradient all-reduce (src/training/
  * wan_runner.jl:213-227 and AdamW update!, src/training/optimizer.jl:48-73),

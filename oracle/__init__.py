@@ -71,6 +71,9 @@ def lib():
                                              _i64, _i64, _i64, _i64, ctypes.c_float, vp, vp, vp]
         L.oracle_dropout_keep.argtypes = [_i64, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64,
                                           np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")]
+        L.oracle_layernorm.argtypes = [_f32p, _i64, _i64, ctypes.c_float, vp, vp, _f32p]
+        L.oracle_modulate.argtypes = [_f32p, _i64, _i64, _i64, vp, vp, _f32p]
+        L.oracle_layernorm_backward.argtypes = [_f32p, _f32p, _i64, _i64, ctypes.c_float, vp, _f32p]
         L.oracle_rel_l2.argtypes = [_f32p, _f32p, _i64]
         L.oracle_rel_l2.restype = ctypes.c_double
         _LIB = L
@@ -258,6 +261,43 @@ def lora_dropout(X, Z, dY, q, scales, layout, A, B, alpha, dscale, bias=None):
     lib().oracle_lora_backward_z(X, Z.ctypes.data, dscale.ctypes.data, dY, q, scales, layout, A, B, M, K, N, r,
                                  float(alpha), dX.ctypes.data, dA.ctypes.data, dB.ctypes.data)
     return Y, dX, dA, dB
+
+
+def _ptr_or_none(a):
+    return None if a is None else _c(a, np.float32).ctypes.data
+
+
+def layernorm(X, eps, w=None, b=None):
+    """layernorm (src/layers/linear.jl:49-59) in fp32, unrounded."""
+    X = _c(X, np.float32)
+    M, K = X.shape
+    Y = np.empty_like(X)
+    w = None if w is None else _c(w, np.float32)
+    b = None if b is None else _c(b, np.float32)
+    lib().oracle_layernorm(X, M, K, eps, _ptr_or_none(w), _ptr_or_none(b), Y)
+    return Y
+
+
+def modulate(LN, tps, scale=None, shift=None):
+    """mixed_affine's fp32 part (linear.jl:26-36), unrounded; scale/shift [batch][K]."""
+    LN = _c(LN, np.float32)
+    M, K = LN.shape
+    out = np.empty_like(LN)
+    scale = None if scale is None else _c(scale, np.float32)
+    shift = None if shift is None else _c(shift, np.float32)
+    lib().oracle_modulate(LN, M, K, tps, _ptr_or_none(scale), _ptr_or_none(shift), out)
+    return out
+
+
+def layernorm_backward(X, G, eps, w=None):
+    """The LayerNorm's pullback (fp64) for the gradient G at its output."""
+    X = _c(X, np.float32)
+    G = _c(G, np.float32)
+    M, K = X.shape
+    DX = np.empty_like(X)
+    w = None if w is None else _c(w, np.float32)
+    lib().oracle_layernorm_backward(X, G, M, K, eps, _ptr_or_none(w), DX)
+    return DX
 
 
 def rel_l2(a, b) -> float:

@@ -348,6 +348,80 @@ double oracle_sumsq(const float *g, int64_t n, float gs)
     return s;
 }
 
+/* mixed_affine(layernorm(x; eps, w, b), scale, shift) (src/layers/linear.jl:
+ * 26-36,49-59) per row of X [M][K]; sample = row / tps.  The mean and the
+ * variance are summed in fp64 and rounded to fp32 (the reference sums in fp32
+ * in its reduction's order); the rest is the reference's fp32 sequence:
+ *   y = (x - mean) / sqrt(var + eps) (* w) (+ b)   -> LN (the caller rounds)
+ * Out receives y; the caller rounds it to the element type, then forms
+ * round(ln * (1 + scale) + shift) with oracle_modulate. */
+void oracle_layernorm(const float *X, int64_t M, int64_t K, float eps, const float *w, const float *b, float *Y)
+{
+    for (int64_t m = 0; m < M; ++m) {
+        const float *x = X + m * K;
+        double s = 0.0;
+        for (int64_t k = 0; k < K; ++k) s += x[k];
+        const float mean = (float)s / (float)K;
+        double q = 0.0;
+        for (int64_t k = 0; k < K; ++k) {
+            const float c = x[k] - mean;
+            q += (double)c * (double)c;
+        }
+        const float var = (float)q / (float)K;
+        const float d = sqrtf(var + eps);
+        for (int64_t k = 0; k < K; ++k) {
+            float y = (x[k] - mean) / d;
+            if (w) y = y * w[k];
+            if (b) y = y + b[k];
+            Y[m * K + k] = y;
+        }
+    }
+}
+
+/* mixed_affine's fp32 part: ln * (1 + scale[b]) + shift[b]. */
+void oracle_modulate(const float *LN, int64_t M, int64_t K, int64_t tps, const float *scale, const float *shift,
+                     float *Out)
+{
+    for (int64_t m = 0; m < M; ++m) {
+        const int64_t b = m / tps;
+        for (int64_t k = 0; k < K; ++k) {
+            float v = LN[m * K + k];
+            if (scale) v = v * (1.0f + scale[b * K + k]);
+            if (shift) v = v + shift[b * K + k];
+            Out[m * K + k] = v;
+        }
+    }
+}
+
+/* The LayerNorm's pullback in fp64 from G = the gradient reaching its
+ * (rounded) output, per row: with yhat = (x - mean)/d and gw = G * w,
+ *   dx = (gw - mean(gw) - yhat * mean(gw * yhat)) / d. */
+void oracle_layernorm_backward(const float *X, const float *G, int64_t M, int64_t K, float eps, const float *w,
+                               float *DX)
+{
+    for (int64_t m = 0; m < M; ++m) {
+        const float *x = X + m * K;
+        double s = 0.0;
+        for (int64_t k = 0; k < K; ++k) s += x[k];
+        const double mean = s / (double)K;
+        double q = 0.0;
+        for (int64_t k = 0; k < K; ++k) q += (x[k] - mean) * (x[k] - mean);
+        const double d = sqrt(q / (double)K + (double)eps);
+        double s1 = 0.0, s2 = 0.0;
+        for (int64_t k = 0; k < K; ++k) {
+            const double gw = (double)G[m * K + k] * (w ? (double)w[k] : 1.0);
+            s1 += gw;
+            s2 += gw * (x[k] - mean) / d;
+        }
+        s1 /= (double)K;
+        s2 /= (double)K;
+        for (int64_t k = 0; k < K; ++k) {
+            const double gw = (double)G[m * K + k] * (w ? (double)w[k] : 1.0);
+            DX[m * K + k] = (float)((gw - s1 - (x[k] - mean) / d * s2) / d);
+        }
+    }
+}
+
 /* Relative L2 error ||a - b|| / ||b|| in fp64 (the north-star metric). */
 double oracle_rel_l2(const float *a, const float *b, int64_t n)
 {

@@ -7,12 +7,17 @@ package is the Python-side mirror of the reference's layer API
 """
 from .lowvram import (  # noqa: F401
     DenseLayer,
+    LayerNormModulateFunction,
     GeluFeedForwardFunction,
     LoRALinear,
     LoRALinearFunction,
     QuantizedMatrix,
     check_device_status,
     dropout_mask,
+    gated_residual,
+    gated_residual_backward,
+    layernorm_modulate,
+    layernorm_modulate_backward,
     linear,
     lora_backward,
     lora_forward,

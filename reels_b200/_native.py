@@ -64,6 +64,13 @@ SIGNATURES = {
                                              _f, _int, _f, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _vp, _int, _vp,
                                              _sz, _vp]),
     "reels_dropout_mask": (_int, [_i64, _f, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp]),
+    "reels_layernorm_modulate": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _f, _int, _vp, _vp]),
+    "reels_layernorm_modulate_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "reels_layernorm_modulate_backward": (_int, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _f, _int, _vp, _vp, _vp,
+                                                 _int, _vp, _sz, _vp]),
+    "reels_gated_residual": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp]),
+    "reels_gated_residual_workspace_bytes": (_sz, [_i64, _i64, _i64]),
+    "reels_gated_residual_backward": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _int, _vp, _sz, _vp]),
     "reels_opt_workspace_bytes": (_sz, [_int]),
     "reels_opt_prepare": (_int, [ctypes.POINTER(OptTensor), _int, _vp, _sz, _vp]),
     "reels_grad_norm_sq": (_int, [_vp, _f, _vp, _vp]),

@@ -17,6 +17,7 @@
 #include "q8_gemm.cuh"
 #include "q8_gemm_2sm.cuh"
 #include "dropout.cuh"
+#include "norm.cuh"
 #include "optim.cuh"
 #include "q8ts_gemm.cuh"
 
@@ -176,6 +177,10 @@ int bind_device(const void *ptr, DeviceState **out) {
         REELS_CUDA(set_q8_attrs<DT_F16>());
         REELS_CUDA(set_ts_attrs<DT_BF16>());
         REELS_CUDA(set_ts_attrs<DT_F16>());
+        for (auto fn : {(const void *)ln_modulate_kernel<DT_BF16>, (const void *)ln_modulate_kernel<DT_F16>,
+                        (const void *)ln_modulate_kernel<DT_F32>, (const void *)ln_modulate_bwd_kernel<DT_BF16>,
+                        (const void *)ln_modulate_bwd_kernel<DT_F16>, (const void *)ln_modulate_bwd_kernel<DT_F32>})
+            REELS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * LN_MAX_K * 4));
         REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         Q8PairGeom::SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -997,6 +1002,14 @@ int rank_down_tc(const void *x, const void *A, int64_t M, int64_t K, int64_t r, 
 
 }  // namespace
 
+// Calls f with the element type as a compile-time constant.
+template <typename F>
+void dispatch_dt(int dt, F &&f) {
+    if (dt == REELS_BF16) f(std::integral_constant<int, DT_BF16>{});
+    else if (dt == REELS_F16) f(std::integral_constant<int, DT_F16>{});
+    else f(std::integral_constant<int, DT_F32>{});
+}
+
 // =====================================================================
 extern "C" {
 
@@ -1478,6 +1491,192 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
                               void *stream) {
     return q8lora_backward_impl(x, dy, q, scales, layout, A, B, saved, M, K, N, r, alpha, grad_scale, act_dtype, act,
                                 pre_x, 0.0f, 0, dx, dA, dB, accumulate, workspace, ws_bytes, stream);
+}
+
+static int check_ln(const void *x, int64_t M, int64_t K, int64_t tps, float eps, int dt) {
+    if (!x) return fail("null x");
+    if (M < 0 || K <= 0 || K > LN_MAX_K) return fail("LayerNorm needs 0 <= M and 0 < K <= " + std::to_string(LN_MAX_K));
+    if (tps <= 0) return fail("tokens_per_sample must be positive");
+    if (!(eps >= 0.0f) || !std::isfinite(eps)) return fail("epsilon must be finite and non-negative");
+    if (dt != REELS_F32 && dt != REELS_F16 && dt != REELS_BF16) return fail("unknown act_dtype");
+    return REELS_OK;
+}
+
+static int64_t ln_chunks(int64_t tps) { return cdiv(tps, LN_COL_ROWS); }
+
+size_t reels_layernorm_modulate_workspace_bytes(int64_t M, int64_t K, int64_t tokens_per_sample) {
+    if (M < 0 || K <= 0 || tokens_per_sample <= 0) return 0;
+    const int64_t batch = cdiv(M, tokens_per_sample);
+    return align256((size_t)M * 8) + align256((size_t)batch * ln_chunks(tokens_per_sample) * 2 * K * 4);
+}
+
+int reels_layernorm_modulate(const void *x, int64_t M, int64_t K, int64_t tokens_per_sample, const void *scale,
+                             const void *shift, const void *ln_weight, const void *ln_bias, float epsilon, int dt,
+                             void *out, void *stream) {
+    int rc = check_ln(x, M, K, tokens_per_sample, epsilon, dt);
+    if (rc) return rc;
+    if (!out) return fail("null out");
+    if (M == 0) return ok(REELS_PATH_NONE);
+    DeviceState *ds;
+    rc = bind_device(x, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const dim3 grid((unsigned)std::min<int64_t>(M, 16LL * ds->sms));
+    const size_t smem = (size_t)K * 4;
+    if (dt == REELS_BF16)
+        launch_pdl(ln_modulate_kernel<DT_BF16>, grid, dim3(LN_THREADS), smem, st, x, M, K, tokens_per_sample, scale,
+                   shift, ln_weight, ln_bias, epsilon, out);
+    else if (dt == REELS_F16)
+        launch_pdl(ln_modulate_kernel<DT_F16>, grid, dim3(LN_THREADS), smem, st, x, M, K, tokens_per_sample, scale,
+                   shift, ln_weight, ln_bias, epsilon, out);
+    else
+        launch_pdl(ln_modulate_kernel<DT_F32>, grid, dim3(LN_THREADS), smem, st, x, M, K, tokens_per_sample, scale,
+                   shift, ln_weight, ln_bias, epsilon, out);
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
+}
+
+int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M, int64_t K,
+                                      int64_t tokens_per_sample, const void *scale, const void *ln_weight,
+                                      const void *ln_bias, float epsilon, int dt, void *dx, float *dscale,
+                                      float *dshift, int accumulate, void *workspace, size_t ws_bytes,
+                                      void *stream) {
+    int rc = check_ln(x, M, K, tokens_per_sample, epsilon, dt);
+    if (rc) return rc;
+    if (!dout) return fail("null dout");
+    const bool params = dscale || dshift;
+    if (!dx && !params) return ok(REELS_PATH_NONE);
+    const int64_t batch = cdiv(M, tokens_per_sample);
+    if (params) {
+        if (!workspace) return fail("null workspace; size it with reels_layernorm_modulate_workspace_bytes");
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("workspace must be 256-byte aligned");
+        if (ws_bytes < reels_layernorm_modulate_workspace_bytes(M, K, tokens_per_sample))
+            return fail("workspace too small");
+    }
+    DeviceState *ds;
+    rc = bind_device(x, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (M == 0) {
+        if (params && !accumulate) {
+            if (dscale) REELS_CUDA(cudaMemsetAsync(dscale, 0, sizeof(float) * batch * K, st));
+            if (dshift) REELS_CUDA(cudaMemsetAsync(dshift, 0, sizeof(float) * batch * K, st));
+        }
+        return ok(REELS_PATH_NONE);
+    }
+    float2 *stats = params ? reinterpret_cast<float2 *>(workspace) : nullptr;
+    float *part = params ? reinterpret_cast<float *>(reinterpret_cast<char *>(workspace) + align256((size_t)M * 8))
+                         : nullptr;
+    const dim3 grid((unsigned)std::min<int64_t>(M, 16LL * ds->sms));
+    const size_t smem = (size_t)K * 8;
+    // dx (and the row statistics); without dx the rows still run for the statistics
+    void *dxo = dx;
+    if (!dx) return fail("dx is required (the parameter gradients reuse its row statistics)");
+    if (dt == REELS_BF16)
+        launch_pdl(ln_modulate_bwd_kernel<DT_BF16>, grid, dim3(LN_THREADS), smem, st, x, dout, M, K,
+                   tokens_per_sample, scale, ln_weight, epsilon, dxo, stats);
+    else if (dt == REELS_F16)
+        launch_pdl(ln_modulate_bwd_kernel<DT_F16>, grid, dim3(LN_THREADS), smem, st, x, dout, M, K,
+                   tokens_per_sample, scale, ln_weight, epsilon, dxo, stats);
+    else
+        launch_pdl(ln_modulate_bwd_kernel<DT_F32>, grid, dim3(LN_THREADS), smem, st, x, dout, M, K,
+                   tokens_per_sample, scale, ln_weight, epsilon, dxo, stats);
+    REELS_LAUNCHED();
+    if (params) {
+        const int64_t cps = ln_chunks(tokens_per_sample);
+        if (batch * cps > 65535) return fail("too many token blocks for the parameter reduction");
+        const dim3 pg((unsigned)cdiv(K, LN_THREADS), (unsigned)(batch * cps));
+        if (dt == REELS_BF16)
+            launch_pdl(ln_param_partial_kernel<DT_BF16>, pg, dim3(LN_THREADS), 0, st, x, dout, (const float2 *)stats,
+                       M, K, tokens_per_sample, ln_weight, ln_bias, cps, part);
+        else if (dt == REELS_F16)
+            launch_pdl(ln_param_partial_kernel<DT_F16>, pg, dim3(LN_THREADS), 0, st, x, dout, (const float2 *)stats, M,
+                       K, tokens_per_sample, ln_weight, ln_bias, cps, part);
+        else
+            launch_pdl(ln_param_partial_kernel<DT_F32>, pg, dim3(LN_THREADS), 0, st, x, dout, (const float2 *)stats, M,
+                       K, tokens_per_sample, ln_weight, ln_bias, cps, part);
+        REELS_LAUNCHED();
+        launch_pdl(ln_param_final_kernel, dim3(launch_grid(batch * K)), dim3(256), 0, st, (const float *)part, K, batch,
+                   cps, accumulate, dscale, dshift);
+        REELS_LAUNCHED();
+    }
+    return ok(REELS_PATH_CUDACORE);
+}
+
+static int check_gate(int64_t M, int64_t N, int64_t tps, int dt) {
+    if (M < 0 || N <= 0) return fail("gated residual needs 0 <= M and 0 < N");
+    if (tps <= 0) return fail("tokens_per_sample must be positive");
+    if (dt != REELS_F32 && dt != REELS_F16 && dt != REELS_BF16) return fail("unknown act_dtype");
+    return REELS_OK;
+}
+
+int reels_gated_residual(const void *x, const void *y, const void *gate, int64_t M, int64_t N,
+                         int64_t tokens_per_sample, int dt, void *out, void *stream) {
+    int rc = check_gate(M, N, tokens_per_sample, dt);
+    if (rc) return rc;
+    if (!x || !y || !gate || !out) return fail("null x, y, gate or out");
+    if (M == 0) return ok(REELS_PATH_NONE);
+    DeviceState *ds;
+    rc = bind_device(x, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dispatch_dt(dt, [&](auto d) {
+        launch_pdl(gated_residual_kernel<decltype(d)::value>, dim3(launch_grid(M * N)), dim3(256), 0, st, x, y, gate,
+                   M, N, tokens_per_sample, out);
+    });
+    REELS_LAUNCHED();
+    return ok(REELS_PATH_CUDACORE);
+}
+
+size_t reels_gated_residual_workspace_bytes(int64_t M, int64_t N, int64_t tokens_per_sample) {
+    if (M < 0 || N <= 0 || tokens_per_sample <= 0) return 0;
+    return align256((size_t)cdiv(M, tokens_per_sample) * ln_chunks(tokens_per_sample) * N * 4);
+}
+
+int reels_gated_residual_backward(const void *dout, const void *y, const void *gate, int64_t M, int64_t N,
+                                  int64_t tokens_per_sample, int dt, void *dy, float *dgate, int accumulate,
+                                  void *workspace, size_t ws_bytes, void *stream) {
+    int rc = check_gate(M, N, tokens_per_sample, dt);
+    if (rc) return rc;
+    if (!dout || !gate) return fail("null dout or gate");
+    if (dgate && !y) return fail("dgate needs y");
+    if (dgate) {
+        if (!workspace) return fail("null workspace; size it with reels_gated_residual_workspace_bytes");
+        if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("workspace must be 256-byte aligned");
+        if (ws_bytes < reels_gated_residual_workspace_bytes(M, N, tokens_per_sample)) return fail("workspace too small");
+    }
+    if (!dy && !dgate) return ok(REELS_PATH_NONE);
+    DeviceState *ds;
+    rc = bind_device(dout, &ds);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int64_t batch = cdiv(M, tokens_per_sample);
+    if (M == 0) {
+        if (dgate && !accumulate) REELS_CUDA(cudaMemsetAsync(dgate, 0, sizeof(float) * batch * N, st));
+        return ok(REELS_PATH_NONE);
+    }
+    if (dy) {
+        dispatch_dt(dt, [&](auto d) {
+            launch_pdl(gated_residual_dy_kernel<decltype(d)::value>, dim3(launch_grid(M * N)), dim3(256), 0, st, dout,
+                       gate, M, N, tokens_per_sample, dy);
+        });
+        REELS_LAUNCHED();
+    }
+    if (dgate) {
+        const int64_t cps = ln_chunks(tokens_per_sample);
+        if (batch * cps > 65535) return fail("too many token blocks for the gate reduction");
+        float *part = reinterpret_cast<float *>(workspace);
+        const dim3 pg((unsigned)cdiv(N, LN_THREADS), (unsigned)(batch * cps));
+        dispatch_dt(dt, [&](auto d) {
+            launch_pdl(gate_grad_partial_kernel<decltype(d)::value>, pg, dim3(LN_THREADS), 0, st, dout, y, M, N,
+                       tokens_per_sample, cps, part);
+        });
+        REELS_LAUNCHED();
+        launch_pdl(gate_grad_final_kernel, dim3(launch_grid(batch * N)), dim3(256), 0, st, (const float *)part, N,
+                   batch, cps, accumulate, dgate);
+        REELS_LAUNCHED();
+    }
+    return ok(REELS_PATH_CUDACORE);
 }
 
 size_t reels_opt_workspace_bytes(int count) {

@@ -536,3 +536,120 @@ class GeluFeedForwardFunction(torch.autograd.Function):
         g_in = lora_backward(ffn_in, x, g_out.dx, saved=saved_in)
         return (g_in.dx, g_in.A.to(ffn_in.A.dtype), g_in.B.to(ffn_in.B.dtype), g_out.A.to(ffn_out.A.dtype),
                 g_out.B.to(ffn_out.B.dtype), None, None)
+
+
+# ------------------------------------------------------- norm + modulation
+def layernorm_modulate(x: torch.Tensor, scale: Optional[torch.Tensor] = None, shift: Optional[torch.Tensor] = None,
+                       epsilon: float = 1e-6, weight: Optional[torch.Tensor] = None,
+                       bias: Optional[torch.Tensor] = None, tokens_per_sample: Optional[int] = None) -> torch.Tensor:
+    """``mixed_affine(layernorm(x; epsilon, weight, bias), scale, shift)``
+    (linear.jl:26-36,49-59) in one pass per token: the input of the Wan
+    block's linears (transformer.jl:287-289).  ``x`` is (..., K); ``scale``
+    and ``shift`` are (batch, K), sample b covering ``tokens_per_sample``
+    consecutive tokens (default: all tokens, batch 1)."""
+    K = x.shape[-1]
+    _require_cuda(x)
+    xf = _flat(x, K)
+    M = xf.shape[0]
+    tps = M if tokens_per_sample is None else int(tokens_per_sample)
+    out = torch.empty_like(xf)
+    args = [t.contiguous().to(x.dtype) if t is not None else None for t in (scale, shift, weight, bias)]
+    code = nat.lib().reels_layernorm_modulate(xf.data_ptr(), M, K, max(tps, 1), *[_ptr(t) for t in args],
+                                              float(epsilon), _dt(x.dtype), out.data_ptr(), _stream(x.device))
+    nat.check("layernorm_modulate", code)
+    return out.reshape(x.shape)
+
+
+def layernorm_modulate_backward(x: torch.Tensor, dout: torch.Tensor, scale: Optional[torch.Tensor] = None,
+                                epsilon: float = 1e-6, weight: Optional[torch.Tensor] = None,
+                                bias: Optional[torch.Tensor] = None, tokens_per_sample: Optional[int] = None,
+                                param_grads: bool = False):
+    """Pullback of :func:`layernorm_modulate`: ``dx``, and with
+    ``param_grads`` the fp32 gradients of ``scale`` and ``shift``
+    (modulation.jl:13-22), as ``(dx, dscale, dshift)``."""
+    K = x.shape[-1]
+    _require_cuda(x, dout)
+    xf = _flat(x, K)
+    df = _flat(dout, K)
+    M = xf.shape[0]
+    tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
+    batch = max((M + tps - 1) // tps, 1)
+    dx = torch.empty_like(xf)
+    dscale = dshift = None
+    ws, wsn = None, 0
+    if param_grads:
+        dscale = torch.empty((batch, K), dtype=torch.float32, device=x.device)
+        dshift = torch.empty((batch, K), dtype=torch.float32, device=x.device)
+        wsn = nat.lib().reels_layernorm_modulate_workspace_bytes(M, K, tps)
+        ws = _WS.get(x.device, wsn).data_ptr()
+    args = [t.contiguous().to(x.dtype) if t is not None else None for t in (scale, weight, bias)]
+    code = nat.lib().reels_layernorm_modulate_backward(xf.data_ptr(), df.data_ptr(), M, K, tps, *[_ptr(t) for t in args],
+                                                       float(epsilon), _dt(x.dtype), dx.data_ptr(), _ptr(dscale),
+                                                       _ptr(dshift), 0, ws, wsn, _stream(x.device))
+    nat.check("layernorm_modulate_backward", code)
+    return dx.reshape(x.shape), dscale, dshift
+
+
+class LayerNormModulateFunction(torch.autograd.Function):
+    """Autograd rule for :func:`layernorm_modulate`: gradients for x, scale
+    and shift (the LayerNorm's own weight and bias are frozen)."""
+
+    @staticmethod
+    def forward(ctx, x, scale, shift, epsilon=1e-6, weight=None, bias=None, tokens_per_sample=None):
+        ctx.save_for_backward(x, scale, weight, bias)
+        ctx.args = (epsilon, tokens_per_sample, shift is not None)
+        return layernorm_modulate(x, scale, shift, epsilon, weight, bias, tokens_per_sample)
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, scale, weight, bias = ctx.saved_tensors
+        epsilon, tps, has_shift = ctx.args
+        want = ctx.needs_input_grad[1] or ctx.needs_input_grad[2]
+        dx, dscale, dshift = layernorm_modulate_backward(x, dout.contiguous(), scale, epsilon, weight, bias, tps,
+                                                         param_grads=want)
+        gs = dscale.to(scale.dtype) if (dscale is not None and scale is not None) else None
+        gh = dshift.to(x.dtype) if (dshift is not None and has_shift) else None
+        return dx, gs, gh, None, None, None, None
+
+
+# ---------------------------------------------------------- gated residual
+def gated_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, tokens_per_sample: Optional[int] = None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``mixed_add(x, mixed_mul(y, gate))`` (transformer.jl:272,293) in one
+    pass; ``gate`` is (batch, N), sample b covering ``tokens_per_sample``
+    tokens.  ``out=x`` updates the residual stream in place."""
+    N = x.shape[-1]
+    _require_cuda(x, y, gate)
+    if y.shape != x.shape or y.dtype != x.dtype:
+        raise ValueError("x and y must have the same shape and dtype")
+    xf, yf = _flat(x, N), _flat(y, N)
+    M = xf.shape[0]
+    tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
+    o = torch.empty_like(xf) if out is None else _flat(out, N)
+    g = gate.contiguous().to(x.dtype)
+    nat.check("gated_residual", nat.lib().reels_gated_residual(xf.data_ptr(), yf.data_ptr(), g.data_ptr(), M, N, tps,
+                                                               _dt(x.dtype), o.data_ptr(), _stream(x.device)))
+    return o.reshape(x.shape) if out is None else out
+
+
+def gated_residual_backward(dout: torch.Tensor, y: torch.Tensor, gate: torch.Tensor,
+                            tokens_per_sample: Optional[int] = None, gate_grad: bool = True):
+    """Pullback of :func:`gated_residual`: ``(dy, dgate)`` (the residual's
+    gradient is ``dout``); dgate is fp32 (batch, N)."""
+    N = dout.shape[-1]
+    _require_cuda(dout, y, gate)
+    df, yf = _flat(dout, N), _flat(y, N)
+    M = df.shape[0]
+    tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
+    batch = max((M + tps - 1) // tps, 1)
+    dy = torch.empty_like(df)
+    dgate, ws, wsn = None, None, 0
+    if gate_grad:
+        dgate = torch.empty((batch, N), dtype=torch.float32, device=dout.device)
+        wsn = nat.lib().reels_gated_residual_workspace_bytes(M, N, tps)
+        ws = _WS.get(dout.device, wsn).data_ptr()
+    g = gate.contiguous().to(dout.dtype)
+    nat.check("gated_residual_backward", nat.lib().reels_gated_residual_backward(
+        df.data_ptr(), yf.data_ptr(), g.data_ptr(), M, N, tps, _dt(dout.dtype), dy.data_ptr(), _ptr(dgate), 0, ws,
+        wsn, _stream(dout.device)))
+    return dy.reshape(dout.shape), dgate
