@@ -1544,8 +1544,8 @@ int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M
     int rc = check_ln(x, M, K, tokens_per_sample, epsilon, dt);
     if (rc) return rc;
     if (!dout) return fail("null dout");
+    if (!dx) return fail("null dx (the parameter gradients reuse its row statistics)");
     const bool params = dscale || dshift;
-    if (!dx && !params) return ok(REELS_PATH_NONE);
     const int64_t batch = cdiv(M, tokens_per_sample);
     if (params) {
         if (!workspace) return fail("null workspace; size it with reels_layernorm_modulate_workspace_bytes");
@@ -1569,9 +1569,8 @@ int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M
                          : nullptr;
     const dim3 grid((unsigned)std::min<int64_t>(M, 16LL * ds->sms));
     const size_t smem = (size_t)K * 8;
-    // dx (and the row statistics); without dx the rows still run for the statistics
+    // dx, and the row statistics the parameter reduction reads
     void *dxo = dx;
-    if (!dx) return fail("dx is required (the parameter gradients reuse its row statistics)");
     if (dt == REELS_BF16)
         launch_pdl(ln_modulate_bwd_kernel<DT_BF16>, grid, dim3(LN_THREADS), smem, st, x, dout, M, K,
                    tokens_per_sample, scale, ln_weight, epsilon, dxo, stats);

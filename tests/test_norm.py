@@ -70,6 +70,7 @@ def test_layernorm_rejects_bad_arguments(lib):
     assert f(p, 4, 16, 4, None, None, None, None, 1e-6, nat.BF16, None, None) == nat.EINVAL
     b = lib.reels_layernorm_modulate_backward
     assert b(p, None, 4, 16, 4, None, None, None, 1e-6, nat.BF16, p, None, None, 0, None, 0, None) == nat.EINVAL
+    assert b(p, p, 4, 16, 4, None, None, None, 1e-6, nat.BF16, None, None, None, 0, None, 0, None) == nat.EINVAL
     # parameter gradients need a workspace
     assert b(p, p, 4, 16, 4, None, None, None, 1e-6, nat.BF16, p, p, p, 0, None, 0, None) == nat.EINVAL
     assert lib.reels_layernorm_modulate_workspace_bytes(4, 16, 4) > 0
