@@ -531,7 +531,9 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.partial = reinterpret_cast<float *>(ws_base + wl.part);
     a.err = ds.status;
     a.epi = s.splits > 1 ? 2 : c.epi_final;
-    dim3 grid((unsigned)cdiv(c.rows, 128), (unsigned)s.splits);
+    a.splits = s.splits;
+    // persistent CTAs, one per SM at most (200 KB of ring each)
+    const dim3 grid((unsigned)std::min<int64_t>(cdiv(c.rows, 128) * s.splits, ds.sms));
     if (dt == REELS_BF16) launch_pdl(sk_gemm_kernel<DT_BF16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     else launch_pdl(sk_gemm_kernel<DT_F16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     REELS_LAUNCHED();

@@ -19,6 +19,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
 }
 
 // ------------------------------------------------------------ skinny gemm
+// Persistent: each CTA walks work units u = blockIdx.x, blockIdx.x + gridDim.x,
+// ... (a unit is one 128-row tile of D over one reduction split).  The TMA
+// ring runs on across units, so a CTA's next tile streams in while the
+// current one is multiplied, and the TMEM accumulator is double-buffered so
+// the epilogue of one unit overlaps the MMAs of the next: the pipeline fill
+// and the epilogue are paid once per CTA, not once per tile.
 constexpr int SK_THREADS = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
 constexpr int SK_A_BYTES = 128 * 128;
 constexpr int SK_MAX_STAGES = 8;
@@ -27,7 +33,8 @@ constexpr int SK_MAX_STAGES = 8;
 // many bytes in flight as the budget allows (8 stages up to rank 64).
 constexpr int SK_RING_BYTES = 200 * 1024;
 constexpr int SK_BAR_OFF = SK_RING_BYTES;
-constexpr int SK_SMEM_BYTES = SK_BAR_OFF + (2 * SK_MAX_STAGES + 1) * 8 + 16 + 1024;
+constexpr int SK_NBAR = 2 * SK_MAX_STAGES + 5;  // full, empty, acc_full[2], acc_empty[2], mma_done
+constexpr int SK_SMEM_BYTES = SK_BAR_OFF + SK_NBAR * 8 + 16 + 1024;
 
 __host__ __device__ constexpr int sk_stage_bytes(int npad) { return SK_A_BYTES + npad * 128; }
 __host__ __device__ constexpr int sk_stages(int npad) {
@@ -39,6 +46,7 @@ struct SkArgs {
     int rows;          // rows of D
     int kb_total;      // reduction blocks of 64
     int kb_per_split;
+    int splits;
     int npad;          // MMA N = B-operand rows (multiple of 16, <= 256)
     int a_mn;          // A operand MN-major (rows of D contiguous in memory)
     int epi;           // 0 transposed store act dtype, 1 fp32 accumulate, 2 fp32 partial
@@ -51,6 +59,18 @@ struct SkArgs {
     float *partial;    // epi 2: [splits][rows][npad]
     unsigned *err;
 };
+
+struct SkUnit {
+    int row0, sp, kb0, n_iter;
+};
+__device__ __forceinline__ SkUnit sk_unit(const SkArgs &a, int tiles, int u) {
+    SkUnit w;
+    w.sp = u / tiles;
+    w.row0 = (u - w.sp * tiles) * 128;
+    w.kb0 = w.sp * a.kb_per_split;
+    w.n_iter = max(0, min(a.kb_total, w.kb0 + a.kb_per_split) - w.kb0);
+    return w;
+}
 
 template <int DT>
 __global__ void __launch_bounds__(SK_THREADS, 1)
@@ -65,24 +85,27 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + SK_BAR_OFF);
     uint64_t *empty = full + SK_MAX_STAGES;
     uint64_t *acc_full = full + 2 * SK_MAX_STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SK_BAR_OFF + (2 * SK_MAX_STAGES + 1) * 8);
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *mma_done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + SK_BAR_OFF + SK_NBAR * 8);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = blockIdx.x * 128;
-    const int sp = blockIdx.y;
-    const int kb0 = sp * args.kb_per_split;
-    const int kb1 = min(args.kb_total, kb0 + args.kb_per_split);
-    const int n_iter = max(0, kb1 - kb0);
+    const int tiles = (args.rows + 127) / 128;
+    const int units = tiles * args.splits;
     const uint32_t b_bytes = (uint32_t)args.npad * 128u;
-    const uint32_t tmem_cols = args.npad <= 32 ? 32u : (args.npad <= 64 ? 64u : (args.npad <= 128 ? 128u : 256u));
+    const uint32_t acc_cols = args.npad <= 32 ? 32u : (args.npad <= 64 ? 64u : (args.npad <= 128 ? 128u : 256u));
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+        }
+        mbar_init(mma_done, 1);
         *abort = 0;
         fence_mbar_init();
     }
@@ -91,7 +114,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, tmem_cols);
+        tmem_alloc(tmem_slot, 2 * acc_cols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -103,67 +126,97 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int it = 0; it < n_iter; ++it) {
-                const int s = it % NS;
-                const uint32_t ph = (it / NS) & 1;
-                if (!wait_bar(&empty[s], ph ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
-                    aborted_here = true;
-                    break;
+            uint32_t g = 0;
+            for (int u = blockIdx.x; u < units && !aborted_here; u += gridDim.x) {
+                const SkUnit w = sk_unit(args, tiles, u);
+                for (int it = 0; it < w.n_iter; ++it, ++g) {
+                    const int s = g % NS;
+                    const uint32_t ph = (g / NS) & 1;
+                    if (!wait_bar(&empty[s], ph ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
+                        aborted_here = true;
+                        break;
+                    }
+                    uint8_t *a_dst = smem + s * STAGE;
+                    uint8_t *b_dst = a_dst + SK_A_BYTES;
+                    const int kb = w.kb0 + it;
+                    mbar_arrive_expect_tx(&full[s], SK_A_BYTES + b_bytes);
+                    if (args.a_mn) {
+                        tma_load_2d(a_dst, &tmA, w.row0, kb * BK, &full[s]);
+                        tma_load_2d(a_dst + 8192, &tmA, w.row0 + 64, kb * BK, &full[s]);
+                    } else {
+                        tma_load_2d(a_dst, &tmA, kb * BK, w.row0, &full[s]);
+                    }
+                    tma_load_2d(b_dst, &tmB, kb * BK, 0, &full[s]);
                 }
-                uint8_t *a_dst = smem + s * STAGE;
-                uint8_t *b_dst = a_dst + SK_A_BYTES;
-                const int kb = kb0 + it;
-                mbar_arrive_expect_tx(&full[s], SK_A_BYTES + b_bytes);
-                if (args.a_mn) {
-                    tma_load_2d(a_dst, &tmA, row0, kb * BK, &full[s]);
-                    tma_load_2d(a_dst + 8192, &tmA, row0 + 64, kb * BK, &full[s]);
-                } else {
-                    tma_load_2d(a_dst, &tmA, kb * BK, row0, &full[s]);
-                }
-                tma_load_2d(b_dst, &tmB, kb * BK, 0, &full[s]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const int ab = (DT == DT_BF16) ? 1 : 0;
             const uint32_t id = idesc_f16(ab, args.a_mn, 0, 128, args.npad);
-            for (int it = 0; it < n_iter; ++it) {
-                const int s = it % NS;
-                const uint32_t ph = (it / NS) & 1;
-                if (!wait_bar(&full[s], ph, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
+            uint32_t g = 0, lu = 0;
+            for (int u = blockIdx.x; u < units && !aborted_here; u += gridDim.x, ++lu) {
+                const SkUnit w = sk_unit(args, tiles, u);
+                const int acc = lu & 1;
+                if (!wait_bar(&acc_empty[acc], ((lu >> 1) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                     aborted_here = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a_base = sbase + s * STAGE;
-                const uint32_t b_base = a_base + SK_A_BYTES;
+                const uint32_t d_tm = tmem + acc * acc_cols;
+                for (int it = 0; it < w.n_iter; ++it, ++g) {
+                    const int s = g % NS;
+                    const uint32_t ph = (g / NS) & 1;
+                    if (!wait_bar(&full[s], ph, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
+                        aborted_here = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = sbase + s * STAGE;
+                    const uint32_t b_base = a_base + SK_A_BYTES;
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ad = args.a_mn ? sdesc_sw128(a_base + kk * 2048, 8192, 1024)
-                                                  : sdesc_sw128(a_base + kk * 32, 16, 1024);
-                    const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
-                    mma_f16_ss(tmem, ad, bd, id, (it > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < BK / 16; ++kk) {
+                        const uint64_t ad = args.a_mn ? sdesc_sw128(a_base + kk * 2048, 8192, 1024)
+                                                      : sdesc_sw128(a_base + kk * 32, 16, 1024);
+                        const uint64_t bd = sdesc_sw128(b_base + kk * 32, 16, 1024);
+                        mma_f16_ss(d_tm, ad, bd, id, (it > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);
                 }
-                mma_commit(&empty[s]);
+                if (aborted_here) break;
+                mma_commit(&acc_full[acc]);
             }
-            mma_commit(acc_full);
+            mma_commit(mma_done);
         }
     } else {
         const int q = warp & 3;
-        if (warp_wait(acc_full, 0, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+        uint32_t lu = 0;
+        for (int u = blockIdx.x; u < units && !aborted_here; u += gridDim.x, ++lu) {
+            const SkUnit w = sk_unit(args, tiles, u);
+            const int acc = lu & 1;
+            if (!warp_wait(&acc_full[acc], (lu >> 1) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+                aborted_here = true;
+                break;
+            }
             tc_fence_after();
-            const int row = row0 + 32 * q + lane;
+            const int row = w.row0 + 32 * q + lane;
             for (int c = 0; c < args.npad; c += 16) {
                 uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + acc * acc_cols + c, v);
                 tmem_wait_ld();
+                if (c + 16 >= args.npad) {
+                    // the whole accumulator is in registers: the next unit may use it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                }
                 if (row >= args.rows) continue;
-                if (n_iter == 0) {
+                if (w.n_iter == 0) {
 #pragma unroll
                     for (int t = 0; t < 16; ++t) v[t] = 0u;
                 }
                 if (args.epi == 2) {
-                    float *dst = args.partial + ((long long)sp * args.rows + row) * args.npad + c;
+                    float *dst = args.partial + ((long long)w.sp * args.rows + row) * args.npad + c;
 #pragma unroll
                     for (int t = 0; t < 16; t += 4)
                         *reinterpret_cast<float4 *>(dst + t) =
@@ -201,7 +254,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
         tc_fence_after();
         if (lane == 0) {
             long long t0 = clock64();
-            while (!mbar_try_wait(acc_full, 0)) {
+            while (!mbar_try_wait(mma_done, 0)) {
                 if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
                     atomicOr(args.err, DEVERR_TIMEOUT_ACC);
                     break;
@@ -209,7 +262,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
             }
         }
         __syncwarp();
-        tmem_dealloc(tmem, tmem_cols);
+        tmem_dealloc(tmem, 2 * acc_cols);
     }
 }
 
