@@ -114,3 +114,35 @@ def test_gated_residual(torch, M, N, tps, dtype):
     sample = np.arange(M) // tps
     dg_ref = np.stack([(dout * y)[sample == i].sum(0, dtype=np.float64) for i in range(batch)])
     assert lc.rel_l2(dgate.cpu().numpy(), dg_ref) <= 1e-5
+
+
+def test_modulation_finite_differences(torch):
+    """The reference's modulation test (test/unit/layers.jl:43-54) on the
+    fused LayerNorm + modulation in fp32: 3 features, 4 tokens per sample, 2
+    samples; dx, dscale and dshift against central differences of
+    sum(out .* dy) with step 1e-3, rtol 3e-3."""
+    from reels_b200 import layernorm_modulate, layernorm_modulate_backward
+    rng = np.random.default_rng(22)
+    x = torch.from_numpy(rng.standard_normal((8, 3)).astype(np.float32)).cuda()
+    scale = torch.from_numpy(rng.standard_normal((2, 3)).astype(np.float32)).cuda()
+    shift = torch.from_numpy(rng.standard_normal((2, 3)).astype(np.float32)).cuda()
+    dy = torch.from_numpy(rng.standard_normal((8, 3)).astype(np.float32)).cuda()
+    eps = 1e-6
+
+    def objective():
+        return float((layernorm_modulate(x, scale, shift, eps, tokens_per_sample=4).double() * dy.double()).sum())
+
+    def fd(t, idx, h=1e-3):
+        old = t[idx].item()
+        t[idx] = old + h
+        plus = objective()
+        t[idx] = old - h
+        minus = objective()
+        t[idx] = old
+        return (plus - minus) / (2 * h)
+
+    dx, dscale, dshift = layernorm_modulate_backward(x, dy, scale, eps, tokens_per_sample=4, param_grads=True)
+    for idx in ((1, 2), (5, 0), (6, 1)):
+        assert dx[idx].item() == pytest.approx(fd(x, idx), rel=3e-3, abs=1e-4)
+    assert dscale[0, 1].item() == pytest.approx(fd(scale, (0, 1)), rel=3e-3, abs=1e-4)
+    assert dshift[1, 2].item() == pytest.approx(fd(shift, (1, 2)), rel=3e-3, abs=1e-4)

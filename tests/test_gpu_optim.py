@@ -128,3 +128,28 @@ def test_unprepared_workspace_reports_an_error(torch):
     rc = L.reels_lowvram_check_device_status(stream)
     assert rc == nat.EDEVICE and "reels_opt_prepare" in L.reels_lowvram_last_error().decode()
     assert L.reels_lowvram_check_device_status(stream) == 0  # the status word was cleared
+
+
+def test_reference_known_answers(torch):
+    """test/unit/training.jl:87-127 on the GPU: exclusions give exactly 0.95
+    and 1; an fp16 parameter moves, its fp32 master is kept, and the
+    parameter equals the master rounded to fp16."""
+    from reels_b200 import check_device_status
+    from reels_b200 import optim
+    params = [torch.ones(2, device="cuda"), torch.ones(2, device="cuda")]
+    grads = [torch.zeros(2, device="cuda"), torch.zeros(2, device="cuda")]
+    state = optim.AdamWState(params)
+    mask = optim.weight_decay_mask(["blocks.0.attn.lora_A.weight", "blocks.0.attn.bias"], [r"bias$"])
+    optim.update_(optim.AdamW(learning_rate=0.1, weight_decay=0.5), state, params, grads, weight_decay_mask=mask)
+    check_device_status()
+    assert params[0].cpu().tolist() == [float(f32(0.95))] * 2
+    assert params[1].cpu().tolist() == [1.0, 1.0]
+    p16 = torch.tensor([1.0, -2.0], device="cuda").to(torch.float16)
+    st16 = optim.AdamWState([p16])
+    assert st16.master[0].dtype == torch.float32 and st16.master[0].cpu().tolist() == [1.0, -2.0]
+    optim.update_(optim.AdamW(learning_rate=1e-2, weight_decay=0.0), st16, [p16],
+                  [torch.tensor([0.25, -0.5], device="cuda")])
+    check_device_status()
+    assert st16.step == 1
+    assert st16.master[0].cpu().tolist() != [1.0, -2.0]
+    assert torch.equal(p16, st16.master[0].to(torch.float16))

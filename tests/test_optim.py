@@ -117,3 +117,15 @@ def test_prepare_rejects_bad_tables(lib):
     assert lib.reels_adamw_update(ws, float("nan"), 0.9, 0.999, 1e-8, 0.01, 0.1, 0.001, 1.0, None, 0.0,
                                   None) == nat.EINVAL
     assert lib.reels_adamw_update(ws, 1e-4, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.001, 1.0, ws, 0.0, None) == nat.EINVAL
+
+
+def test_reference_known_answers_on_the_oracle():
+    """The reference's own AdamW cases (test/unit/training.jl:87-127):
+    named weight-decay exclusions give exactly 0.95 and 1 after one step of
+    lr 0.1, weight decay 0.5 on zero gradients."""
+    assert optim.weight_decay_mask(["blocks.0.attn.lora_A.weight", "blocks.0.attn.bias"], [r"bias$"]) == [True, False]
+    c1, c2 = optim.bias_corrections(optim.AdamW(), 1)
+    for decay, expect in ((0.5, 0.95), (0.0, 1.0)):
+        _, _, w = oracle.adamw_update(np.zeros(2, f32), np.zeros(2), np.zeros(2), np.ones(2), 0.1, 0.9, 0.999, 1e-8,
+                                      decay, c1, c2)
+        assert np.array_equal(w, np.full(2, f32(expect)))

@@ -207,3 +207,12 @@ def test_gelu_tanh_grad_matches_finite_differences():
     fd = (f(z + h) - f(z - h)) / (2 * h)
     got = oracle.gelu_tanh_grad(z.astype(np.float32))
     assert np.max(np.abs(got - fd)) < 2e-6
+
+
+def test_gelu_tanh_float16_reference_case():
+    """test/unit/layers.jl:12-18: gelu_tanh of Float16 values, rounded to
+    Float16, is within rtol 2e-3 / atol 2e-4 of the Float32 result."""
+    v = np.array([-2, -0.5, 0, 0.5, 2], np.float16)
+    h = oracle.gelu_tanh(v.astype(np.float32)).astype(np.float16).astype(np.float32)
+    ref = oracle.gelu_tanh(v.astype(np.float32))
+    assert np.allclose(h, ref, rtol=2e-3, atol=2e-4)
