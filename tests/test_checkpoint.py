@@ -148,3 +148,33 @@ def test_int8_storage_required(tmp_path):
         ck.load_quantized_linear(p, "lin", 8, 4)
     with pytest.raises(KeyError):
         ck.load_quantized_linear(p, "other", 4, 8)
+
+
+def test_reference_streaming_io_case(tmp_path):
+    """The file test/unit/safetensors.jl:1-13 writes: z = reshape(Float32.(1:6),
+    2, 3) and a = Float16[1, 2] under metadata format=reels.  Its writer
+    (src/checkpoints/safetensors.jl:101-130) sorts the names, records
+    size(z) = [2, 3] and stores z row-major (permutedims of the column-major
+    array), so the data section is a's two halves then 1, 3, 5, 2, 4, 6.  The
+    bytes are built here as that writer lays them out; loading them gives z
+    as the logical 2 x 3 matrix [[1, 3, 5], [2, 4, 6]] and a unchanged, and
+    writing the same tensors with this module gives the same data section."""
+    header = {"__metadata__": {"format": "reels"},
+              "a": {"dtype": "F16", "shape": [2], "data_offsets": [0, 4]},
+              "z": {"dtype": "F32", "shape": [2, 3], "data_offsets": [4, 28]}}
+    data = np.array([1, 2], np.float16).tobytes() + np.array([1, 3, 5, 2, 4, 6], np.float32).tobytes()
+    p = str(tmp_path / "adapter.safetensors")
+    _write_raw(p, header, data)
+    h = ck.inspect_safetensors(p)
+    assert h.metadata["format"] == "reels"
+    assert sorted(h.tensors) == ["a", "z"]
+    z = ck.load_safetensor(p, "z", h)
+    assert z.tolist() == [[1, 3, 5], [2, 4, 6]]
+    assert ck.load_safetensor(p, "a", h).tolist() == [1.0, 2.0]
+    with pytest.raises(KeyError):
+        ck.load_safetensor(p, "missing", h)
+    q = str(tmp_path / "ours.safetensors")
+    ck.write_safetensors(q, {"z": z, "a": torch.tensor([1, 2], dtype=torch.float16)}, {"format": "reels"})
+    raw = open(q, "rb").read()
+    (n,) = struct.unpack("<Q", raw[:8])
+    assert raw[8 + n:] == data
