@@ -78,6 +78,20 @@ const char *reels_lowvram_last_error(void);
 
 int reels_lowvram_abi_version(void);
 
+/* The plan the q8 GEMM takes for D[M][Nout] over a reduction of Kred, for
+ * diagnostics and tests; no device work.  info (7 entries):
+ *   [0] kernel: 1 weight-in-TMEM, 0 both operands in shared memory, 2 pair
+ *   [1] tokens per tile  [2] reduction elements per pipeline stage
+ *   [3] reduction splits [4] pipeline stages per split
+ *   [5] output-column tiles  [6] token tiles
+ * act: REELS_ACT_NONE or REELS_ACT_GELU_TANH (the epilogue weighs the plans).
+ * sms <= 0: the current device's SM count (148 without a device). */
+int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64_t *info);
+
+/* The skinny rank-r GEMM's reduction split for `rows` rows over `red`:
+ * info[0] splits, info[1] 64-element blocks per split. */
+int reels_sk_plan(int64_t rows, int64_t red, int64_t r, int sms, int64_t *info);
+
 /* Path taken by the last successful compute call on this thread. */
 int reels_lowvram_last_path(void);
 

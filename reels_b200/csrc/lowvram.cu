@@ -1019,6 +1019,42 @@ const char *reels_lowvram_last_error(void) { return t_last_error.c_str(); }
 int reels_lowvram_abi_version(void) { return REELS_LOWVRAM_ABI_VERSION; }
 int reels_lowvram_last_path(void) { return t_last_path; }
 
+static int current_sms() {
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    } else {
+        cudaGetLastError();
+    }
+    return sms;
+}
+
+int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64_t *info) {
+    if (!info) return fail("null info");
+    if (M <= 0 || Nout <= 0 || Kred <= 0) return fail("plan needs positive M, Nout and Kred");
+    if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
+    const Q8Plan p = plan_q8(M, Nout, Kred, sms > 0 ? sms : current_sms(), 0, true,
+                             act == REELS_ACT_NONE ? ACT_NONE : ACT_GELU_TANH);
+    info[0] = p.ts ? 1 : (p.pair ? 2 : 0);
+    info[1] = p.ts ? p.ts : 128 * p.mt;
+    info[2] = p.ts ? 64 * p.ts_kb2 : BK;
+    info[3] = p.split.splits;
+    info[4] = p.split.kb_per;
+    info[5] = p.ntiles;
+    info[6] = p.mtiles;
+    return REELS_OK;
+}
+
+int reels_sk_plan(int64_t rows, int64_t red, int64_t r, int sms, int64_t *info) {
+    if (!info) return fail("null info");
+    if (rows <= 0 || red <= 0 || r <= 0 || r > 256) return fail("plan needs positive rows, red and 0 < r <= 256");
+    const Split sp = plan_sk(rows, red, sms > 0 ? sms : current_sms(), r);
+    info[0] = sp.splits;
+    info[1] = sp.kb_per;
+    return REELS_OK;
+}
+
 int reels_lowvram_profile_enable(int enable) {
     t_prof.on = enable != 0;
     t_prof.used = 0;
@@ -1124,15 +1160,7 @@ int reels_q8_materialize(const int8_t *q, const float *scales, int layout, int64
 
 size_t reels_q8lora_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t r, int act_dtype, int pass) {
     if (M < 0 || K <= 0 || N <= 0 || r < 0) return 0;
-    int sms = 148;
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) {
-        int v = 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
-    } else {
-        cudaGetLastError();
-    }
-    return ws_layout(M, K, N, r, act_dtype, pass, sms).total;
+    return ws_layout(M, K, N, r, act_dtype, pass, current_sms()).total;
 }
 
 size_t reels_q8lora_saved_bytes(int64_t M, int64_t r, int act_dtype) {

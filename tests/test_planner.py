@@ -1,0 +1,99 @@
+"""CPU checks of the GEMM planners and of workspace sizing (no device work).
+
+The planners choose kernels, tiles and reduction splits from a time model
+fitted to B200 measurements; the workspace query must cover whatever they
+choose, or a split's fp32 partials would overrun the caller's buffer.  These
+properties are checked over the BASELINE shapes and a seeded spread of
+others."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from reels_b200 import _native as nat
+from reels_b200 import build as native_build
+
+SMS = 148
+
+
+@pytest.fixture(scope="module")
+def lib():
+    native_build.build()
+    return nat.lib()
+
+
+def q8(lib, M, Nout, Kred, act=0):
+    info = (ctypes.c_int64 * 7)()
+    assert lib.reels_q8_plan(M, Nout, Kred, act, SMS, info) == 0
+    return dict(zip(["kernel", "tokens", "stage", "splits", "kb_per", "ntiles", "mtiles"], list(info)))  # kb_per: stages
+
+
+def sk(lib, rows, red, r):
+    info = (ctypes.c_int64 * 2)()
+    assert lib.reels_sk_plan(rows, red, r, SMS, info) == 0
+    return info[0], info[1]
+
+
+def test_bench_shapes_take_the_256_token_tmem_tiles(lib):
+    # Wan 1.3B block linears at 32760 tokens: forward (Nout = N) and dX (Nout = K)
+    for M, K, N in [(32760, 1536, 1536), (32760, 1536, 8960), (32760, 8960, 1536)]:
+        for Nout, Kred in ((N, K), (K, N)):
+            p = q8(lib, M, Nout, Kred)
+            assert p["kernel"] == 1 and p["tokens"] == 256 and p["splits"] == 1, (M, Nout, Kred, p)
+            assert p["ntiles"] == -(-Nout // 128) and p["mtiles"] == -(-M // 256)
+
+
+def test_small_token_counts_take_the_wide_stage_tiles(lib):
+    # BASELINE config 5 at 128 tokens: one 128-token tile, 128-wide stages
+    p = q8(lib, 128, 13824, 5120)
+    assert p["kernel"] == 1 and p["tokens"] == 128 and p["stage"] == 128
+    assert p["splits"] * p["kb_per"] * p["stage"] >= 5120  # the splits cover the reduction
+
+
+def test_splits_cover_the_reduction_exactly(lib):
+    rng = np.random.default_rng(0)
+    for _ in range(300):
+        M = int(rng.integers(1, 40000))
+        Nout = 16 * int(rng.integers(1, 1200))
+        Kred = 16 * int(rng.integers(1, 1200))
+        for act in (0, 1):
+            p = q8(lib, M, Nout, Kred, act)
+            kb = -(-Kred // p["stage"])
+            assert p["splits"] >= 1 and p["kb_per"] >= 1
+            assert (p["splits"] - 1) * p["kb_per"] < kb <= p["splits"] * p["kb_per"], (M, Nout, Kred, p)
+
+
+def test_workspace_covers_every_split(lib):
+    """reels_q8lora_workspace_bytes >= the fp32 partials of the splits the
+    planners pick, for both passes, with and without the fused activation."""
+    rng = np.random.default_rng(1)
+    shapes = [(128, 5120, 13824, 8), (512, 5120, 13824, 64), (32760, 1536, 8960, 32), (96, 3072, 256, 8)]
+    for _ in range(200):
+        shapes.append((int(rng.integers(1, 9000)), 16 * int(rng.integers(1, 700)), 16 * int(rng.integers(1, 700)),
+                       int(rng.integers(0, 257))))
+    for M, K, N, r in shapes:
+        np_ = max(16, -(-max(r, 1) // 16) * 16)
+        for pas in (nat.PASS_FORWARD, nat.PASS_BACKWARD):
+            ws = lib.reels_q8lora_workspace_bytes(M, K, N, r, nat.BF16, pas)
+            need = 0
+            q8_shapes = [(M, N, K)] if pas == nat.PASS_FORWARD else [(M, K, N)]
+            for rows, cols, red in q8_shapes:
+                for act in (0, 1):
+                    p = q8(lib, rows, cols, red, act)
+                    if p["splits"] > 1:
+                        need = max(need, p["splits"] * rows * cols * 4)
+            if r > 0:
+                sk_shapes = [(M, K)] if pas == nat.PASS_FORWARD else [(M, K), (M, N), (K, M), (N, M)]
+                for rows, red in sk_shapes:
+                    splits, _ = sk(lib, rows, red, r)
+                    if splits > 1:
+                        need = max(need, splits * rows * np_ * 4)
+            assert ws >= need, (M, K, N, r, pas, ws, need)
+
+
+def test_plan_queries_reject_bad_arguments(lib):
+    info = (ctypes.c_int64 * 7)()
+    assert lib.reels_q8_plan(0, 16, 16, 0, SMS, info) == nat.EINVAL
+    assert lib.reels_q8_plan(16, 16, 16, 5, SMS, info) == nat.EINVAL
+    assert lib.reels_q8_plan(16, 16, 16, 0, SMS, None) == nat.EINVAL
+    assert lib.reels_sk_plan(16, 16, 300, SMS, info) == nat.EINVAL
