@@ -66,14 +66,17 @@ def _require_cuda(*tensors):
 
 
 class _Workspace:
-    """Per-device scratch buffer, grown on demand by the caller side (the
-    native library itself never allocates)."""
+    """Scratch buffer per (device, stream), grown on demand by the caller
+    side (the native library itself never allocates).  One buffer per stream:
+    calls on different streams may run concurrently, and the caching
+    allocator only orders a replaced buffer's reuse after work on its own
+    stream."""
 
     def __init__(self):
         self._bufs = {}
 
     def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.type, device.index)
+        key = (device.type, device.index, torch.cuda.current_stream(device).cuda_stream)
         buf = self._bufs.get(key)
         if buf is None or buf.numel() < nbytes:
             buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
