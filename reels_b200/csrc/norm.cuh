@@ -255,6 +255,15 @@ namespace reels {
 // in one pass (the reference's two broadcasts write an intermediate).  out may
 // be x itself.  Its pullback: dx = dout; dy = round(dout * gate[b]) (the
 // product's pullback); dgate[b] = sum over the sample's tokens of dout * y.
+// 16-bit types with N % 8 == 0 and 16-byte aligned pointers: eight elements
+// of one row per 16-byte access.
+template <int DT>
+__device__ __forceinline__ bool gr_vec(int64_t N, const void *a, const void *b, const void *c, const void *d) {
+    return DT != DT_F32 && (N & 7) == 0 &&
+           ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
+             reinterpret_cast<uintptr_t>(d)) & 15) == 0;
+}
+
 template <int DT>
 __global__ void gated_residual_kernel(const void *x, const void *y, const void *gate, int64_t M, int64_t N,
                                       int64_t tps, void *out) {
@@ -264,6 +273,30 @@ __global__ void gated_residual_kernel(const void *x, const void *y, const void *
     const T *yp = reinterpret_cast<const T *>(y);
     const T *gp = reinterpret_cast<const T *>(gate);
     T *op = reinterpret_cast<T *>(out);
+    if constexpr (DT != DT_F32) {
+        if (gr_vec<DT>(N, x, y, gate, out)) {
+            const int64_t nv = M * N / 8, rowv = N / 8;
+            for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+                const int64_t m = v / rowv, nb = v - m * rowv;
+                const uint4 xw = reinterpret_cast<const uint4 *>(xp)[v], yw = reinterpret_cast<const uint4 *>(yp)[v];
+                const uint4 gw = reinterpret_cast<const uint4 *>(gp + (m / tps) * N)[nb];
+                const uint32_t xs[4] = {xw.x, xw.y, xw.z, xw.w}, ys[4] = {yw.x, yw.y, yw.z, yw.w},
+                               gs[4] = {gw.x, gw.y, gw.z, gw.w};
+                uint32_t os[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    float x0, x1, y0, y1, g0, g1;
+                    unpack2<DT>(xs[h], x0, x1);
+                    unpack2<DT>(ys[h], y0, y1);
+                    unpack2<DT>(gs[h], g0, g1);
+                    os[h] = Elem<DT>::pack2(__fadd_rn(x0, round_act<DT>(__fmul_rn(y0, g0))),
+                                            __fadd_rn(x1, round_act<DT>(__fmul_rn(y1, g1))));
+                }
+                reinterpret_cast<uint4 *>(op)[v] = make_uint4(os[0], os[1], os[2], os[3]);
+            }
+            return;
+        }
+    }
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * N; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = i / N, n = i - m * N;
         const float prod = round_act<DT>(__fmul_rn(Elem<DT>::to_f(yp[i]), Elem<DT>::to_f(gp[(m / tps) * N + n])));
@@ -279,6 +312,27 @@ __global__ void gated_residual_dy_kernel(const void *dout, const void *gate, int
     const T *dp = reinterpret_cast<const T *>(dout);
     const T *gp = reinterpret_cast<const T *>(gate);
     T *o = reinterpret_cast<T *>(dy);
+    if constexpr (DT != DT_F32) {
+        if (gr_vec<DT>(N, dout, gate, dy, dy)) {
+            const int64_t nv = M * N / 8, rowv = N / 8;
+            for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+                const int64_t m = v / rowv, nb = v - m * rowv;
+                const uint4 dw = reinterpret_cast<const uint4 *>(dp)[v];
+                const uint4 gw = reinterpret_cast<const uint4 *>(gp + (m / tps) * N)[nb];
+                const uint32_t ds[4] = {dw.x, dw.y, dw.z, dw.w}, gs[4] = {gw.x, gw.y, gw.z, gw.w};
+                uint32_t os[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    float d0, d1, g0, g1;
+                    unpack2<DT>(ds[h], d0, d1);
+                    unpack2<DT>(gs[h], g0, g1);
+                    os[h] = Elem<DT>::pack2(__fmul_rn(d0, g0), __fmul_rn(d1, g1));
+                }
+                reinterpret_cast<uint4 *>(o)[v] = make_uint4(os[0], os[1], os[2], os[3]);
+            }
+            return;
+        }
+    }
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < M * N; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = i / N, n = i - m * N;
         o[i] = Elem<DT>::from_f(__fmul_rn(Elem<DT>::to_f(dp[i]), Elem<DT>::to_f(gp[(m / tps) * N + n])));
