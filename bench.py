@@ -35,16 +35,18 @@ sys.path.insert(0, ROOT)
 HIDDEN, FFN, CONTEXT = 1536, 8960, 512
 
 
-def block_layers(tokens: int, context: int = CONTEXT):
-    """(name, M, K, N) of the ten linears of a Wan-2.1-1.3B block."""
+def block_layers(tokens: int, context: int = CONTEXT, hidden: int = HIDDEN, ffn: int = FFN):
+    """(name, M, K, N) of the ten linears of a DiT block (Wan 2.1 1.3B by
+    default): self-attention q/k/v/o, cross-attention q/o over the tokens and
+    k/v over the context, and the FFN pair."""
     L = []
     for n in ("self_q", "self_k", "self_v", "self_o", "cross_q"):
-        L.append((n, tokens, HIDDEN, HIDDEN))
-    L.append(("cross_k", context, HIDDEN, HIDDEN))
-    L.append(("cross_v", context, HIDDEN, HIDDEN))
-    L.append(("cross_o", tokens, HIDDEN, HIDDEN))
-    L.append(("ffn_up", tokens, HIDDEN, FFN))
-    L.append(("ffn_down", tokens, FFN, HIDDEN))
+        L.append((n, tokens, hidden, hidden))
+    L.append(("cross_k", context, hidden, hidden))
+    L.append(("cross_v", context, hidden, hidden))
+    L.append(("cross_o", tokens, hidden, hidden))
+    L.append(("ffn_up", tokens, hidden, ffn))
+    L.append(("ffn_down", tokens, ffn, hidden))
     return L
 
 
@@ -57,6 +59,14 @@ def workload(config: str):
         # few hundred MB in total, the case the ncu captures use.
         return dict(name="wan21-1.3b-ffn-up-8k", layers=[("ffn_up", 8192, 1536, 8960)], tokens=8192, rank=32,
                     alpha=32.0)
+    if config == "wan14b":
+        # BASELINE config 3, per GPU: one Wan 2.1 14B block (hidden 5120, FFN 13824)
+        return dict(name="wan21-14b-block-linears", layers=block_layers(32760, 512, 5120, 13824), tokens=32760,
+                    rank=32, alpha=32.0, context=512)
+    if config == "ltx":
+        # BASELINE config 4, per GPU: one LTX-2.3 block (hidden 4096, FFN 16384), 2 x 6144 tokens, context 2048
+        return dict(name="ltx23-block-linears", layers=block_layers(12288, 2048, 4096, 16384), tokens=12288,
+                    rank=64, alpha=64.0, context=2048)
     return dict(name="wan21-1.3b-block-linears", layers=block_layers(32760), tokens=32760, rank=32, alpha=32.0)
 
 
@@ -152,7 +162,7 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------- CPU baseline
-def cpu_sample(layers, r, alpha, tokens_sample, seconds, seed=0):
+def cpu_sample(layers, r, alpha, tokens_sample, seconds, seed=0, context=CONTEXT):
     """Time the reference CPU path (numpy + OpenBLAS fp32) on the block with
     `tokens_sample` tokens per sample; returns (tokens/s, iters, threads)."""
     from oracle import numpy_port
@@ -160,7 +170,7 @@ def cpu_sample(layers, r, alpha, tokens_sample, seconds, seed=0):
     g = np.random.default_rng(seed)
     data = []
     for (_, M, K, N) in layers:
-        m = min(M, tokens_sample) if M > CONTEXT else M
+        m = M if M == context else min(M, tokens_sample)  # the context linears keep their length
         X = g.standard_normal((m, K), dtype=np.float32)
         dY = g.standard_normal((m, N), dtype=np.float32)
         W = (0.02 * g.standard_normal((K, N), dtype=np.float32))
@@ -366,9 +376,10 @@ def run_ours(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             sample = 512 if args.config == "block" else 256
-            tps, it, threads, secs = cpu_sample(layers, r, alpha, sample, args.cpu_seconds)
+            tps, it, threads, secs = cpu_sample(layers, r, alpha, sample, args.cpu_seconds,
+                                                context=wl.get("context", CONTEXT))
             cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
-                   "sample": f"{args.config} linears fwd+bwd at {sample} tokens/sample (context {CONTEXT}), "
+                   "sample": f"{args.config} linears fwd+bwd at {sample} tokens/sample (context {wl.get('context', CONTEXT)}), "
                              f"numpy+OpenBLAS fp32, {it} iterations in {secs:.1f} s"}
         result = {
             "metric": "int8-W LoRA linear fwd+bwd tokens/s (TFLOP/s and % of roofline alongside)",
@@ -383,7 +394,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded normal activations, N(0,0.02) weights int8 per row)",
-            "config": {"workload": wl["name"], "tokens_per_sample": tokens, "context_tokens": CONTEXT,
+            "config": {"workload": wl["name"], "tokens_per_sample": tokens, "context_tokens": wl.get("context", CONTEXT),
                        "linears": [list(l) for l in layers], "rank": r, "alpha": alpha,
                        "weight_layout": "out-contiguous (reference)", "global_batch": world,
                        "parallelism": f"dp{world}",
@@ -426,8 +437,9 @@ def run_reference(args):
     sample = 512 if args.config == "block" else 256
     g = np.random.default_rng(0)
     data = []
+    ctx = wl.get("context", CONTEXT)
     for (_, M, K, N) in layers:
-        m = min(M, sample) if M > CONTEXT else M
+        m = M if M == ctx else min(M, sample)  # the context linears keep their length
         W = (0.02 * g.standard_normal((K, N), dtype=np.float32))
         q, s = oracle.quantize(W, 0)
         data.append((g.standard_normal((m, K), dtype=np.float32), g.standard_normal((m, N), dtype=np.float32), q,
@@ -466,7 +478,7 @@ def run_reference(args):
         "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": wl["name"], "tokens_per_sample": wl["tokens"], "sample_tokens": sample,
-                   "context_tokens": CONTEXT, "rank": r, "alpha": alpha, "parallelism": "host CPU"},
+                   "context_tokens": wl.get("context", CONTEXT), "rank": r, "alpha": alpha, "parallelism": "host CPU"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"each step: {wl['name']} fwd+bwd at {sample} tokens/sample through "
                                    "oracle/numpy_port.py (Julia is not installed, so the reference's CPU "
@@ -483,7 +495,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="block", choices=["block", "cfg1", "ffn8k"])
+    ap.add_argument("--config", default="block", choices=["block", "cfg1", "ffn8k", "wan14b", "ltx"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
