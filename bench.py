@@ -35,6 +35,19 @@ sys.path.insert(0, ROOT)
 HIDDEN, FFN, CONTEXT = 1536, 8960, 512
 
 
+L2_BYTES = 126 * 2 ** 20
+
+
+def l2_note(layers) -> str:
+    """How the timed steps stand against the 126 MB L2: the bytes of
+    activations, outputs and upstream gradients one step touches."""
+    step = sum(2 * (2 * M * K + 2 * M * N) for (_, M, K, N) in layers)
+    if step > 2 * L2_BYTES:
+        return f"inputs larger than L2 ({step / 2 ** 30:.1f} GB of activations and gradients per step)"
+    return (f"inputs fit in L2 ({step / 2 ** 20:.0f} MB of activations and gradients per step); "
+            "steps run back to back without a flush (warm L2)")
+
+
 def block_layers(tokens: int, context: int = CONTEXT, hidden: int = HIDDEN, ffn: int = FFN):
     """(name, M, K, N) of the ten linears of a DiT block (Wan 2.1 1.3B by
     default): self-attention q/k/v/o, cross-attention q/o over the tokens and
@@ -398,7 +411,7 @@ def run_ours(args):
                        "linears": [list(l) for l in layers], "rank": r, "alpha": alpha,
                        "weight_layout": "out-contiguous (reference)", "global_batch": world,
                        "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2 (about 5 GB of activations and gradients per step)"},
+                       "l2": l2_note(layers)},
             "tflops": flops * world * args.steps / (ms / 1e3) / 1e12,
             "roofline": {"bound": "tensor", "kernel": "q8ts_gemm_kernel (forward Y and dX)",
                          "achieved": q8_tflops, "peak": peak, "unit": "TFLOP/s",
