@@ -14,6 +14,7 @@ from .lowvram import (  # noqa: F401
     QuantizedMatrix,
     check_device_status,
     dropout_mask,
+    frozen_weight_transfer,
     gated_residual,
     gated_residual_backward,
     layernorm_modulate,
@@ -22,6 +23,7 @@ from .lowvram import (  # noqa: F401
     lora_backward,
     lora_forward,
     lora_forward_gelu,
+    lora_parameters,
     materialize_weight,
     merged_weight,
     quantize_frozen_matrix,

@@ -12,6 +12,8 @@ _weight_mul                     :func:`weight_mul` (quantization.jl:73-74)
 _weight_transpose_mul           :func:`weight_transpose_mul` (quantization.jl:75-76)
 DenseLayer / linear             :class:`DenseLayer`, :func:`linear` (layers/linear.jl:1-46)
 LoRALinear                      :class:`LoRALinear` (layers/lora.jl:1-35)
+lora_parameters                 :func:`lora_parameters` (lora.jl:36-37)
+frozen_weight_transfer          :func:`frozen_weight_transfer` (quantization.jl:78-140)
 lora_forward                    :func:`lora_forward` (lora.jl:56-95)
 lora_backward                   :func:`lora_backward` (lora.jl:106-118)
 merged_weight                   :func:`merged_weight` (lora.jl:120-122)
@@ -287,6 +289,58 @@ class LoRALinear:
 def set_adapter_enabled(layer: LoRALinear, enabled: bool) -> LoRALinear:
     layer.enabled = bool(enabled)
     return layer
+
+
+def lora_parameters(layer: LoRALinear) -> dict:
+    """The trainable tensors of a layer (lora.jl:36-37): A and B, plus the
+    bias when it is trained."""
+    return dict(A=layer.A, B=layer.B, bias=layer.bias) if layer.train_bias else dict(A=layer.A, B=layer.B)
+
+
+_PRECISIONS = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+class FrozenWeightTransfer:
+    """Moves frozen weights to their compute form (quantization.jl:78-85,
+    111-140): with ``quantization="int8"`` a floating-point weight becomes a
+    :class:`QuantizedMatrix` on the device through the GPU quantiser (the
+    weight's memory layout is kept), and a QuantizedMatrix is moved as is;
+    otherwise the weight is cast to the compute precision."""
+
+    def __init__(self, device, precision: str, quantization: str = "none"):
+        self.device = torch.device(device)
+        self.precision = precision
+        self.dtype = _PRECISIONS[precision]
+        self.quantization = quantization
+
+    def __call__(self, weight):
+        if self.quantization == "int8":
+            if isinstance(weight, QuantizedMatrix):
+                return QuantizedMatrix(weight.values.to(self.device), weight.scales.to(self.device), self.dtype)
+            return quantize_frozen_matrix(weight.to(self.device), self.dtype)
+        if isinstance(weight, QuantizedMatrix):
+            return materialize_weight(QuantizedMatrix(weight.values.to(self.device), weight.scales.to(self.device),
+                                                      weight.dtype), self.dtype)
+        return weight.to(self.device, self.dtype)
+
+
+def frozen_weight_transfer(device, precision: str, quantization: str = "none",
+                           cpu_offload: bool = False) -> FrozenWeightTransfer:
+    """frozen_weight_transfer (quantization.jl:87-101), with the reference's
+    argument errors.  Two differences: bf16 compute is accepted with Int8
+    weights (the reference rejects it; these kernels support it), and CPU
+    weight offload is not provided (it is outside this path)."""
+    if quantization not in ("none", "int8"):
+        raise ValueError("frozen weight quantization must be none or int8")
+    if precision not in _PRECISIONS:
+        raise ValueError(f"unknown precision {precision}")
+    if cpu_offload:
+        if torch.device(device).type != "cuda":
+            raise ValueError("CPU weight offloading requires device=cuda")
+        raise NotImplementedError("CPU weight offloading is not provided by the native int8 path")
+    if quantization == "int8" and torch.device(device).type != "cuda":
+        raise ValueError("int8 frozen weights run on the GPU path (device=cuda)")
+    return FrozenWeightTransfer(device, precision, quantization)
 
 
 def _colmajor(t: torch.Tensor, dtype) -> torch.Tensor:

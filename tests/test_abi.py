@@ -111,3 +111,26 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(nat, "_lib", None)
     with pytest.raises(RuntimeError, match="not found"):
         nat.lib()
+
+
+def test_layer_api_mirrors():
+    """lora_parameters (lora.jl:36-37) and frozen_weight_transfer's argument
+    errors (quantization.jl:87-101), which need no GPU."""
+    import torch
+    from reels_b200 import LoRALinear, QuantizedMatrix, frozen_weight_transfer, lora_parameters
+    qm = QuantizedMatrix(torch.zeros(6, 4, dtype=torch.int8), torch.ones(6), torch.float16)
+    A = torch.zeros(2, 4, dtype=torch.float16)
+    B = torch.zeros(6, 2, dtype=torch.float16)
+    layer = LoRALinear(qm, None, A, B, 2.0)
+    assert set(lora_parameters(layer)) == {"A", "B"}
+    trained = LoRALinear(qm, torch.zeros(6, dtype=torch.float16), A, B, 2.0, train_bias=True)
+    assert set(lora_parameters(trained)) == {"A", "B", "bias"}
+    with pytest.raises(ValueError, match="none or int8"):
+        frozen_weight_transfer("cuda", "fp16", quantization="int4")
+    with pytest.raises(ValueError, match="requires device=cuda"):
+        frozen_weight_transfer("cpu", "fp16", cpu_offload=True)
+    with pytest.raises(ValueError, match="GPU path"):
+        frozen_weight_transfer("cpu", "fp16", quantization="int8")
+    t = frozen_weight_transfer("cpu", "fp32")
+    w = torch.ones(3, 2, dtype=torch.float16)
+    assert t(w).dtype == torch.float32

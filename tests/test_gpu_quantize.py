@@ -98,3 +98,20 @@ def test_materialise_bit_exact(torch_cuda, layout):
     assert np.array_equal(f16, oracle.dequantize_f16_bits(q, s, 1))
     bf = materialize_weight(qm, torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16)
     assert np.array_equal(bf, oracle.dequantize_bf16_bits(q, s, 1))
+
+
+def test_frozen_weight_transfer_int8(torch_cuda):
+    """frozen_weight_transfer (quantization.jl:87-140) with int8: a host fp32
+    weight becomes a device QuantizedMatrix equal to the oracle's bytes, and
+    moving a QuantizedMatrix keeps its values and scales."""
+    torch = torch_cuda
+    from reels_b200 import frozen_weight_transfer
+    w = (0.02 * np.random.default_rng(4).standard_normal((64, 32))).astype(np.float32)
+    transfer = frozen_weight_transfer("cuda", "fp16", quantization="int8")
+    qm = transfer(torch.from_numpy(w))
+    assert qm.values.is_cuda and qm.values.dtype == torch.int8 and qm.dtype == torch.float16
+    q_ref, s_ref = oracle.quantize(w, layout=1)
+    assert np.array_equal(qm.values.cpu().numpy(), q_ref)
+    assert np.array_equal(qm.scales.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+    moved = transfer(qm)
+    assert torch.equal(moved.values, qm.values) and torch.equal(moved.scales, qm.scales)
