@@ -216,3 +216,27 @@ def test_gelu_tanh_float16_reference_case():
     h = oracle.gelu_tanh(v.astype(np.float32)).astype(np.float16).astype(np.float32)
     ref = oracle.gelu_tanh(v.astype(np.float32))
     assert np.allclose(h, ref, rtol=2e-3, atol=2e-4)
+
+
+def test_dropout_oracle_matches_numpy():
+    """oracle.lora_dropout (the forward and backward with the adapter fed
+    Z and its dx part scaled per element) against an fp64 numpy statement."""
+    rng = np.random.default_rng(12)
+    M, K, N, r, alpha = 9, 24, 16, 4, 8.0
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    Wm = (0.02 * rng.standard_normal((K, N))).astype(np.float32)
+    q, s = oracle.quantize(Wm, 0)
+    A = rng.standard_normal((K, r)).astype(np.float32)
+    B = rng.standard_normal((r, N)).astype(np.float32)
+    dY = rng.standard_normal((M, N)).astype(np.float32)
+    keep = (rng.random((M, K)) > 0.3).astype(np.float32)
+    Z = (X * keep / np.float32(0.7)).astype(np.float32)
+    Y, dX, dA, dB = oracle.lora_dropout(X, Z, dY, q, s, 0, A, B, alpha, keep / np.float32(0.7))
+    W = oracle.dequantize_f32(q, s, 0).astype(np.float64)  # [K][N]
+    sc = float(np.float32(alpha / r))
+    T = Z.astype(np.float64) @ A
+    G = dY.astype(np.float64) @ B.T
+    assert np.allclose(Y, X @ W + sc * T @ B, rtol=1e-5, atol=1e-5)
+    assert np.allclose(dX, dY @ W.T + sc * (G @ A.T) * (keep / np.float32(0.7)), rtol=1e-5, atol=1e-5)
+    assert np.allclose(dA, sc * Z.T.astype(np.float64) @ G, rtol=1e-5, atol=1e-5)
+    assert np.allclose(dB, sc * T.T @ dY, rtol=1e-5, atol=1e-5)
