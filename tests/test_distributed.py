@@ -105,3 +105,56 @@ def test_init_rejects_bad_world():
         rd.init_distributed(backend="mpi", world_size=2, rank=0)
     with pytest.raises(ValueError):
         rd.init_distributed(backend="gloo", world_size=2, rank=3)
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 leaves before the gradient exchange (it exits between steps,
+    with nothing in flight); rank 0 must see an error from its next
+    collective within the process group's timeout instead of waiting."""
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import time
+    from reels_b200 import distributed as rd
+    rt = rd.init_distributed(backend="gloo", timeout_seconds=5)
+    rd.distributed_barrier(rt)  # both ranks are up
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()  # the message is sent before the process goes
+        os._exit(0)  # a rank that dies between steps
+    t0 = time.time()
+    try:
+        rd.allreduce_gradients(rt, [torch.ones(4)])
+        q.put((rank, "no error"))
+    except Exception as e:  # the failure, surfaced on the host
+        q.put((rank, ("error", type(e).__name__, time.time() - t0)))
+
+
+def test_peer_failure_surfaces_as_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=90) for _ in procs)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()  # this test's own child, by handle
+    assert res[1] == "left"
+    assert isinstance(res[0], tuple) and res[0][0] == "error", res[0]
+    assert res[0][2] < 60  # bounded by the process-group timeout, not a hang
+
+
+def test_closed_runtime_refuses_collectives():
+    from reels_b200 import distributed as rd
+    rt = rd.DistributedRuntime(rank=0, world_size=2, local_rank=0, backend="gloo")
+    rt.closed = True
+    with pytest.raises(ValueError, match="closed"):
+        rd.allreduce_gradients(rt, [torch.ones(2)])
+    with pytest.raises(ValueError, match="closed"):
+        rd.allreduce_mean(rt, torch.ones(2))
