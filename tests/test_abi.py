@@ -134,3 +134,47 @@ def test_layer_api_mirrors():
     t = frozen_weight_transfer("cpu", "fp32")
     w = torch.ones(3, 2, dtype=torch.float16)
     assert t(w).dtype == torch.float32
+
+
+C_CONSUMER = r"""
+#include <stdio.h>
+#include <string.h>
+#include "reels_lowvram.h"
+
+int main(void) {
+    int64_t info[7];
+    int8_t q[16];
+    float s[4];
+    if (reels_lowvram_abi_version() != REELS_LOWVRAM_ABI_VERSION) return 1;
+    if (reels_q8lora_workspace_bytes(32760, 1536, 8960, 32, REELS_BF16, REELS_PASS_BACKWARD) == 0) return 2;
+    if (reels_q8lora_saved_bytes(7, 3, REELS_BF16) != 48) return 3;
+    if (reels_q8_plan(32760, 1536, 8960, REELS_ACT_NONE, 148, info) != REELS_OK) return 4;
+    if (info[3] < 1 || info[5] * info[6] < 1) return 5;
+    if (reels_q8_quantize(NULL, REELS_F32, REELS_W_OUT_CONTIGUOUS, 4, 4, q, s, NULL) != REELS_EINVAL) return 6;
+    if (strlen(reels_lowvram_last_error()) == 0) return 7;
+    if (reels_opt_workspace_bytes(3) == 0) return 8;
+    printf("ok %lld\n", (long long)info[0]);
+    return 0;
+}
+"""
+
+
+@pytest.mark.parametrize("compiler,std", [("gcc", "-std=c99"), ("g++", "-std=c++17")])
+def test_header_serves_a_c_consumer(lib, tmp_path, compiler, std):
+    """include/reels_lowvram.h compiles warning-free as C99 and C++ and links
+    against the shared library, as a foreign-function binding sees it; the
+    calls made need no GPU."""
+    import shutil
+    import subprocess
+    if shutil.which(compiler) is None:
+        pytest.skip(f"{compiler} not installed")
+    src = tmp_path / ("consumer.c" if compiler == "gcc" else "consumer.cpp")
+    src.write_text(C_CONSUMER)
+    exe = tmp_path / "consumer"
+    libdir = os.path.dirname(nat.library_path())
+    cmd = [compiler, std, "-pedantic", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"),
+           str(src), "-o", str(exe), "-L", libdir, "-lreels_lowvram", f"-Wl,-rpath,{libdir}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0 and run.stdout.startswith("ok"), (run.returncode, run.stdout, run.stderr)
