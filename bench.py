@@ -20,6 +20,7 @@ instead; the reference itself is Julia and cannot run in this image.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -127,51 +128,96 @@ def q8_algorithmic_bytes(layers, r):
 
 
 # ---------------------------------------------------------------- clocks
+def smi_device(local_index: int) -> str:
+    """The nvidia-smi id of CUDA device ``local_index``: the matching entry of
+    CUDA_VISIBLE_DEVICES (an index or a UUID) when it is set, else the index."""
+    cvd = [e.strip() for e in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if e.strip()]
+    return cvd[local_index] if local_index < len(cvd) else str(local_index)
+
+
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi samples of SM clock and throttle reasons every INTERVAL_MS.
+    Each sample carries nvidia-smi's own timestamp, so only the samples taken
+    between :meth:`begin` and :meth:`end` (the timed region) are summarised,
+    whatever the pipe's buffering; with none inside, the one nearest the
+    region's middle is used and ``window`` says so."""
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    INTERVAL_MS = 100
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, command: str = "nvidia-smi"):
         self.proc = None
-        self.gpu = gpu_index
+        self.gpu = smi_device(gpu_index)
+        self.command = command
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                [self.command, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.INTERVAL_MS), "-i", self.gpu],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
+        # let the sampler come up before the timed region starts
+        time.sleep(2 * self.INTERVAL_MS / 1e3)
+
+    def begin(self):
+        self.t0 = datetime.datetime.now()
+
+    def end(self):
+        self.t1 = datetime.datetime.now()
+
+    @staticmethod
+    def _stamp(text: str):
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+            try:
+                return datetime.datetime.strptime(text, fmt)
+            except ValueError:
+                pass
+        return None
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.25)
+        time.sleep(2 * self.INTERVAL_MS / 1e3)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        return self.summarise(out)
+
+    def summarise(self, out: str):
+        rows = []
         for line in out.splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                sm, mx = float(parts[2]), float(parts[3])
             except ValueError:
                 continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() in ("active", "yes", "1"):
-                    reasons.add(nm)
-        if not sm:
+            reasons = {nm for nm, v in zip(self.REASONS, parts[6:10]) if v.lower() in ("active", "yes", "1")}
+            rows.append((self._stamp(parts[0]), sm, mx, reasons))
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
-                "reasons": sorted(reasons)}
+        window = "timed region"
+        if self.t0 is not None and self.t1 is not None and all(r[0] is not None for r in rows):
+            inside = [r for r in rows if self.t0 <= r[0] <= self.t1]
+            if not inside:
+                mid = self.t0 + (self.t1 - self.t0) / 2
+                inside = [min(rows, key=lambda r: abs((r[0] - mid).total_seconds()))]
+                window = "nearest sample to the timed region"
+            rows = inside
+        else:
+            window = "whole sampler run (timestamps unavailable)"
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": max(r[2] for r in rows),
+                "samples": len(rows), "window": window,
+                "reasons": sorted(set().union(*(r[3] for r in rows)))}
 
 
 # ----------------------------------------------------------- CPU baseline
@@ -293,17 +339,19 @@ def run_ours(args):
 
     # ---------------- device-timed region ----------------
     clocks = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    clocks.start()
+    nat.profile_enable(True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    nat.profile_enable(True)
-    clocks.start()
+    clocks.begin()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    clocks.end()
     clk = clocks.stop()
     q8_ms, q8_n, q8_flops, launches = nat.profile_read()
     nat.profile_enable(False)

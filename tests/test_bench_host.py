@@ -1,0 +1,95 @@
+"""CPU checks of bench.py's host logic: the clock sampler's timed-region
+window (with a stand-in for nvidia-smi), the device-id mapping and the
+algorithmic FLOP count the roofline divides."""
+import datetime
+import os
+import stat
+import sys
+import time
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def _line(t, sm, reasons=("Not Active",) * 4):
+    return ", ".join([t.strftime("%Y/%m/%d %H:%M:%S.%f")[:-3], "0", str(sm), "1965", "700.0", "0x0"] + list(reasons))
+
+
+def test_summary_keeps_only_the_timed_region():
+    s = bench.ClockSampler(0)
+    base = datetime.datetime(2026, 1, 1, 12, 0, 0)
+    s.t0, s.t1 = base + datetime.timedelta(seconds=1), base + datetime.timedelta(seconds=2)
+    idle = [_line(base + datetime.timedelta(milliseconds=100 * i), 1965) for i in range(5)]
+    load = [_line(base + datetime.timedelta(milliseconds=1000 + 100 * i), 1800 + i,
+                  ("Not Active", "Not Active", "Not Active", "Active")) for i in range(1, 10)]
+    after = [_line(base + datetime.timedelta(milliseconds=2500), 1965)]
+    out = s.summarise("\n".join(idle + load + after))
+    assert out["samples"] == 9 and out["sm_mhz"] == 1805 and out["window"] == "timed region"
+    assert out["reasons"] == ["sw_power_cap"] and out["sm_max_mhz"] == 1965
+
+
+def test_summary_falls_back_to_the_nearest_sample():
+    s = bench.ClockSampler(0)
+    base = datetime.datetime(2026, 1, 1, 12, 0, 0)
+    s.t0, s.t1 = base + datetime.timedelta(milliseconds=130), base + datetime.timedelta(milliseconds=170)
+    out = s.summarise("\n".join([_line(base, 1965), _line(base + datetime.timedelta(milliseconds=190), 1700),
+                                 "garbage", ""]))
+    assert out["samples"] == 1 and out["sm_mhz"] == 1700 and out["window"].startswith("nearest")
+    assert s.summarise("") is None
+
+
+def test_slowdown_reasons_are_reported():
+    s = bench.ClockSampler(0)
+    now = datetime.datetime(2026, 1, 1)
+    s.t0, s.t1 = now, now + datetime.timedelta(seconds=1)
+    out = s.summarise(_line(now + datetime.timedelta(milliseconds=500), 1200,
+                            ("Active", "Not Active", "Active", "Not Active")))
+    assert out["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+
+
+def test_sampler_process_round_trip(tmp_path):
+    """start/begin/end/stop against a stand-in that prints a timestamped
+    sample every 20 ms until it is terminated."""
+    fake = tmp_path / "fake-smi"
+    fake.write_text(f"#!{sys.executable}\n"
+                    "import datetime, sys, time\n"
+                    "while True:\n"
+                    "    t = datetime.datetime.now().strftime('%Y/%m/%d %H:%M:%S.%f')[:-3]\n"
+                    "    print(t + ', 0, 1850, 1965, 800.0, 0x4, Not Active, Not Active, Not Active, Active', flush=True)\n"
+                    "    time.sleep(0.02)\n")
+    fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
+    s = bench.ClockSampler(0, command=str(fake))
+    s.start()
+    s.begin()
+    time.sleep(0.3)
+    s.end()
+    out = s.stop()
+    assert out is not None and out["window"] == "timed region" and out["samples"] >= 3
+    assert out["sm_mhz"] == 1850 and out["reasons"] == ["sw_power_cap"]
+
+
+def test_missing_sampler_gives_no_clock_record():
+    s = bench.ClockSampler(0, command="/nonexistent/nvidia-smi")
+    s.start()
+    s.begin()
+    s.end()
+    assert s.stop() is None
+
+
+def test_smi_device_follows_visible_devices(monkeypatch):
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "5,GPU-1234")
+    assert bench.smi_device(0) == "5" and bench.smi_device(1) == "GPU-1234" and bench.smi_device(2) == "2"
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.smi_device(3) == "3"
+
+
+def test_step_flops_match_the_algorithmic_count():
+    # config 1: 4*M*N*K + 6*M*r*(K+N) = 70.5 G + 1.29 G
+    f = bench.step_flops([("ffn_up", 1280, 1536, 8960)], 16)
+    assert f == pytest.approx(71.75e9, rel=1e-3)
+    layers = bench.block_layers(32760)
+    assert len(layers) == 10 and sum(1 for l in layers if l[1] == 512) == 2
