@@ -120,9 +120,10 @@ class QuantizedMatrix:
         return _weight_layout(self.values)
 
     def __getitem__(self, idx):
-        # quantization.jl:18-19: T(values[i, j]) * T(scales[i])
+        # quantization.jl:18-19: T(values[i, j]) * T(scales[i]), the product
+        # taken in T (for 16-bit T the scale is rounded to T first)
         i, j = idx
-        return (self.values[i, j].to(torch.float32) * self.scales[i]).to(self.dtype)
+        return self.values[i, j].to(self.dtype) * self.scales[i].to(self.dtype)
 
 
 def _weight_layout(values: torch.Tensor) -> int:

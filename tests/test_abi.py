@@ -136,6 +136,21 @@ def test_layer_api_mirrors():
     assert t(w).dtype == torch.float32
 
 
+def test_quantized_matrix_getindex_rounds_the_scale_first():
+    """getindex (quantization.jl:18-19) is T(q) * T(s): for Float16 the
+    scale is rounded to Float16 before the product, so 127 * (1/3) gives
+    42.3125, not the once-rounded 42.34375."""
+    import torch
+    from reels_b200 import QuantizedMatrix
+    s = torch.tensor([1.0 / 3.0, 0.5], dtype=torch.float32)
+    q = torch.tensor([[127, -3], [5, 0]], dtype=torch.int8)
+    h = QuantizedMatrix(q, s, torch.float16)
+    assert h[0, 0].item() == 42.3125 and h[0, 0].dtype == torch.float16
+    assert h[1, 0].item() == 2.5 and h[1, 1].item() == 0.0
+    f = QuantizedMatrix(q, s, torch.float32)
+    assert f[0, 0].item() == float(torch.tensor(127.0) * s[0])
+
+
 C_CONSUMER = r"""
 #include <stdio.h>
 #include <string.h>
