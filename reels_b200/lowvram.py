@@ -274,8 +274,9 @@ class LoRALinear:
         self.base_bias = bias
         self.A = A
         self.B = B
-        self.alpha = float(alpha)
-        self.dropout = float(dropout)
+        # alpha and dropout are Float32 fields in the reference (lora.jl:6-7)
+        self.alpha = _f32(alpha)
+        self.dropout = _f32(dropout)
         self.enabled = bool(enabled)
         self.train_bias = bool(train_bias)
 
@@ -285,6 +286,10 @@ class LoRALinear:
 
     def __call__(self, x, **kw):
         return lora_forward(self, x, **kw)
+
+
+def _f32(v) -> float:
+    return torch.tensor(float(v), dtype=torch.float32).item()
 
 
 def set_adapter_enabled(layer: LoRALinear, enabled: bool) -> LoRALinear:
@@ -533,7 +538,7 @@ def saved_buffer(layer: LoRALinear, x: torch.Tensor) -> torch.Tensor:
 def merged_weight(layer: LoRALinear) -> torch.Tensor:
     """merged_weight (lora.jl:120-122), fp32 (out, in) on the layer's device."""
     w = materialize_weight(layer.weight, torch.float32)
-    s = layer.alpha / layer.rank
+    s = torch.tensor(layer.alpha, dtype=torch.float32, device=w.device) / layer.rank   # Float32 / Int
     return w + s * (layer.B.float() @ layer.A.float())
 
 

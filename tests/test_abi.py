@@ -193,3 +193,16 @@ def test_header_serves_a_c_consumer(lib, tmp_path, compiler, std):
     assert res.returncode == 0, res.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0 and run.stdout.startswith("ok"), (run.returncode, run.stdout, run.stderr)
+
+
+def test_lora_fields_are_float32():
+    """alpha and dropout are Float32 fields (lora.jl:6-7): the adapter scale
+    alpha/rank is formed from the rounded alpha."""
+    import torch
+    from reels_b200 import LoRALinear, QuantizedMatrix
+    qm = QuantizedMatrix(torch.zeros(6, 4, dtype=torch.int8), torch.ones(6), torch.float32)
+    layer = LoRALinear(qm, None, torch.zeros(3, 4), torch.zeros(6, 3), 0.1, dropout=0.3)
+    assert layer.alpha == float(torch.tensor(0.1, dtype=torch.float32)) and layer.alpha != 0.1
+    assert layer.dropout == float(torch.tensor(0.3, dtype=torch.float32))
+    with pytest.raises(ValueError, match="dropout"):
+        LoRALinear(qm, None, torch.zeros(3, 4), torch.zeros(6, 3), 1.0, dropout=1.0)
