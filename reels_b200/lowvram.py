@@ -67,6 +67,18 @@ def _require_cuda(*tensors):
             raise ValueError("low-VRAM int8 kernels require CUDA tensors (no CPU path)")
 
 
+def _check_numel(t: Optional[torch.Tensor], n: int, what: str, device=None):
+    """The kernels read exactly ``n`` entries of ``t``: a mismatch is a
+    DimensionMismatch in the reference's broadcasts, and an out-of-bounds
+    read here, so it is refused before any launch."""
+    if t is None:
+        return
+    if t.numel() != n:
+        raise ValueError(f"{what} must have {n} entries, found {t.numel()} (shape {tuple(t.shape)})")
+    if device is not None and t.device != device:
+        raise ValueError(f"{what} is on {t.device}, the input on {device}")
+
+
 class _Workspace:
     """Scratch buffer per (device, stream), grown on demand by the caller
     side (the native library itself never allocates).  One buffer per stream:
@@ -200,6 +212,7 @@ def weight_mul(weight: QuantizedMatrix, x: torch.Tensor, bias: Optional[torch.Te
     _require_cuda(x, weight.values)
     xf = _flat(x, K)
     M = xf.shape[0]
+    _check_numel(bias, N, "bias", x.device)
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     dt = _dt(x.dtype)
     ws, wsn = _workspace(x.device, M, K, N, 0, dt, nat.PASS_FORWARD)
@@ -383,6 +396,7 @@ def _lora_forward_dropout(layer, x, saved, seed, stream):
     xf = _flat(x, K)
     M = xf.shape[0]
     dt = _dt(x.dtype)
+    _check_numel(layer.bias, N, "bias", x.device)
     b = layer.bias.contiguous().to(x.dtype) if layer.bias is not None else None
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     r = layer.rank
@@ -426,6 +440,7 @@ def _lora_forward(layer, x, training, saved, act, keep_pre):
     M = xf.shape[0]
     dt = _dt(x.dtype)
     active_bias = layer.base_bias if (layer.train_bias and not layer.enabled) else layer.bias
+    _check_numel(active_bias, N, "bias", x.device)
     b = active_bias.contiguous().to(x.dtype) if active_bias is not None else None
     y = torch.empty((M, N), dtype=x.dtype, device=x.device)
     pre = torch.empty((M, N), dtype=x.dtype, device=x.device) if keep_pre else None
@@ -490,6 +505,14 @@ def lora_backward(layer: LoRALinear, x: torch.Tensor, dy: torch.Tensor, saved: O
     B_mem = _colmajor(layer.B, x.dtype)
     accumulate = dA_acc is not None
     if accumulate:
+        if dB_acc is None:
+            raise ValueError("dA_acc and dB_acc are given together")
+        if tuple(dA_acc.shape) != (r, K) or tuple(dB_acc.shape) != (N, r):
+            raise ValueError("gradient accumulators must have the shapes of A (rank, in) and B (out, rank)")
+        if dA_acc.dtype != torch.float32 or dB_acc.dtype != torch.float32:
+            raise ValueError("gradient accumulators must be column-major fp32")
+        if dA_acc.device != x.device or dB_acc.device != x.device:
+            raise ValueError("gradient accumulators must be on the input's device")
         dA_mem, dB_mem = dA_acc.t(), dB_acc.t()
         if not (dA_mem.is_contiguous() and dB_mem.is_contiguous()):
             raise ValueError("gradient accumulators must be column-major fp32")
@@ -615,6 +638,12 @@ def layernorm_modulate(x: torch.Tensor, scale: Optional[torch.Tensor] = None, sh
     xf = _flat(x, K)
     M = xf.shape[0]
     tps = M if tokens_per_sample is None else int(tokens_per_sample)
+    if tps <= 0 and M > 0:
+        raise ValueError("tokens_per_sample must be positive")
+    batch = max((M + max(tps, 1) - 1) // max(tps, 1), 1)
+    for t, n, what in ((scale, batch * K, "scale"), (shift, batch * K, "shift"), (weight, K, "LayerNorm weight"),
+                       (bias, K, "LayerNorm bias")):
+        _check_numel(t, n, what, x.device)
     out = torch.empty_like(xf)
     args = [t.contiguous().to(x.dtype) if t is not None else None for t in (scale, shift, weight, bias)]
     code = nat.lib().reels_layernorm_modulate(xf.data_ptr(), M, K, max(tps, 1), *[_ptr(t) for t in args],
@@ -632,11 +661,15 @@ def layernorm_modulate_backward(x: torch.Tensor, dout: torch.Tensor, scale: Opti
     (modulation.jl:13-22), as ``(dx, dscale, dshift)``."""
     K = x.shape[-1]
     _require_cuda(x, dout)
+    if dout.shape != x.shape:
+        raise ValueError("dout must have the shape of x")
     xf = _flat(x, K)
     df = _flat(dout, K)
     M = xf.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
     batch = max((M + tps - 1) // tps, 1)
+    for t, n, what in ((scale, batch * K, "scale"), (weight, K, "LayerNorm weight"), (bias, K, "LayerNorm bias")):
+        _check_numel(t, n, what, x.device)
     dx = torch.empty_like(xf)
     dscale = dshift = None
     ws, wsn = None, 0
@@ -688,7 +721,11 @@ def gated_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, tokens_
     xf, yf = _flat(x, N), _flat(y, N)
     M = xf.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
-    o = torch.empty_like(xf) if out is None else _flat(out, N)
+    _check_numel(gate, max((M + tps - 1) // tps, 1) * N, "gate", x.device)
+    if out is not None and (out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous()
+                            or out.device != x.device):
+        raise ValueError("out must be a contiguous tensor of x's shape, dtype and device")
+    o = torch.empty_like(xf) if out is None else out.view(-1, N)
     g = gate.contiguous().to(x.dtype)
     nat.check("gated_residual", nat.lib().reels_gated_residual(xf.data_ptr(), yf.data_ptr(), g.data_ptr(), M, N, tps,
                                                                _dt(x.dtype), o.data_ptr(), _stream(x.device)))
@@ -701,10 +738,13 @@ def gated_residual_backward(dout: torch.Tensor, y: torch.Tensor, gate: torch.Ten
     gradient is ``dout``); dgate is fp32 (batch, N)."""
     N = dout.shape[-1]
     _require_cuda(dout, y, gate)
+    if y.shape != dout.shape or y.dtype != dout.dtype:
+        raise ValueError("y and dout must have the same shape and dtype")
     df, yf = _flat(dout, N), _flat(y, N)
     M = df.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
     batch = max((M + tps - 1) // tps, 1)
+    _check_numel(gate, batch * N, "gate", dout.device)
     dy = torch.empty_like(df)
     dgate, ws, wsn = None, None, 0
     if gate_grad:

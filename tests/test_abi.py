@@ -206,3 +206,47 @@ def test_lora_fields_are_float32():
     assert layer.dropout == float(torch.tensor(0.3, dtype=torch.float32))
     with pytest.raises(ValueError, match="dropout"):
         LoRALinear(qm, None, torch.zeros(3, 4), torch.zeros(6, 3), 1.0, dropout=1.0)
+
+
+def test_host_side_size_checks(monkeypatch):
+    """Operands whose sizes disagree with the call are refused on the host
+    before any launch (the kernels would read or write out of bounds); the
+    device requirement is lifted here so the checks run without a GPU."""
+    import torch
+    from reels_b200 import (LoRALinear, QuantizedMatrix, gated_residual, gated_residual_backward, layernorm_modulate,
+                            layernorm_modulate_backward, lora_backward, lora_forward, weight_mul)
+    from reels_b200 import lowvram
+    monkeypatch.setattr(lowvram, "_require_cuda", lambda *a: None)
+    x = torch.zeros(8, 4, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="scale must have 8 entries"):
+        layernorm_modulate(x, torch.zeros(1, 4, dtype=torch.bfloat16), None, tokens_per_sample=4)
+    with pytest.raises(ValueError, match="LayerNorm weight"):
+        layernorm_modulate(x, None, None, weight=torch.zeros(5, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="tokens_per_sample"):
+        layernorm_modulate(x, None, None, tokens_per_sample=0)
+    with pytest.raises(ValueError, match="dout must have the shape"):
+        layernorm_modulate_backward(x, torch.zeros(8, 5, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="gate must have 8 entries"):
+        gated_residual(x, x, torch.zeros(1, 4, dtype=torch.bfloat16), tokens_per_sample=4)
+    with pytest.raises(ValueError, match="out must be a contiguous"):
+        gated_residual(x, x, torch.zeros(1, 4, dtype=torch.bfloat16), out=torch.zeros(4, 8, dtype=torch.bfloat16).t())
+    with pytest.raises(ValueError, match="y and dout"):
+        gated_residual_backward(x, x.float(), torch.zeros(1, 4))
+    qm = QuantizedMatrix(torch.zeros(6, 4, dtype=torch.int8), torch.ones(6), torch.bfloat16)
+    with pytest.raises(ValueError, match="bias must have 6 entries"):
+        weight_mul(qm, x, torch.zeros(5, dtype=torch.bfloat16))
+    layer = LoRALinear(qm, torch.zeros(7, dtype=torch.bfloat16), torch.zeros(2, 4, dtype=torch.bfloat16),
+                       torch.zeros(6, 2, dtype=torch.bfloat16), 2.0)
+    with pytest.raises(ValueError, match="bias must have 6 entries"):
+        lora_forward(layer, x)
+    layer.bias = None
+    dy = torch.zeros(8, 6, dtype=torch.bfloat16)
+    good_A, good_B = torch.zeros(4, 2).t(), torch.zeros(2, 6).t()
+    with pytest.raises(ValueError, match="shapes of A"):
+        lora_backward(layer, x, dy, dA_acc=torch.zeros(4, 3).t(), dB_acc=good_B)
+    with pytest.raises(ValueError, match="fp32"):
+        lora_backward(layer, x, dy, dA_acc=good_A.bfloat16(), dB_acc=good_B)
+    with pytest.raises(ValueError, match="column-major"):
+        lora_backward(layer, x, dy, dA_acc=torch.zeros(2, 4), dB_acc=good_B)
+    with pytest.raises(ValueError, match="together"):
+        lora_backward(layer, x, dy, dA_acc=good_A)
