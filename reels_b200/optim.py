@@ -66,7 +66,9 @@ def learning_rate(base: float, kind: str, warmup_steps: int, step: int, total: i
     or cosine), as an fp32 value."""
     f32 = np.float32
     if warmup_steps > 0 and step <= warmup_steps:
-        return float(f32(base * step / warmup_steps))
+        # base is the Float32 training.learning_rate (config/schema.jl:40):
+        # Float32 * Int and Float32 / Int each round to Float32
+        return float(f32(f32(base) * f32(step)) / f32(warmup_steps))
     progress = f32(min(max((step - warmup_steps) / max(total - warmup_steps, 1), 0.0), 1.0))
     if kind == "constant":
         return float(f32(base))

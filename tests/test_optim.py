@@ -37,6 +37,10 @@ def test_learning_rate_schedule():
     cos = optim.learning_rate(2e-3, "cosine", 0, 30, 120)
     assert cos == pytest.approx(2e-3 * (1 + math.cos(math.pi * 0.25)) / 2, rel=1e-6)
     assert optim.learning_rate(1e-3, "linear", 0, 500, 100) == 0.0  # progress clamps at 1
+    # warm-up in Float32 arithmetic (base::Float32 * step / warm, each op
+    # rounded): at the last warm-up step 1f-4 * 5 / 5 is 9.999999f-5, not 1f-4
+    assert optim.learning_rate(1e-4, "constant", 5, 5, 100) == float(f32(9.999999e-05))
+    assert optim.learning_rate(3e-4, "cosine", 7, 5, 100) == float(f32(0.00021428571))
     with pytest.raises(ValueError):
         optim.learning_rate(1e-3, "step", 0, 1, 10)
 
