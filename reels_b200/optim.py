@@ -144,7 +144,8 @@ class AdamWState:
         for p, g, w in zip(params, grads, self.master):
             if g.dtype != torch.float32 or not g.is_contiguous() or g.numel() != w.numel() or p.numel() != w.numel():
                 raise ValueError("gradients must be contiguous fp32 tensors of the parameters' sizes")
-        key = (tuple(p.data_ptr() for p in params), tuple(g.data_ptr() for g in grads),
+        # the table holds pointers, element types and the decay flags
+        key = (tuple((p.data_ptr(), p.dtype) for p in params), tuple(g.data_ptr() for g in grads),
                tuple(bool(x) for x in mask) if mask is not None else None)
         if key == self._key and self._ws is not None:
             return self._ws
