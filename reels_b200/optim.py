@@ -142,7 +142,9 @@ class AdamWState:
         if mask is not None and len(mask) != len(params):
             raise ValueError("weight-decay mask and parameter lengths differ")
         for p, g, w in zip(params, grads, self.master):
-            if g.dtype != torch.float32 or not g.is_contiguous() or g.numel() != w.numel() or p.numel() != w.numel():
+            if p.dtype not in _DT or not p.is_contiguous() or p.numel() != w.numel() or p.device != w.device:
+                raise ValueError("parameters must be the contiguous fp32/fp16/bf16 tensors the state was made for")
+            if g.dtype != torch.float32 or not g.is_contiguous() or g.numel() != w.numel() or g.device != w.device:
                 raise ValueError("gradients must be contiguous fp32 tensors of the parameters' sizes")
         # the table holds pointers, element types and the decay flags
         key = (tuple((p.data_ptr(), p.dtype) for p in params), tuple(g.data_ptr() for g in grads),
