@@ -204,12 +204,23 @@ def load_quantized_linear(path: str, key: str, out_features: int, in_features: i
     return QuantizedMatrix(values=values, scales=scales, dtype=dtype)
 
 
+def cast_unquantized(tensors: Mapping[str, torch.Tensor], compute_dtype: torch.dtype) -> Dict[str, torch.Tensor]:
+    """The other tensors of an Int8 checkpoint in the compute type, as
+    quantized_umt5_state_dict does (text_encoder.jl:322-326): every
+    floating-point tensor except a ``.scale`` is cast; integer tensors and
+    the fp32 scales are kept."""
+    return {name: (t.to(compute_dtype) if t.is_floating_point() and not name.endswith(".scale") else t)
+            for name, t in tensors.items()}
+
+
 def quantize_checkpoint(src: str, dst: str, keys: Iterable[str], device="cuda",
                         compute_dtype: torch.dtype = torch.float16,
-                        metadata: Optional[Mapping[str, str]] = None) -> str:
+                        metadata: Optional[Mapping[str, str]] = None, cast_others: bool = True) -> str:
     """Convert the floating-point linears ``{key}.weight`` of ``src`` to Int8
     on the GPU (bit-exact quantiser) and write every tensor of ``src`` to
-    ``dst``, the listed linears as Int8 with their scales."""
+    ``dst``, the listed linears as Int8 with their scales.  With
+    ``cast_others`` the remaining floating-point tensors are written in
+    ``compute_dtype``, as the reference's Int8 writer does."""
     header = inspect_safetensors(src)
     keys = list(keys)
     wanted = {f"{k}.weight" for k in keys}
@@ -228,6 +239,8 @@ def quantize_checkpoint(src: str, dst: str, keys: Iterable[str], device="cuda",
     missing = [k for k in keys if k not in linears]
     if missing:
         raise KeyError(f"missing weights: {missing}")
+    if cast_others:
+        others = cast_unquantized(others, compute_dtype)
     info = dict(header.metadata)
     info.update(metadata or {})
     return write_quantized_checkpoint(dst, linears, others, compute_dtype, info)

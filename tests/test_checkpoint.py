@@ -178,3 +178,15 @@ def test_reference_streaming_io_case(tmp_path):
     raw = open(q, "rb").read()
     (n,) = struct.unpack("<Q", raw[:8])
     assert raw[8 + n:] == data
+
+
+def test_unquantized_tensors_take_the_compute_type():
+    """quantized_umt5_state_dict (text_encoder.jl:322-326): floating-point
+    tensors other than scales go to the compute type; integers and scales
+    are kept."""
+    t = {"norm.weight": torch.ones(4, dtype=torch.float32), "lin.weight.scale": torch.ones(4),
+         "lin.weight": torch.zeros(4, 4, dtype=torch.int8), "pos": torch.arange(3)}
+    out = ck.cast_unquantized(t, torch.float16)
+    assert out["norm.weight"].dtype == torch.float16
+    assert out["lin.weight.scale"].dtype == torch.float32
+    assert out["lin.weight"].dtype == torch.int8 and out["pos"].dtype == torch.int64
