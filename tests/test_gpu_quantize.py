@@ -66,6 +66,32 @@ def test_bit_exact_vs_oracle(torch_cuda, layout, wdtype, shape):
     assert np.array_equal(qm.values.cpu().numpy(), q_ref)
 
 
+@pytest.mark.parametrize("layout", [0, 1])
+def test_extreme_rows_bit_exact(torch_cuda, layout):
+    """Rows at the ends of fp32 (largest finite values, subnormal maxima and
+    scales, signed zeros, scale exactly 1 with .5 ties) and rows spanning
+    2^-140 .. 2^120: the GPU quantiser keeps gradual underflow as the
+    reference's fp32 division does."""
+    torch = torch_cuda
+    from reels_b200 import quantize_frozen_matrix
+    f = np.float32
+    tiny = np.finfo(f).tiny
+    rows = [[np.finfo(f).max, -np.finfo(f).max, 1.0, 0.0], [tiny, -tiny / 2, tiny / 8, 0.0],
+            [np.float32(1e-45), 0.0, -0.0, np.float32(-1e-45)], [0.0, 0.0, 3.0, 0.0], [-0.0, -0.0, -0.0, -0.0],
+            [127.0, 63.5, -0.5, 0.5], [1e30, 1e-30, -1e30, 2.5e29]]
+    g = np.random.default_rng(17)
+    e = g.integers(-140, 120, size=(40, 1))
+    rand = (g.standard_normal((40, 4)) * np.exp2(e)).astype(f)
+    W = np.concatenate([np.array(rows, f), rand])
+    Wt = _to_dev(torch, W)
+    if layout == 0:
+        Wt = Wt.t().contiguous().t()
+    qm = quantize_frozen_matrix(Wt)
+    q_ref, s_ref = oracle.quantize(W, 1)
+    assert np.array_equal(qm.scales.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+    assert np.array_equal(qm.values.cpu().numpy(), q_ref)
+
+
 def test_non_finite_weight_raises(torch_cuda):
     torch = torch_cuda
     from reels_b200 import quantize_frozen_matrix

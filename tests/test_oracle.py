@@ -47,6 +47,53 @@ def test_quantizer_matches_numpy_restatement():
     assert np.array_equal(q, qn)
 
 
+def _numpy_quantize(W):
+    m = np.abs(W).max(axis=1)
+    s = (m / np.float32(127)).astype(np.float32)
+    s[m == 0] = 1
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        qn = np.rint(np.clip(W / s[:, None], -127, 127)).astype(np.int8)
+    return qn, s
+
+
+def test_quantizer_extreme_rows_match_numpy():
+    """Rows at the ends of fp32 (largest finite values, subnormals, a lone
+    nonzero among zeros, mixed signs of zero) quantise identically in the C
+    oracle and the numpy statement; fp32 division with gradual underflow."""
+    f = np.float32
+    tiny = np.finfo(f).tiny
+    rows = [
+        [np.finfo(f).max, -np.finfo(f).max, 1.0, 0.0],
+        [tiny, -tiny / 2, tiny / 8, 0.0],                 # subnormal maxima and scales
+        [np.float32(1e-45), 0.0, -0.0, np.float32(-1e-45)],
+        [0.0, 0.0, 3.0, 0.0],
+        [-0.0, -0.0, -0.0, -0.0],
+        [127.0, 63.5, -0.5, 0.5],                         # exact scale 1: ties to even
+        [1e30, 1e-30, -1e30, 2.5e29],
+    ]
+    W = np.array(rows, f)
+    q, s = oracle.quantize(W, 1)
+    qn, sn = _numpy_quantize(W)
+    assert np.array_equal(s.view(np.uint32), sn.view(np.uint32))
+    assert np.array_equal(q, qn)
+    assert q[5].tolist() == [127, 64, 0, 0] and s[4] == 1
+
+
+def test_quantizer_random_scales_match_numpy():
+    """Rows whose magnitudes span 2^-140 .. 2^120, in both layouts."""
+    g = np.random.default_rng(17)
+    for trial in range(20):
+        e = g.integers(-140, 120, size=(32, 1))
+        W = (g.standard_normal((32, 48)) * np.exp2(e)).astype(np.float32)
+        W[g.random(W.shape) < 0.1] = 0
+        qn, sn = _numpy_quantize(W)
+        for layout in (0, 1):
+            Wm = np.ascontiguousarray(W.T) if layout == 0 else W
+            q, s = oracle.quantize(Wm, layout)
+            assert np.array_equal(s.view(np.uint32), sn.view(np.uint32)), trial
+            assert np.array_equal(q.T if layout == 0 else q, qn), trial
+
+
 def test_quantizer_rejects_non_finite():
     W = np.ones((3, 4), np.float32)
     W[1, 2] = np.nan
