@@ -62,12 +62,17 @@ extern "C" {
 #define REELS_PASS_BACKWARD 1
 #define REELS_PASS_DROPOUT 2 /* or-ed into the pass: room for the dropped-out input */
 
-/* execution paths reported by reels_lowvram_last_path() */
 /* Activation fused into a linear's output (forward) or its input's gradient
  * (backward). */
 #define REELS_ACT_NONE 0
 #define REELS_ACT_GELU_TANH 1 /* gelu_tanh, src/layers/linear.jl:61-68 */
 
+/* Empty inputs: every call that takes a token count M (or a length n)
+ * accepts 0.  Then nothing is read, the buffers sized by M may be NULL, and
+ * gradients of parameters (dA, dB, dscale, dshift, dgate) are zero-filled,
+ * or left unchanged when accumulating -- a sum over no tokens. */
+
+/* execution paths reported by reels_lowvram_last_path() */
 #define REELS_PATH_NONE 0
 #define REELS_PATH_TENSORCORE 1
 #define REELS_PATH_CUDACORE 2

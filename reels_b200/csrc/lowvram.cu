@@ -1187,9 +1187,11 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
                                void *saved, void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
-    if (!x || !q || !scales || !y) return fail("null x, q, scales or y");
+    // With M == 0 the token-sized buffers (x, y, pre, saved) may be NULL.
+    if (!q || !scales) return fail("null q or scales");
+    if (M > 0 && (!x || !y)) return fail("null x or y");
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
-    if (pre == y) return fail("pre and y must be different buffers");
+    if (pre && pre == y) return fail("pre and y must be different buffers");
     if (r > 0 && (!A || !B)) return fail("null LoRA A or B");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
     rc = check_dropout(dropout, M);
@@ -1297,19 +1299,22 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
                                 void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_common(M, K, N, r, dt, layout);
     if (rc) return rc;
-    if (!dy || !q || !scales) return fail("null dy, q or scales");
+    // With M == 0 the token-sized buffers (x, dy, pre_x, dx, saved) may be NULL.
+    if (!q || !scales) return fail("null q or scales");
+    if (M > 0 && !dy) return fail("null dy");
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
     if (act != REELS_ACT_NONE && dx && !pre_x) return fail("null pre-activation of x");
     if (act != REELS_ACT_NONE && dx && pre_x == dx) return fail("pre_x and dx must be different buffers");
     rc = check_dropout(dropout, M);
     if (rc) return rc;
     if (dropout > 0.0f && act != REELS_ACT_NONE) return fail("dropout is not combined with a fused activation");
-    if (r > 0 && (!A || !B || !dA || !dB || !x)) return fail("null x, A, B, dA or dB with r > 0");
+    if (r > 0 && (!A || !B || !dA || !dB)) return fail("null A, B, dA or dB with r > 0");
+    if (r > 0 && M > 0 && !x) return fail("null x with r > 0");
     if (r > 0 && !std::isfinite(alpha)) return fail("alpha must be finite");
     if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
     if (!dx && r == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
-    rc = bind_device(dy, &ds);
+    rc = bind_device(M > 0 ? dy : static_cast<const void *>(q), &ds);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (M == 0) {
@@ -1524,7 +1529,7 @@ int reels_q8lora_backward_act(const void *x, const void *dy, const int8_t *q, co
 }
 
 static int check_ln(const void *x, int64_t M, int64_t K, int64_t tps, float eps, int dt) {
-    if (!x) return fail("null x");
+    if (!x && M > 0) return fail("null x");
     if (M < 0 || K <= 0 || K > LN_MAX_K) return fail("LayerNorm needs 0 <= M and 0 < K <= " + std::to_string(LN_MAX_K));
     if (tps <= 0) return fail("tokens_per_sample must be positive");
     if (!(eps >= 0.0f) || !std::isfinite(eps)) return fail("epsilon must be finite and non-negative");
@@ -1545,7 +1550,7 @@ int reels_layernorm_modulate(const void *x, int64_t M, int64_t K, int64_t tokens
                              void *out, void *stream) {
     int rc = check_ln(x, M, K, tokens_per_sample, epsilon, dt);
     if (rc) return rc;
-    if (!out) return fail("null out");
+    if (!out && M > 0) return fail("null out");
     if (M == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
     rc = bind_device(x, &ds);
@@ -1573,11 +1578,11 @@ int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M
                                       void *stream) {
     int rc = check_ln(x, M, K, tokens_per_sample, epsilon, dt);
     if (rc) return rc;
-    if (!dout) return fail("null dout");
-    if (!dx) return fail("null dx (the parameter gradients reuse its row statistics)");
+    if (!dout && M > 0) return fail("null dout");
+    if (!dx && M > 0) return fail("null dx (the parameter gradients reuse its row statistics)");
     const bool params = dscale || dshift;
     const int64_t batch = cdiv(M, tokens_per_sample);
-    if (params) {
+    if (params && M > 0) {
         if (!workspace) return fail("null workspace; size it with reels_layernorm_modulate_workspace_bytes");
         if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("workspace must be 256-byte aligned");
         if (ws_bytes < reels_layernorm_modulate_workspace_bytes(M, K, tokens_per_sample))
@@ -1643,8 +1648,8 @@ int reels_gated_residual(const void *x, const void *y, const void *gate, int64_t
                          int64_t tokens_per_sample, int dt, void *out, void *stream) {
     int rc = check_gate(M, N, tokens_per_sample, dt);
     if (rc) return rc;
-    if (!x || !y || !gate || !out) return fail("null x, y, gate or out");
     if (M == 0) return ok(REELS_PATH_NONE);
+    if (!x || !y || !gate || !out) return fail("null x, y, gate or out");
     DeviceState *ds;
     rc = bind_device(x, &ds);
     if (rc) return rc;
@@ -1667,9 +1672,9 @@ int reels_gated_residual_backward(const void *dout, const void *y, const void *g
                                   void *workspace, size_t ws_bytes, void *stream) {
     int rc = check_gate(M, N, tokens_per_sample, dt);
     if (rc) return rc;
-    if (!dout || !gate) return fail("null dout or gate");
-    if (dgate && !y) return fail("dgate needs y");
-    if (dgate) {
+    if (M > 0 && (!dout || !gate)) return fail("null dout or gate");
+    if (M > 0 && dgate && !y) return fail("dgate needs y");
+    if (dgate && M > 0) {
         if (!workspace) return fail("null workspace; size it with reels_gated_residual_workspace_bytes");
         if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("workspace must be 256-byte aligned");
         if (ws_bytes < reels_gated_residual_workspace_bytes(M, N, tokens_per_sample)) return fail("workspace too small");
@@ -1811,7 +1816,7 @@ int reels_adamw_update(void *workspace, float lr, float beta1, float beta2, floa
 int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *scales, int layout, int64_t M,
                                   int64_t K, int64_t N, int act_dtype, void *dx, void *workspace, size_t ws_bytes,
                                   void *stream) {
-    if (!dx) return fail("null dx");
+    if (!dx && M > 0) return fail("null dx");
     return reels_q8lora_backward(nullptr, dy, q, scales, layout, nullptr, nullptr, nullptr, M, K, N, 0, 1.0f, 1.0f,
                                  act_dtype, dx, nullptr, nullptr, 0, workspace, ws_bytes, stream);
 }
@@ -1838,8 +1843,8 @@ extern "C" int reels_q8lora_forward_static_ws(const void *x, const int8_t *q, co
                                               void *stream) {
     int rc = check_common(M, K, N, r, act_dtype, layout);
     if (rc) return rc;
-    if (!x) return fail("null x");
     if (M == 0) return ok(REELS_PATH_NONE);
+    if (!x) return fail("null x");
     int dev = -1;
     cudaPointerAttributes attr;
     if (cudaPointerGetAttributes(&attr, x) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {

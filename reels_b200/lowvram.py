@@ -643,7 +643,8 @@ def layernorm_modulate(x: torch.Tensor, scale: Optional[torch.Tensor] = None, sh
     batch = max((M + max(tps, 1) - 1) // max(tps, 1), 1)
     for t, n, what in ((scale, batch * K, "scale"), (shift, batch * K, "shift"), (weight, K, "LayerNorm weight"),
                        (bias, K, "LayerNorm bias")):
-        _check_numel(t, n, what, x.device)
+        if M > 0:
+            _check_numel(t, n, what, x.device)
     out = torch.empty_like(xf)
     args = [t.contiguous().to(x.dtype) if t is not None else None for t in (scale, shift, weight, bias)]
     code = nat.lib().reels_layernorm_modulate(xf.data_ptr(), M, K, max(tps, 1), *[_ptr(t) for t in args],
@@ -668,6 +669,11 @@ def layernorm_modulate_backward(x: torch.Tensor, dout: torch.Tensor, scale: Opti
     M = xf.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
     batch = max((M + tps - 1) // tps, 1)
+    if M == 0:
+        # no tokens: the parameter gradients are sums over nothing
+        rows = scale.numel() // K if scale is not None else 1
+        z = (lambda: torch.zeros((rows, K), dtype=torch.float32, device=x.device)) if param_grads else (lambda: None)
+        return torch.empty_like(x), z(), z()
     for t, n, what in ((scale, batch * K, "scale"), (weight, K, "LayerNorm weight"), (bias, K, "LayerNorm bias")):
         _check_numel(t, n, what, x.device)
     dx = torch.empty_like(xf)
@@ -721,7 +727,8 @@ def gated_residual(x: torch.Tensor, y: torch.Tensor, gate: torch.Tensor, tokens_
     xf, yf = _flat(x, N), _flat(y, N)
     M = xf.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
-    _check_numel(gate, max((M + tps - 1) // tps, 1) * N, "gate", x.device)
+    if M > 0:
+        _check_numel(gate, max((M + tps - 1) // tps, 1) * N, "gate", x.device)
     if out is not None and (out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous()
                             or out.device != x.device):
         raise ValueError("out must be a contiguous tensor of x's shape, dtype and device")
@@ -744,6 +751,10 @@ def gated_residual_backward(dout: torch.Tensor, y: torch.Tensor, gate: torch.Ten
     M = df.shape[0]
     tps = max(M if tokens_per_sample is None else int(tokens_per_sample), 1)
     batch = max((M + tps - 1) // tps, 1)
+    if M == 0:
+        rows = gate.numel() // N
+        return torch.empty_like(dout), (torch.zeros((rows, N), dtype=torch.float32, device=dout.device)
+                                        if gate_grad else None)
     _check_numel(gate, batch * N, "gate", dout.device)
     dy = torch.empty_like(df)
     dgate, ws, wsn = None, None, 0

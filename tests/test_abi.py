@@ -85,6 +85,26 @@ def test_backward_rejects_null_gradients(lib):
     assert "dA" in _err(lib)
 
 
+def test_empty_inputs_accept_null_token_buffers(lib):
+    """M == 0 (and n == 0): the token-sized buffers may be NULL, the calls
+    succeed without reading anything, and none of these touches a GPU."""
+    p = ctypes.c_void_p(0x1000)
+    assert lib.reels_q8lora_forward(None, p, p, 0, p, p, None, 0, 16, 16, 2, 2.0, nat.BF16, None, None, None, 0,
+                                    None) == nat.OK
+    assert lib.reels_q8lora_forward_act(None, p, p, 0, p, p, None, 0, 16, 16, 2, 2.0, nat.BF16, nat.ACT_GELU_TANH,
+                                        None, None, None, None, 0, None) == nat.OK
+    assert lib.reels_q8_weight_mul(None, p, p, 1, None, 0, 16, 16, nat.F16, None, None, 0, None) == nat.OK
+    # dx only, no adapter: nothing to write
+    assert lib.reels_q8_weight_transpose_mul(None, p, p, 0, 0, 16, 16, nat.BF16, None, None, 0, None) == nat.OK
+    assert lib.reels_layernorm_modulate(None, 0, 16, 1, None, None, None, None, 1e-6, nat.BF16, None,
+                                        None) == nat.OK
+    assert lib.reels_gated_residual(None, None, None, 0, 16, 1, nat.BF16, None, None) == nat.OK
+    assert lib.reels_dropout_mask(0, 0.5, 1, 0, None, None) == nat.OK
+    # the weights themselves are never optional
+    assert lib.reels_q8lora_forward(None, None, p, 0, p, p, None, 0, 16, 16, 2, 2.0, nat.BF16, None, None, None,
+                                    0, None) == nat.EINVAL
+
+
 def test_activation_entry_points_reject_bad_arguments(lib):
     p = ctypes.c_void_p(0x1000)
     q = ctypes.c_void_p(0x2000)
@@ -250,3 +270,28 @@ def test_host_side_size_checks(monkeypatch):
         lora_backward(layer, x, dy, dA_acc=torch.zeros(2, 4), dB_acc=good_B)
     with pytest.raises(ValueError, match="together"):
         lora_backward(layer, x, dy, dA_acc=good_A)
+
+
+def test_empty_batches_through_the_layer_api(monkeypatch):
+    """The Python mirror with no tokens: shapes and the early returns of the
+    parameter-gradient pullbacks, on CPU (the native calls made here return
+    before any device work when M == 0)."""
+    import torch
+    from reels_b200 import (LoRALinear, QuantizedMatrix, gated_residual, gated_residual_backward, layernorm_modulate,
+                            layernorm_modulate_backward, lora_forward)
+    from reels_b200 import lowvram
+    monkeypatch.setattr(lowvram, "_require_cuda", lambda *a: None)
+    monkeypatch.setattr(lowvram, "_stream", lambda d: 0)
+    monkeypatch.setattr(lowvram, "_workspace", lambda *a: (None, 0))
+    qm = QuantizedMatrix(torch.zeros(6, 4, dtype=torch.int8).t().contiguous().t(), torch.ones(6), torch.bfloat16)
+    layer = LoRALinear(qm, None, torch.zeros(2, 4, dtype=torch.bfloat16), torch.zeros(6, 2, dtype=torch.bfloat16), 2.0)
+    x = torch.empty((3, 0, 4), dtype=torch.bfloat16)
+    assert tuple(lora_forward(layer, x).shape) == (3, 0, 6)
+    scale = torch.zeros((2, 4), dtype=torch.bfloat16)
+    assert tuple(layernorm_modulate(x, scale, scale, tokens_per_sample=5).shape) == (3, 0, 4)
+    dx, ds, dh = layernorm_modulate_backward(x, x, scale, param_grads=True)
+    assert tuple(dx.shape) == (3, 0, 4) and tuple(ds.shape) == (2, 4) and not ds.any() and not dh.any()
+    gate = torch.ones((2, 4), dtype=torch.bfloat16)
+    assert tuple(gated_residual(x, x, gate).shape) == (3, 0, 4)
+    dyr, dg = gated_residual_backward(x, x, gate)
+    assert tuple(dyr.shape) == (3, 0, 4) and tuple(dg.shape) == (2, 4) and not dg.any()

@@ -167,6 +167,41 @@ def test_zero_B_equals_weight_mul(torch):
     assert torch.equal(y, y0)
 
 
+def test_empty_token_batch(torch):
+    """No tokens (the reference's (in, 0) activations): empty outputs, zero
+    adapter gradients, accumulators left as they are, and the same for the
+    block neighbours and the dropout path."""
+    from reels_b200 import (check_device_status, gated_residual, gated_residual_backward, layernorm_modulate,
+                            layernorm_modulate_backward, lora_backward, lora_forward, saved_buffer,
+                            weight_transpose_mul)
+    c = lc.make_case(16, 256, 384, 8, dtype="bf16", layout=0, seed=9)
+    layer = lc.device_layer(torch, c)
+    x = torch.empty((0, 256), dtype=torch.bfloat16, device="cuda")
+    dy = torch.empty((0, 384), dtype=torch.bfloat16, device="cuda")
+    saved = saved_buffer(layer, x)
+    y = lora_forward(layer, x, saved=saved)
+    assert tuple(y.shape) == (0, 384)
+    g = lora_backward(layer, x, dy, saved=saved)
+    assert tuple(g.dx.shape) == (0, 256)
+    assert not g.A.any() and not g.B.any()
+    accA = torch.full((256, 8), 0.5, device="cuda").t()
+    accB = torch.full((8, 384), -1.0, device="cuda").t()
+    lora_backward(layer, x, dy, dA_acc=accA, dB_acc=accB, need_dx=False)
+    assert bool((accA == 0.5).all()) and bool((accB == -1.0).all())
+    assert tuple(weight_transpose_mul(layer.weight, dy).shape) == (0, 256)
+    layer.dropout = 0.25
+    assert tuple(lora_forward(layer, x, training=True, dropout_seed=3).shape) == (0, 384)
+    scale = torch.zeros((1, 256), dtype=torch.bfloat16, device="cuda")
+    assert tuple(layernorm_modulate(x, scale, scale).shape) == (0, 256)
+    dxn, ds, dh = layernorm_modulate_backward(x, x, scale, param_grads=True)
+    assert tuple(dxn.shape) == (0, 256) and not ds.any() and not dh.any()
+    gate = torch.ones((1, 256), dtype=torch.bfloat16, device="cuda")
+    assert tuple(gated_residual(x, x, gate).shape) == (0, 256)
+    dyr, dg = gated_residual_backward(x, x, gate)
+    assert tuple(dyr.shape) == (0, 256) and not dg.any()
+    check_device_status()
+
+
 def test_accumulate_into_fp32_buffers(torch):
     from reels_b200 import lora_backward
     c = lc.make_case(512, 256, 384, 16, dtype="bf16", layout=1, seed=6)
