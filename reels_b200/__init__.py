@@ -7,6 +7,7 @@ package is the Python-side mirror of the reference's layer API
 """
 from .lowvram import (  # noqa: F401
     DenseLayer,
+    FrozenLinearFunction,
     LayerNormModulateFunction,
     GeluFeedForwardFunction,
     LoRALinear,

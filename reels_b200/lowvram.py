@@ -17,6 +17,7 @@ frozen_weight_transfer          :func:`frozen_weight_transfer` (quantization.jl:
 lora_forward                    :func:`lora_forward` (lora.jl:56-95)
 lora_backward                   :func:`lora_backward` (lora.jl:106-118)
 merged_weight                   :func:`merged_weight` (lora.jl:120-122)
+rrule(linear)                   :class:`FrozenLinearFunction` (training/ad_rules.jl:55-68)
 rrule(_weight_mul) / Zygote     :class:`LoRALinearFunction` (training/ad_rules.jl:70-80)
 _projection + gelu_tanh         :func:`lora_forward_gelu` (models/wan21/transformer.jl:289-291,
                                 layers/linear.jl:61-68)
@@ -569,6 +570,21 @@ def check_device_status(device=None) -> None:
     """Synchronise and raise if a kernel's bounded pipeline wait gave up."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     nat.check("device status", nat.lib().reels_lowvram_check_device_status(_stream(dev)))
+
+
+class FrozenLinearFunction(torch.autograd.Function):
+    """Autograd rule of ``linear`` over a frozen DenseLayer (ad_rules.jl:55-68):
+    the pullback transmits the activation gradient, dequant(W)' * dy, and
+    produces no tangents for the frozen weight or bias."""
+
+    @staticmethod
+    def forward(ctx, x, layer):
+        ctx.layer = layer
+        return linear(layer, x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        return weight_transpose_mul(ctx.layer.weight, dy.contiguous()), None
 
 
 class LoRALinearFunction(torch.autograd.Function):

@@ -228,6 +228,21 @@ def test_weight_transpose_mul_is_the_frozen_pullback(torch):
     assert lc.rel_l2(dx, c.dY.astype(np.float64) @ Wd.astype(np.float64)) <= lc.TOL
 
 
+def test_frozen_linear_autograd_is_the_transpose_mul(torch):
+    """rrule(linear) (ad_rules.jl:55-68): the frozen dense layer's pullback
+    is exactly dequant(W)' * dy, with no tangent for the weight or bias."""
+    from reels_b200 import DenseLayer, FrozenLinearFunction, linear, weight_transpose_mul
+    c = lc.make_case(300, 512, 640, 8, dtype="bf16", layout=1, seed=12, bias=True)
+    layer = lc.device_layer(torch, c)
+    dense = DenseLayer(layer.weight, layer.bias)
+    x = torch.from_numpy(c.X).cuda().to(torch.bfloat16).requires_grad_(True)
+    dy = torch.from_numpy(c.dY).cuda().to(torch.bfloat16)
+    y = FrozenLinearFunction.apply(x, dense)
+    assert torch.equal(y, linear(dense, x.detach()))
+    y.backward(dy)
+    assert torch.equal(x.grad, weight_transpose_mul(dense.weight, dy))
+
+
 def test_autograd_function_matches_explicit_backward(torch):
     from reels_b200 import LoRALinearFunction, lora_backward
     c = lc.make_case(256, 512, 512, 16, dtype="bf16", layout=0, seed=10)
