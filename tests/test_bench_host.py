@@ -93,3 +93,36 @@ def test_step_flops_match_the_algorithmic_count():
     assert f == pytest.approx(71.75e9, rel=1e-3)
     layers = bench.block_layers(32760)
     assert len(layers) == 10 and sum(1 for l in layers if l[1] == 512) == 2
+
+
+def _run_bench(args, env_extra=None):
+    import json
+    import subprocess
+    env = dict(os.environ)
+    env.update(env_extra or {})
+    res = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *args], capture_output=True, text=True,
+                         env=env, timeout=600)
+    lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+    return res.returncode, [json.loads(l) for l in lines], res.stderr
+
+
+def test_reference_arm_contract():
+    """--impl reference times the CPU restatement and prints one JSON line
+    with the reference fields the driver reads; it needs no GPU."""
+    rc, lines, err = _run_bench(["--impl", "reference", "--config", "cfg1", "--steps", "1", "--warmup", "3"])
+    assert rc == 0, err[-2000:]
+    assert len(lines) == 1
+    d = lines[0]
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["steps"] == 1 and d["warmup"] >= 3
+    cb = d["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    assert d["config"]["workload"] == "wan21-1.3b-ffn-up"
+
+
+def test_reference_arm_other_ranks_print_nothing():
+    rc, lines, err = _run_bench(["--impl", "reference", "--config", "cfg1", "--steps", "1", "--warmup", "3"],
+                                {"RANK": "1", "WORLD_SIZE": "2"})
+    assert rc == 0, err[-2000:]
+    assert lines == []
