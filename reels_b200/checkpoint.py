@@ -75,17 +75,25 @@ def inspect_safetensors(path: str) -> SafeTensorHeader:
         if 8 + header_len > size:
             raise ValueError("SafeTensors header exceeds file size")
         raw = json.loads(f.read(header_len).decode("utf-8"))
+    if not isinstance(raw, dict):
+        raise ValueError("SafeTensors header is not a JSON object")
     metadata: Dict[str, str] = {}
     tensors: Dict[str, TensorInfo] = {}
     for name, value in raw.items():
-        if name == "__metadata__":
-            metadata = {str(k): str(v) for k, v in value.items()}
-            continue
-        offsets = [int(v) for v in value["data_offsets"]]
+        try:
+            if name == "__metadata__":
+                metadata = {str(k): str(v) for k, v in value.items()}
+                continue
+            offsets = [int(v) for v in value["data_offsets"]]
+            shape = tuple(int(v) for v in value["shape"])
+            dtype = str(value["dtype"])
+        except (AttributeError, KeyError, TypeError, ValueError):
+            raise ValueError(f"malformed SafeTensors header entry {name!r}") from None
         if len(offsets) != 2 or not 0 <= offsets[0] <= offsets[1]:
             raise ValueError(f"invalid offsets for tensor {name}")
-        tensors[name] = TensorInfo(str(value["dtype"]), tuple(int(v) for v in value["shape"]),
-                                   (offsets[0], offsets[1]))
+        if any(d < 0 for d in shape):
+            raise ValueError(f"negative dimension for tensor {name}")
+        tensors[name] = TensorInfo(dtype, shape, (offsets[0], offsets[1]))
     previous = 0
     for lo, hi, name in sorted((t.data_offsets[0], t.data_offsets[1], n) for n, t in tensors.items()):
         if lo < previous:

@@ -190,3 +190,57 @@ def test_unquantized_tensors_take_the_compute_type():
     assert out["norm.weight"].dtype == torch.float16
     assert out["lin.weight.scale"].dtype == torch.float32
     assert out["lin.weight"].dtype == torch.int8 and out["pos"].dtype == torch.int64
+
+
+def _raw_file(path, header_bytes, payload=b""):
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(header_bytes)))
+        f.write(header_bytes)
+        f.write(payload)
+    return str(path)
+
+
+@pytest.mark.parametrize("header", [
+    b"[1, 2, 3]",                                                   # not an object
+    b'{"a": {"dtype": "F32", "shape": [2]}}',                       # no offsets
+    b'{"a": {"dtype": "F32", "shape": 3, "data_offsets": [0, 4]}}',  # shape not a list
+    b'{"a": {"dtype": "F32", "shape": [-1], "data_offsets": [0, 4]}}',
+    b'{"a": {"dtype": "F32", "shape": [1], "data_offsets": [4, 0]}}',
+    b'{"a": {"dtype": "F32", "shape": [1], "data_offsets": "x"}}',
+    b'{"__metadata__": [1]}',
+    b'{"a": 5}',
+    b"\xff\xfe not utf-8",
+    b"{not json",
+])
+def test_malformed_headers_raise_value_errors(tmp_path, header):
+    """Every malformed header is a ValueError, as inspect_safetensors
+    (safetensors.jl:15-49) throws ArgumentError: never another exception
+    type from deep inside the parser."""
+    p = _raw_file(tmp_path / "bad.safetensors", header, b"\0" * 8)
+    with pytest.raises(ValueError):
+        ck.inspect_safetensors(p)
+
+
+def test_random_bytes_never_crash_the_parser(tmp_path):
+    import random
+    rng = random.Random(7)
+    good = tmp_path / "good.safetensors"
+    ck.write_safetensors(str(good), {"w": torch.arange(6, dtype=torch.float32).reshape(2, 3)}, {"k": "v"})
+    blob = bytearray(good.read_bytes())
+    for trial in range(300):
+        b = bytearray(blob)
+        for _ in range(rng.randint(1, 6)):
+            b[rng.randrange(len(b))] = rng.randrange(256)
+        if rng.random() < 0.3:
+            b = b[:rng.randrange(len(b))]
+        p = tmp_path / f"m{trial}.safetensors"
+        p.write_bytes(bytes(b))
+        try:
+            h = ck.inspect_safetensors(str(p))
+            for name in h.tensors:
+                try:
+                    ck.load_safetensor(str(p), name, h)
+                except (KeyError, ValueError):
+                    pass
+        except ValueError:
+            pass
