@@ -4,8 +4,6 @@ have the prototype's length, with Julia types that agree with the C ones."""
 import os
 import re
 
-import pytest
-
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
