@@ -64,8 +64,9 @@ def test_sampler_process_round_trip(tmp_path):
     fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
     s = bench.ClockSampler(0, command=str(fake))
     s.start()
+    time.sleep(1.0)  # the stand-in is an interpreter: let it come up even on a loaded host
     s.begin()
-    time.sleep(0.3)
+    time.sleep(0.5)
     s.end()
     out = s.stop()
     assert out is not None and out["window"] == "timed region" and out["samples"] >= 3
