@@ -10,7 +10,11 @@
  *     message in reels_lowvram_last_error() (thread-local, like
  *     deps/sentencepiece_bridge.cpp:10-17 of the reference);
  *   - allocates no device memory: scratch space is caller-provided
- *     (`workspace`, sized by reels_q8lora_workspace_bytes).
+ *     (`workspace`, sized by reels_q8lora_workspace_bytes);
+ *   - may be called from several host threads and on several streams at
+ *     once.  The per-thread state is the error message, the last path and
+ *     the profiling counters; calls that share a workspace or a `saved`
+ *     buffer must be ordered on one stream.
  *
  * Array layouts are those of the reference's column-major, feature-first
  * Julia arrays, written as row-major C arrays:
