@@ -14,7 +14,11 @@
  *   - may be called from several host threads and on several streams at
  *     once.  The per-thread state is the error message, the last path and
  *     the profiling counters; calls that share a workspace or a `saved`
- *     buffer must be ordered on one stream.
+ *     buffer must be ordered on one stream;
+ *   - runs on the device that owns its buffers and leaves the calling
+ *     thread's current device (CUDA context) as it found it: a call with
+ *     device-1 buffers while device 0 is current returns with device 0
+ *     current, and a thread with no current context is left with none.
  *
  * Array layouts are those of the reference's column-major, feature-first
  * Julia arrays, written as row-major C arrays:
@@ -129,8 +133,11 @@ int reels_lowvram_profile_read(double *q8_ms, int64_t *q8_launches, double *q8_f
  * q = round_to_even(clamp(w / scale, -127, 127)).
  * `w` (w_dtype REELS_F32/F16/BF16, widened to fp32 exactly like
  * `Float32.(Array(weight))`) and `q` share `layout`.
- * Synchronises `stream` to report non-finite weights (the reference throws
- * InexactError there): returns REELS_EINVAL in that case. */
+ * Synchronises `stream` to report the inputs the reference rejects with
+ * InexactError, returning REELS_EINVAL: non-finite weights, and a row whose
+ * max|w| / 127 underflows to 0 (max|w| <= 63 * 2^-149) while it holds a zero
+ * element (0 / 0 = NaN, which Int8 cannot represent).  Such a row without
+ * zeros quantises to +-127 with scale 0, as in the reference. */
 int reels_q8_quantize(const void *w, int w_dtype, int layout, int64_t N, int64_t K, int8_t *q, float *scales,
                       void *stream);
 

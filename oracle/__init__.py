@@ -92,7 +92,8 @@ def quantize(w: np.ndarray, layout: int = LAYOUT_OUT_CONTIGUOUS):
     """Bit-exact restatement of quantization.jl:35-44.  ``w`` is given in
     ``layout`` ([K][N] for the Julia layout, [N][K] for the PyTorch layout).
     Returns (q int8 same shape as w, scales fp32 [N]).  Raises ValueError on
-    non-finite weights, as the reference does (InexactError)."""
+    non-finite weights and on a row whose scale underflows to 0 while it
+    holds a zero (0/0 = NaN), where the reference raises InexactError."""
     w = _c(w, np.float32)
     if layout == LAYOUT_OUT_CONTIGUOUS:
         K, N = w.shape
@@ -101,8 +102,10 @@ def quantize(w: np.ndarray, layout: int = LAYOUT_OUT_CONTIGUOUS):
     q = np.empty(w.shape, np.int8)
     s = np.empty((N,), np.float32)
     rc = lib().oracle_quantize(w, layout, N, K, q, s)
-    if rc != 0:
+    if rc == -1:
         raise ValueError("frozen weight contains non-finite values")
+    if rc == -2:
+        raise ValueError("a row's max|w| / 127 underflows to 0 while the row holds a zero: 0/0 is NaN")
     return q, s
 
 

@@ -36,11 +36,18 @@
  *   scales[maxima .== 0f0] .= 1f0
  *   values = Int8.(round.(clamp.(host ./ scales, -127f0, 127f0)))
  * Julia's `round` is RoundNearest (ties to even); `rintf` under the default
- * FE_TONEAREST mode is the same rule.  Returns -1 if any weight is not finite:
- * the reference raises InexactError converting NaN to Int8 there. */
+ * FE_TONEAREST mode is the same rule.  Julia's clamp is
+ * ifelse(x > hi, hi, ifelse(x < lo, lo, x)), so a NaN quotient passes through
+ * and Int8(NaN) raises InexactError.  Two inputs reach that:
+ *   - a non-finite weight (max or quotient NaN): returns -1;
+ *   - a row whose maximum m is nonzero but m/127 rounds to 0 (m <= 63*2^-149;
+ *     only m == 0 is replaced by 1) and which holds a zero element: 0/0 = NaN.
+ *     Returns -2.  The row's nonzero elements divide to +-Inf and clamp to
+ *     +-127, so a row without zeros quantises with scale 0.
+ * NaN is never cast to an integer (that is undefined behaviour in C). */
 int oracle_quantize(const float *w, int layout, int64_t N, int64_t K, int8_t *q, float *scales)
 {
-    int bad = 0;
+    int bad = 0, nan_quotient = 0;
     for (int64_t n = 0; n < N; ++n) {
         float m = 0.0f;
         for (int64_t k = 0; k < K; ++k) {
@@ -58,10 +65,15 @@ int oracle_quantize(const float *w, int layout, int64_t N, int64_t K, int8_t *q,
             float c = t;
             if (c > 127.0f) c = 127.0f;
             if (c < -127.0f) c = -127.0f;
+            if (isnan(c)) {
+                if (isfinite(w[i])) nan_quotient = 1;
+                q[i] = 0;
+                continue;
+            }
             q[i] = (int8_t)(int)rintf(c);
         }
     }
-    return bad ? -1 : 0;
+    return bad ? -1 : (nan_quotient ? -2 : 0);
 }
 
 /* quantization.jl:63-64 `_dequantize_for_compute(values, scales, Float32)`:

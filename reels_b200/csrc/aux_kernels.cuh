@@ -21,6 +21,12 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 // src/layers/quantization.jl:35-44, per output row n:
 //   m = max_k |w[n,k]| (fp32),  s = m / 127 (IEEE),  s = 1 if m == 0,
 //   q = Int8(round(clamp(w / s, -127, 127)))   with round = ties-to-even.
+// Only m == 0 is replaced, so a row whose m is at most 63 * 2^-149 gets s = 0
+// (m / 127 underflows).  Its nonzero elements divide to +-Inf and clamp to
+// +-127; a zero element gives 0 / 0 = NaN, which Julia's clamp passes through
+// and Int8(NaN) rejects with InexactError.  The kernels flag that NaN
+// (DEVERR_QUANT_NAN) instead of clamping it: fminf/fmaxf would turn it into
+// a number.
 // Layout 0 (Julia (out, in) column-major): w[k*N + n].  One block handles
 // 32 consecutive rows n (one per lane, coalesced along n); its 8 warps split
 // the k range and combine maxima in shared memory.
@@ -54,11 +60,14 @@ __global__ void __launch_bounds__(256) quantize_outcontig_kernel(const T *__rest
     __syncthreads();
     if (n < N) {
         const float s = sscale[lane];
+        bool nan = false;
         for (int64_t k = wp; k < K; k += 8) {
             float t = __fdiv_rn(to_f32(w[k * N + n]), s);
+            nan |= isnan(t);
             t = fminf(fmaxf(t, -127.0f), 127.0f);
             q[k * N + n] = (int8_t)__float2int_rn(t);
         }
+        if (nan) atomicOr(err, DEVERR_QUANT_NAN);
     }
 }
 
@@ -83,11 +92,14 @@ __global__ void __launch_bounds__(256) quantize_incontig_kernel(const T *__restr
     const float s = (m == 0.0f) ? 1.0f : __fdiv_rn(m, 127.0f);
     if (lane == 0) scales[n] = s;
     int8_t *qr = q + n * K;
+    bool nan = false;
     for (int64_t k = lane; k < K; k += 32) {
         float t = __fdiv_rn(to_f32(row[k]), s);
+        nan |= isnan(t);
         t = fminf(fmaxf(t, -127.0f), 127.0f);
         qr[k] = (int8_t)__float2int_rn(t);
     }
+    if (__any_sync(0xffffffffu, nan) && lane == 0) atomicOr(err, DEVERR_QUANT_NAN);
 }
 
 // ------------------------------------------------------- materialise

@@ -26,6 +26,8 @@ enum DevErr : unsigned {
     DEVERR_TIMEOUT_ACC = 16u,
     DEVERR_NONFINITE_WEIGHT = 256u,
     DEVERR_OPT_TABLE = 512u,  // an optimizer workspace that was not prepared
+    // a row whose max|w| / 127 underflows to 0 holds a zero: 0 / 0 is NaN
+    DEVERR_QUANT_NAN = 1024u,
 };
 
 // ---------------------------------------------------------------- elements

@@ -98,6 +98,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 constexpr int kMaxDevices = 64;
 struct DeviceState {
     bool ready = false;
+    int index = -1;
     int sms = 148;
     int pair_clusters = 0;  // co-resident 2-CTA clusters of the pair kernel
     unsigned *status = nullptr;
@@ -147,7 +148,44 @@ cudaError_t set_ts_attrs() {
     return set_ts_attr<DT, 128, 2>();
 }
 
-int bind_device(const void *ptr, DeviceState **out) {
+// The calling thread's current context is restored when an entry point
+// returns: a caller that passes device-1 buffers while device 0 is current
+// gets device 0 back.  Contexts (not device indices) are compared and
+// restored, so a thread that had no current context is left with none and
+// no primary context is created on a device the caller never used.
+using CtxGetFn = CUresult (*)(CUcontext *);
+using CtxSetFn = CUresult (*)(CUcontext);
+CtxGetFn g_ctx_get = nullptr;
+CtxSetFn g_ctx_set = nullptr;
+std::once_flag g_ctx_once;
+
+struct DeviceScope {
+    CUcontext prev = nullptr;
+    bool restore = false;
+    DeviceScope() = default;
+    DeviceScope(const DeviceScope &) = delete;
+    DeviceScope &operator=(const DeviceScope &) = delete;
+    ~DeviceScope() {
+        if (restore && g_ctx_set) g_ctx_set(prev);
+    }
+};
+
+void resolve_ctx_calls() {
+    std::call_once(g_ctx_once, [] {
+        void *fg = nullptr, *fs = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fg, cudaEnableDefault, &q1) == cudaSuccess &&
+            cudaGetDriverEntryPoint("cuCtxSetCurrent", &fs, cudaEnableDefault, &q2) == cudaSuccess &&
+            q1 == cudaDriverEntryPointSuccess && q2 == cudaDriverEntryPointSuccess && fg && fs) {
+            g_ctx_get = reinterpret_cast<CtxGetFn>(fg);
+            g_ctx_set = reinterpret_cast<CtxSetFn>(fs);
+        } else {
+            cudaGetLastError();
+        }
+    });
+}
+
+int bind_device(const void *ptr, DeviceState **out, DeviceScope &scope) {
     int dev = -1;
     cudaPointerAttributes attr;
     if (ptr && cudaPointerGetAttributes(&attr, ptr) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {
@@ -159,11 +197,20 @@ int bind_device(const void *ptr, DeviceState **out) {
     if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
     // Always bind: on a thread that has not used this device yet (e.g. an
     // autograd worker) this also makes the primary context current, which
-    // the driver-API tensor-map encoder needs.
+    // the driver-API tensor-map encoder needs.  `scope` puts the caller's
+    // context back when the entry point returns.
+    resolve_ctx_calls();
+    CUcontext before = nullptr, after = nullptr;
+    if (g_ctx_get && g_ctx_get(&before) != CUDA_SUCCESS) before = nullptr;
     REELS_CUDA(cudaSetDevice(dev));
+    if (g_ctx_get && g_ctx_get(&after) == CUDA_SUCCESS && after != before && !scope.restore) {
+        scope.prev = before;
+        scope.restore = true;
+    }
     std::lock_guard<std::mutex> lock(g_dev_mu);
     DeviceState &st = g_dev[dev];
     if (!st.ready) {
+        st.index = dev;
         int major = 0, minor = 0;
         REELS_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
         REELS_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
@@ -1083,7 +1130,9 @@ int reels_lowvram_profile_read(double *q8_ms, int64_t *q8_launches, double *q8_f
 
 int reels_lowvram_check_device_status(void *stream) {
     DeviceState *ds;
-    int rc = bind_device(nullptr, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(nullptr, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     unsigned h = 0, zero = 0;
@@ -1108,7 +1157,9 @@ int reels_q8_quantize(const void *w, int w_dtype, int layout, int64_t N, int64_t
     if (layout != REELS_W_OUT_CONTIGUOUS && layout != REELS_W_IN_CONTIGUOUS) return fail("unknown weight layout");
     if (w_dtype != REELS_F32 && w_dtype != REELS_F16 && w_dtype != REELS_BF16) return fail("unknown weight dtype");
     DeviceState *ds;
-    int rc = bind_device(w, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(w, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     REELS_CUDA(cudaMemsetAsync(ds->quant_status, 0, 4, st));
@@ -1140,6 +1191,9 @@ int reels_q8_quantize(const void *w, int w_dtype, int layout, int64_t N, int64_t
     REELS_CUDA(cudaMemcpyAsync(&h, ds->quant_status, 4, cudaMemcpyDeviceToHost, st));
     REELS_CUDA(cudaStreamSynchronize(st));
     if (h & DEVERR_NONFINITE_WEIGHT) return fail("frozen weight contains non-finite values (NaN or Inf)");
+    if (h & DEVERR_QUANT_NAN)
+        return fail("a row's max|w| / 127 underflows to 0 while the row holds a zero: 0/0 is NaN, which Int8 "
+                    "rejects (InexactError in quantize_frozen_matrix)");
     return ok(REELS_PATH_CUDACORE);
 }
 
@@ -1150,7 +1204,9 @@ int reels_q8_materialize(const int8_t *q, const float *scales, int layout, int64
     if (layout != REELS_W_OUT_CONTIGUOUS && layout != REELS_W_IN_CONTIGUOUS) return fail("unknown weight layout");
     if (out_dtype != REELS_F32 && out_dtype != REELS_F16 && out_dtype != REELS_BF16) return fail("unknown dtype");
     DeviceState *ds;
-    int rc = bind_device(q, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(q, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     materialize_kernel<<<launch_grid(N * K), 256, 0, st>>>(q, scales, layout, N, K, out_dtype, out);
@@ -1198,7 +1254,9 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
     if (rc) return rc;
     if (M == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
-    rc = bind_device(x, &ds);
+    DeviceScope scope;
+
+    rc = bind_device(x, &ds, scope);
     if (rc) return rc;
     const bool drop = dropout > 0.0f && r > 0;
     const Ws wl = ws_layout(M, K, N, r, dt, REELS_PASS_FORWARD | (drop ? REELS_PASS_DROPOUT : 0), ds->sms);
@@ -1314,7 +1372,9 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
     if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
     if (!dx && r == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
-    rc = bind_device(M > 0 ? dy : static_cast<const void *>(q), &ds);
+    DeviceScope scope;
+
+    rc = bind_device(M > 0 ? dy : static_cast<const void *>(q), &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (M == 0) {
@@ -1511,7 +1571,9 @@ int reels_dropout_mask(int64_t n, float dropout, uint64_t seed, uint64_t stream_
     if (n == 0) return ok(REELS_PATH_NONE);
     if (!keep) return fail("null mask");
     DeviceState *ds;
-    int rc = bind_device(keep, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(keep, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     dropout_mask_kernel<<<launch_grid(n), 256, 0, st>>>(n, dropout, dropout_key(seed, stream_id), keep);
@@ -1553,7 +1615,9 @@ int reels_layernorm_modulate(const void *x, int64_t M, int64_t K, int64_t tokens
     if (!out && M > 0) return fail("null out");
     if (M == 0) return ok(REELS_PATH_NONE);
     DeviceState *ds;
-    rc = bind_device(x, &ds);
+    DeviceScope scope;
+
+    rc = bind_device(x, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const dim3 grid((unsigned)std::min<int64_t>(M, 16LL * ds->sms));
@@ -1589,7 +1653,9 @@ int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M
             return fail("workspace too small");
     }
     DeviceState *ds;
-    rc = bind_device(x, &ds);
+    DeviceScope scope;
+
+    rc = bind_device(x, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (M == 0) {
@@ -1651,7 +1717,9 @@ int reels_gated_residual(const void *x, const void *y, const void *gate, int64_t
     if (M == 0) return ok(REELS_PATH_NONE);
     if (!x || !y || !gate || !out) return fail("null x, y, gate or out");
     DeviceState *ds;
-    rc = bind_device(x, &ds);
+    DeviceScope scope;
+
+    rc = bind_device(x, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     dispatch_dt(dt, [&](auto d) {
@@ -1681,7 +1749,9 @@ int reels_gated_residual_backward(const void *dout, const void *y, const void *g
     }
     if (!dy && !dgate) return ok(REELS_PATH_NONE);
     DeviceState *ds;
-    rc = bind_device(dout, &ds);
+    DeviceScope scope;
+
+    rc = bind_device(dout, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int64_t batch = cdiv(M, tokens_per_sample);
@@ -1749,7 +1819,9 @@ int reels_opt_prepare(const reels_opt_tensor *tensors, int count, void *workspac
     h->count = count;
     h->total_chunks = chunks;
     DeviceState *ds;
-    int rc = bind_device(workspace, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(workspace, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     char *dws = reinterpret_cast<char *>(workspace);
@@ -1768,7 +1840,9 @@ int reels_grad_norm_sq(void *workspace, float grad_scale, float *sumsq, void *st
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail("optimizer workspace must be 256-byte aligned");
     if (!std::isfinite(grad_scale)) return fail("grad_scale must be finite");
     DeviceState *ds;
-    int rc = bind_device(workspace, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(workspace, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const char *ws = reinterpret_cast<const char *>(workspace);
@@ -1791,7 +1865,9 @@ int reels_adamw_update(void *workspace, float lr, float beta1, float beta2, floa
     if (!(correction1 > 0.0f) || !(correction2 > 0.0f)) return fail("bias corrections must be positive");
     if (sumsq && !(max_norm > 0.0f)) return fail("max_norm must be positive when clipping");
     DeviceState *ds;
-    int rc = bind_device(workspace, &ds);
+    DeviceScope scope;
+
+    int rc = bind_device(workspace, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     AdamArgs a;
@@ -1833,7 +1909,6 @@ static __device__ __align__(256) unsigned char g_static_ws[REELS_STATIC_WS_BYTES
 
 namespace {
 void *g_static_ws_addr[kMaxDevices];
-int g_static_ws_sms[kMaxDevices];
 std::mutex g_static_ws_mu;
 }  // namespace
 
@@ -1845,18 +1920,14 @@ extern "C" int reels_q8lora_forward_static_ws(const void *x, const int8_t *q, co
     if (rc) return rc;
     if (M == 0) return ok(REELS_PATH_NONE);
     if (!x) return fail("null x");
-    int dev = -1;
-    cudaPointerAttributes attr;
-    if (cudaPointerGetAttributes(&attr, x) == cudaSuccess && attr.type == cudaMemoryTypeDevice) {
-        dev = attr.device;
-    } else {
-        cudaGetLastError();
-        REELS_CUDA(cudaGetDevice(&dev));
-    }
-    if (dev < 0 || dev >= kMaxDevices) return fail("device index out of range");
-    REELS_CUDA(cudaSetDevice(dev));
+    // Binds x's device (refusing a GPU the library was not built for) before
+    // the array's address is looked up with that device current.
+    DeviceScope scope;
+    DeviceState *ds;
+    rc = bind_device(x, &ds, scope);
+    if (rc) return rc;
+    const int dev = ds->index;
     void *ws = nullptr;
-    int sms = 0;
     {
         std::lock_guard<std::mutex> lock(g_static_ws_mu);
         if (!g_static_ws_addr[dev]) {
@@ -1864,15 +1935,11 @@ extern "C" int reels_q8lora_forward_static_ws(const void *x, const int8_t *q, co
             cudaError_t e = cudaGetSymbolAddress(&p, g_static_ws);
             if (e != cudaSuccess || !p)
                 return fail_dev(std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
-            int v = 0;
-            REELS_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
-            g_static_ws_sms[dev] = v;
             g_static_ws_addr[dev] = p;
         }
         ws = g_static_ws_addr[dev];
-        sms = g_static_ws_sms[dev];
     }
-    const size_t need = ws_layout(M, K, N, r, act_dtype, REELS_PASS_FORWARD, sms).total;
+    const size_t need = ws_layout(M, K, N, r, act_dtype, REELS_PASS_FORWARD, ds->sms).total;
     if (need > REELS_STATIC_WS_BYTES) {
         char buf[200];
         snprintf(buf, sizeof buf,

@@ -159,8 +159,10 @@ def quantize_frozen_matrix(weight: torch.Tensor, dtype: Optional[torch.dtype] = 
 
     ``weight`` has logical shape (out, in); its memory layout (column-major as
     in the reference, or row-major) is kept for the int8 values unless
-    ``layout`` asks for the other one.  Raises ValueError on non-finite
-    weights, as the reference raises InexactError."""
+    ``layout`` asks for the other one.  Raises ValueError where the
+    reference raises InexactError: on non-finite weights, and on a row whose
+    max|w| / 127 underflows to a zero scale while it holds a zero element
+    (0 / 0 is NaN)."""
     _require_cuda(weight)
     if weight.dim() != 2:
         raise ValueError("frozen weight must be a matrix")

@@ -1,0 +1,191 @@
+"""GPU, two ranks over NCCL: the data-parallel step of the LoRA linears.
+
+The reference's own two-GPU check (test/gpu/distributed_check.jl:10-17,27-74)
+asserts that the adapters agree across ranks and that the two-rank result
+equals a single-process run on the effective batch.  Here each rank runs
+lora_forward / lora_backward on its own token shard of three layers, and the
+per-layer gradients go through OverlappedGradReducer (an fp32 NCCL sum on a
+side stream, launched while the next layer's backward runs, then 1/world).
+Checks, on every rank:
+  - the reduced dA/dB equal (g_shard0 + g_shard1) / 2 computed on one GPU, bit
+    for bit (the kernels are deterministic and a two-term fp32 sum commutes);
+  - they match one backward over both shards' tokens with grad_scale 1/2
+    (relative L2 <= 2e-5, the reference check's rtol: only the fp32
+    summation order differs);
+  - both ranks hold identical gradient bytes, and identical adapter bytes
+    after an AdamW step on the reduced gradients.
+Skipped on a box with fewer than two GPUs.
+"""
+import os
+import socket
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+SHAPES = [(1536, 1536), (8960, 1536), (1536, 8960)]   # (out, in): attention, FFN up, FFN down
+TOKENS = 1024                                          # per rank
+RANK = 32
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layers(torch, dev):
+    import numpy as np
+    from reels_b200 import LoRALinear, quantize_frozen_matrix
+    g = np.random.default_rng(11)
+    out = []
+    for N, K in SHAPES:
+        W = torch.from_numpy((0.02 * g.standard_normal((N, K))).astype(np.float32)).to(dev)
+        qm = quantize_frozen_matrix(W.t().contiguous().t(), torch.bfloat16)
+        A = torch.from_numpy((g.standard_normal((RANK, K)) / np.sqrt(K)).astype(np.float32)).to(dev)
+        B = torch.from_numpy((0.01 * g.standard_normal((N, RANK))).astype(np.float32)).to(dev)
+        out.append(LoRALinear(qm, None, A.to(torch.bfloat16), B.to(torch.bfloat16), float(RANK)))
+    return out
+
+
+def _inputs(torch, dev, world):
+    import numpy as np
+    g = np.random.default_rng(23)
+    xs, dys = [], []
+    for N, K in SHAPES:
+        xs.append(torch.from_numpy(g.standard_normal((world * TOKENS, K)).astype(np.float32)).to(dev)
+                  .to(torch.bfloat16))
+        dys.append(torch.from_numpy(g.standard_normal((world * TOKENS, N)).astype(np.float32)).to(dev)
+                   .to(torch.bfloat16))
+    return xs, dys
+
+
+def _grads(torch, layers, xs, dys, lo, hi, grad_scale=1.0):
+    """fp32 [dA | dB] of every layer over tokens lo:hi (forward, then the
+    backward in reverse layer order)."""
+    from reels_b200 import lora_backward, lora_forward, saved_buffer
+    saved = []
+    for layer, x in zip(layers, xs):
+        sv = saved_buffer(layer, x[lo:hi])
+        lora_forward(layer, x[lo:hi], saved=sv)
+        saved.append(sv)
+    flats = [None] * len(layers)
+    for i in reversed(range(len(layers))):
+        gr = lora_backward(layers[i], xs[i][lo:hi], dys[i][lo:hi], saved=saved[i], grad_scale=grad_scale,
+                           need_dx=True)
+        flats[i] = torch.cat([gr.A.reshape(-1), gr.B.reshape(-1)])
+    return flats
+
+
+def _worker(rank, world, port, q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(world), RANK=str(rank),
+                      LOCAL_RANK=str(rank))
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from reels_b200 import build, check_device_status, lora_backward, lora_forward, saved_buffer
+    from reels_b200 import distributed as rd
+    from reels_b200.optim import AdamW, AdamWState, update_
+    rt = None
+    try:
+        build.build()
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        rt = rd.init_distributed(backend="nccl", timeout_seconds=120)
+        layers = _layers(torch, dev)
+        xs, dys = _inputs(torch, dev, world)
+        lo, hi = rank * TOKENS, (rank + 1) * TOKENS
+
+        # the data-parallel step: own shard, per-layer reduction overlapped
+        # with the backward of the layers before it
+        saved = []
+        for layer, x in zip(layers, xs):
+            sv = saved_buffer(layer, x[lo:hi])
+            lora_forward(layer, x[lo:hi], saved=sv)
+            saved.append(sv)
+        red = rd.OverlappedGradReducer(rt, dev)
+        flats = [None] * len(layers)
+        for i in reversed(range(len(layers))):
+            gr = lora_backward(layers[i], xs[i][lo:hi], dys[i][lo:hi], saved=saved[i], need_dx=True)
+            flats[i] = torch.cat([gr.A.reshape(-1), gr.B.reshape(-1)])
+            red.layer_done(flats[i])
+        red.finish()
+        torch.cuda.synchronize(dev)
+
+        # single-GPU references on this rank's device
+        per_shard = [_grads(torch, layers, xs, dys, s * TOKENS, (s + 1) * TOKENS) for s in range(world)]
+        eff = _grads(torch, layers, xs, dys, 0, world * TOKENS, grad_scale=float(np.float32(1.0 / world)))
+        torch.cuda.synchronize(dev)
+        out = {"bit_equal_mean": [], "rel_eff": [], "ranks_equal": [], "params_equal": None}
+        inv = np.float32(1.0 / world).item()
+        for i in range(len(layers)):
+            mean = per_shard[0][i].clone()
+            for s in range(1, world):
+                mean += per_shard[s][i]
+            mean.mul_(inv)
+            out["bit_equal_mean"].append(bool(torch.equal(flats[i], mean)))
+            d = (flats[i].double() - eff[i].double()).norm() / eff[i].double().norm()
+            out["rel_eff"].append(float(d))
+            gathered = [torch.empty_like(flats[i]) for _ in range(world)]
+            dist.all_gather(gathered, flats[i])
+            out["ranks_equal"].append(all(torch.equal(gathered[0], t) for t in gathered[1:]))
+
+        # one AdamW step on the reduced gradients: the adapters stay identical
+        params = []
+        for layer in layers:
+            params += [layer.A.contiguous(), layer.B.contiguous()]
+        grads = []
+        for i, layer in enumerate(layers):
+            nA = layer.A.numel()
+            grads += [flats[i][:nA].contiguous(), flats[i][nA:].contiguous()]
+        state = AdamWState(params)
+        update_(AdamW(learning_rate=1e-3), state, params, grads, max_gradient_norm=1.0)
+        flat_p = torch.cat([p.reshape(-1).float() for p in params])
+        gathered = [torch.empty_like(flat_p) for _ in range(world)]
+        dist.all_gather(gathered, flat_p)
+        out["params_equal"] = all(torch.equal(gathered[0], t) for t in gathered[1:])
+        check_device_status(dev)
+        rd.distributed_barrier(rt)
+        rd.close_distributed(rt)
+        q.put((rank, out))
+    except Exception as e:  # surfaced to the parent
+        import traceback
+        q.put((rank, "".join(traceback.format_exception(e))))
+        if rt is not None:
+            try:
+                rd.close_distributed(rt)
+            except Exception:
+                pass
+
+
+def test_two_rank_nccl_step_matches_single_gpu():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(2):
+            rank, out = q.get(timeout=600)
+            results[rank] = out
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank in range(2):
+        out = results[rank]
+        assert isinstance(out, dict), out
+        assert all(out["bit_equal_mean"]), out
+        assert max(out["rel_eff"]) <= 2e-5, out
+        assert all(out["ranks_equal"]), out
+        assert out["params_equal"], out

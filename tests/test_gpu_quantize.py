@@ -69,20 +69,27 @@ def test_bit_exact_vs_oracle(torch_cuda, layout, wdtype, shape):
 @pytest.mark.parametrize("layout", [0, 1])
 def test_extreme_rows_bit_exact(torch_cuda, layout):
     """Rows at the ends of fp32 (largest finite values, subnormal maxima and
-    scales, signed zeros, scale exactly 1 with .5 ties) and rows spanning
-    2^-140 .. 2^120: the GPU quantiser keeps gradual underflow as the
-    reference's fp32 division does."""
+    scales, a scale that underflows to 0 in a row without zeros, signed
+    zeros, scale exactly 1 with .5 ties) and rows spanning 2^-140 .. 2^120:
+    the GPU quantiser keeps gradual underflow as the reference's fp32
+    division does."""
     torch = torch_cuda
     from reels_b200 import quantize_frozen_matrix
     f = np.float32
     tiny = np.finfo(f).tiny
+    u = f(2.0 ** -149)
     rows = [[np.finfo(f).max, -np.finfo(f).max, 1.0, 0.0], [tiny, -tiny / 2, tiny / 8, 0.0],
-            [np.float32(1e-45), 0.0, -0.0, np.float32(-1e-45)], [0.0, 0.0, 3.0, 0.0], [-0.0, -0.0, -0.0, -0.0],
+            [u, -u, 2 * u, -3 * u], [0.0, 0.0, 3.0, 0.0], [-0.0, -0.0, -0.0, -0.0],
             [127.0, 63.5, -0.5, 0.5], [1e30, 1e-30, -1e30, 2.5e29]]
     g = np.random.default_rng(17)
     e = g.integers(-140, 120, size=(40, 1))
     rand = (g.standard_normal((40, 4)) * np.exp2(e)).astype(f)
     W = np.concatenate([np.array(rows, f), rand])
+    assert f(1.0) / f(1.0) == 1  # (numpy float32 arithmetic below is IEEE)
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        m = np.abs(W).max(axis=1)
+        sc = np.where(m == 0, f(1), (m / f(127)).astype(f))
+        W = W[~np.isnan(W / sc[:, None]).any(axis=1)]   # rows the reference rejects are tested below
     Wt = _to_dev(torch, W)
     if layout == 0:
         Wt = Wt.t().contiguous().t()
@@ -90,6 +97,31 @@ def test_extreme_rows_bit_exact(torch_cuda, layout):
     q_ref, s_ref = oracle.quantize(W, 1)
     assert np.array_equal(qm.scales.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
     assert np.array_equal(qm.values.cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_underflowed_scale_with_zero_raises(torch_cuda, layout):
+    """The rows src/layers/quantization.jl:35-44 rejects (tests/golden/
+    quant_kat.json "raises"): a NaN quotient reaches Int8 and throws
+    InexactError.  Each row alone and among good rows; the kernel then
+    recovers on a good matrix and matches the known answers."""
+    torch = torch_cuda
+    from reels_b200 import quantize_frozen_matrix
+    kat = json.load(open(os.path.join(GOLDEN, "quant_kat.json")))
+    good = np.array([r["w"] for r in kat["rows"]], np.float32)
+    for r in kat["raises"]:
+        row = np.array([r["w"]], np.float32)
+        for W in (row, np.concatenate([good, row, good])):
+            Wt = _to_dev(torch, W)
+            if layout == 0:
+                Wt = Wt.t().contiguous().t()
+            with pytest.raises(ValueError, match="non-finite|0/0"):
+                quantize_frozen_matrix(Wt)
+    Wt = _to_dev(torch, good)
+    if layout == 0:
+        Wt = Wt.t().contiguous().t()
+    qm = quantize_frozen_matrix(Wt)
+    assert qm.values.cpu().numpy().tolist() == [r["q"] for r in kat["rows"]]
 
 
 def test_non_finite_weight_raises(torch_cuda):

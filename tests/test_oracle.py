@@ -47,12 +47,27 @@ def test_quantizer_matches_numpy_restatement():
     assert np.array_equal(q, qn)
 
 
+def _numpy_nan_rows(W):
+    """Rows the reference rejects: Julia's clamp keeps a NaN quotient and
+    Int8(NaN) throws.  Non-finite weights, or a zero element in a row whose
+    max/127 underflowed to a zero scale (0/0)."""
+    m = np.abs(W).max(axis=1)
+    s = (m / np.float32(127)).astype(np.float32)
+    s[m == 0] = 1
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        t = W / s[:, None]
+    return np.isnan(t).any(axis=1) | ~np.isfinite(W).all(axis=1)
+
+
 def _numpy_quantize(W):
     m = np.abs(W).max(axis=1)
     s = (m / np.float32(127)).astype(np.float32)
     s[m == 0] = 1
     with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
-        qn = np.rint(np.clip(W / s[:, None], -127, 127)).astype(np.int8)
+        t = W / s[:, None]
+    if np.isnan(t).any():
+        raise ValueError("NaN quotient: Int8(NaN) throws InexactError")
+    qn = np.rint(np.clip(t, -127, 127)).astype(np.int8)
     return qn, s
 
 
@@ -65,7 +80,7 @@ def test_quantizer_extreme_rows_match_numpy():
     rows = [
         [np.finfo(f).max, -np.finfo(f).max, 1.0, 0.0],
         [tiny, -tiny / 2, tiny / 8, 0.0],                 # subnormal maxima and scales
-        [np.float32(1e-45), 0.0, -0.0, np.float32(-1e-45)],
+        [np.float32(1e-45), np.float32(-1e-45), np.float32(2e-45), -np.float32(3e-45)],  # scale 0
         [0.0, 0.0, 3.0, 0.0],
         [-0.0, -0.0, -0.0, -0.0],
         [127.0, 63.5, -0.5, 0.5],                         # exact scale 1: ties to even
@@ -77,6 +92,24 @@ def test_quantizer_extreme_rows_match_numpy():
     assert np.array_equal(s.view(np.uint32), sn.view(np.uint32))
     assert np.array_equal(q, qn)
     assert q[5].tolist() == [127, 64, 0, 0] and s[4] == 1
+    assert s[2] == 0 and q[2].tolist() == [127, -127, 127, -127]
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_quantizer_rejects_what_the_reference_rejects(layout):
+    """The hand-derived rows the reference throws InexactError on (a NaN
+    quotient reaching Int8): each alone and inside a matrix of good rows."""
+    bad = json.load(open(os.path.join(GOLDEN, "quant_kat.json")))["raises"]
+    good = np.array([r["w"] for r in _kat()], np.float32)
+    for r in bad:
+        row = np.array([r["w"]], np.float32)
+        for W in (row, np.concatenate([good, row, good])):
+            Wm = np.ascontiguousarray(W.T) if layout == 0 else W
+            with pytest.raises(ValueError):
+                oracle.quantize(Wm, layout)
+            with pytest.raises(ValueError):
+                _numpy_quantize(W)
+            assert _numpy_nan_rows(W).sum() == 1, r["why"]
 
 
 def test_quantizer_random_scales_match_numpy():
@@ -86,6 +119,13 @@ def test_quantizer_random_scales_match_numpy():
         e = g.integers(-140, 120, size=(32, 1))
         W = (g.standard_normal((32, 48)) * np.exp2(e)).astype(np.float32)
         W[g.random(W.shape) < 0.1] = 0
+        bad = _numpy_nan_rows(W)
+        if bad.any():
+            # rows with a zero scale and a zero element: the whole call raises
+            for layout in (0, 1):
+                with pytest.raises(ValueError):
+                    oracle.quantize(np.ascontiguousarray(W.T) if layout == 0 else W, layout)
+            W = W[~bad]
         qn, sn = _numpy_quantize(W)
         for layout in (0, 1):
             Wm = np.ascontiguousarray(W.T) if layout == 0 else W
