@@ -1,6 +1,6 @@
 """The reference's CPU code path for the quantised LoRA linear, in numpy.
 
-TEST / BASELINE INFRASTRUCTURE ONLY (imported by tests/ and by bench.py's
+TEST / CPU-BASELINE INFRASTRUCTURE ONLY (imported by tests/ and by bench.py's
 CPU-baseline leg).  This is what Reels.jl executes when the layer runs on the
 CPU in fp32 (the only CPU precision it allows, src/models/interface.jl:38-41):
 

@@ -15,7 +15,6 @@
 #include "../../include/reels_lowvram.h"
 #include "aux_kernels.cuh"
 #include "q8_gemm.cuh"
-#include "q8_gemm_2sm.cuh"
 #include "dropout.cuh"
 #include "norm.cuh"
 #include "optim.cuh"
@@ -100,7 +99,6 @@ struct DeviceState {
     bool ready = false;
     int index = -1;
     int sms = 148;
-    int pair_clusters = 0;  // co-resident 2-CTA clusters of the pair kernel
     unsigned *status = nullptr;
     unsigned *quant_status = nullptr;
 };
@@ -228,33 +226,6 @@ int bind_device(const void *ptr, DeviceState **out, DeviceScope &scope) {
                         (const void *)ln_modulate_kernel<DT_F32>, (const void *)ln_modulate_bwd_kernel<DT_BF16>,
                         (const void *)ln_modulate_bwd_kernel<DT_F16>, (const void *)ln_modulate_bwd_kernel<DT_F32>})
             REELS_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * LN_MAX_K * 4));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8PairGeom::SMEM_BYTES));
-        REELS_CUDA(cudaFuncSetAttribute(q8_gemm_pair_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        Q8PairGeom::SMEM_BYTES));
-        {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(2 * 74);
-            cfg.blockDim = dim3(Q8_THREADS);
-            cfg.dynamicSmemBytes = Q8PairGeom::SMEM_BYTES;
-            cudaLaunchAttribute at[1];
-            at[0].id = cudaLaunchAttributeClusterDimension;
-            at[0].val.clusterDim.x = 2;
-            at[0].val.clusterDim.y = 1;
-            at[0].val.clusterDim.z = 1;
-            cfg.attrs = at;
-            cfg.numAttrs = 1;
-            int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, q8_gemm_pair_kernel<DT_BF16>, &cfg) != cudaSuccess) {
-                cudaGetLastError();
-                n = 0;
-            }
-            st.pair_clusters = n;
-            if (const char *e = getenv("REELS_PAIR_CLUSTERS")) st.pair_clusters = std::max(0, atoi(e));
-            if (getenv("REELS_LOWVRAM_DEBUG"))
-                fprintf(stderr, "reels_lowvram: device %d: %d SMs, %d co-resident 2-CTA clusters (queried %d)\n",
-                        dev, st.sms, st.pair_clusters, n);
-        }
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         SK_SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -341,7 +312,6 @@ int npad_of(int64_t r) { return (int)std::max<int64_t>(16, round_up(r, 16)); }
 
 struct Q8Plan {
     int mt = 1, bn = 256;
-    bool pair = false;  // 2-CTA cluster kernel on 256x256 tiles
     int ts = 0;         // > 0: weight-in-TMEM kernel, 128 output columns x ts tokens
     int ts_kb2 = 1;     // its pipeline stages cover 64 * ts_kb2 reduction elements
     int64_t ntiles = 1, mtiles = 1;
@@ -362,13 +332,12 @@ struct Q8Plan {
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
 // split reduction adds the write and re-read of fp32 partials (~5 TB/s).
-// REELS_Q8_TILE ("MTxBN" or "pair") and REELS_Q8_TS (256, 192, 128; 2562,
+// REELS_Q8_TILE ("MTxBN") and REELS_Q8_TS (256, 192, 128; 2562,
 // 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements.
-Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters, bool allow_ts, int act) {
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, int act) {
     static const int forced = [] {
-        const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128") or "pair"
+        const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128")
         if (!e) return 0;
-        if (strcmp(e, "pair") == 0) return 1;
         int a = 0, b = 0;
         if (sscanf(e, "%dx%d", &a, &b) == 2 && (a == 1 || a == 2) && (b == 128 || b == 256)) return a * 1000 + b;
         return 0;
@@ -429,25 +398,6 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, int pair_clusters
             if (tiles >= sms) break;  // enough tiles: never split
         }
     }
-    // The pair kernel (256x256 tiles on 2-CTA clusters) is correct but
-    // measured slower than the single-CTA 2x256 plan on every BASELINE shape
-    // (about 770 vs 920-1130 TFLOP/s forward), so it runs only when forced.
-    if (pair_clusters > 0 && forced == 1) {
-        const int64_t kb = cdiv(Kred, BK);
-        const int64_t ntiles = cdiv(Nout, 256), mtiles = cdiv(M, 256);
-        const double units = (double)cdiv(ntiles * mtiles, pair_clusters);
-        const double cost = units * (kb * 0.95 * 1.18 + 1.5);
-        if (forced == 1 || cost < best) {
-            bestp = Q8Plan();
-            bestp.mt = 2;
-            bestp.bn = 256;
-            bestp.pair = true;
-            bestp.ntiles = ntiles;
-            bestp.mtiles = mtiles;
-            bestp.split.splits = 1;
-            bestp.split.kb_per = (int)kb;
-        }
-    }
     return bestp;
 }
 
@@ -490,11 +440,11 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags,
         if (s.splits > 1) part = std::max(part, (size_t)s.splits * rows * np * 4);
     };
     auto q8_part = [&](int64_t rows, int64_t cols, int64_t red) {
-        // the pair plan never splits; the TMEM-weight plan may fall back to the
-        // other; a fused activation weighs the plans differently
+        // the TMEM-weight plan may fall back to the other; a fused activation
+        // weighs the plans differently
         for (int ts = 0; ts < 2; ++ts)
             for (int act : {(int)ACT_NONE, (int)ACT_GELU_TANH}) {
-                Q8Plan p = plan_q8(rows, cols, red, sms, 0, ts == 1, act);
+                Q8Plan p = plan_q8(rows, cols, red, sms, ts == 1, act);
                 if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
             }
     };
@@ -876,7 +826,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
     // The TMEM-weight kernel loads the reduction scales by TMA (16-byte aligned base).
     const bool ts_ok = aligned16(c.scales);
-    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ds.pair_clusters, ts_ok, c.epi_act);
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ts_ok, c.epi_act);
     if (p.ts) return run_q8_ts(c, dt, ds, ws_base, wl, st, p);
     if (c.epi_act != ACT_NONE) {
         // The SMEM-operand kernels have no activation epilogue: the GEMM
@@ -895,10 +845,8 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
         return REELS_OK;
     }
     CUtensorMap ta, tw, te;
-    // Per-CTA boxes: the pair kernel loads 128 token rows and 128 weight
-    // columns per CTA of a 256x256 tile.
-    const int a_rows = p.pair ? 128 : 128 * p.mt;
-    const int w_box = p.pair ? 128 : p.bn;
+    const int a_rows = 128 * p.mt;
+    const int w_box = p.bn;
     int rc = tmap_2d(&ta, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, a_rows,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -983,15 +931,7 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
     const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
     dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
     cudaEvent_t ev_stop = prof_begin(st, c);
-    if (p.pair) {
-        const dim3 pgrid((unsigned)(2 * std::min<int64_t>(total_tiles, ds.pair_clusters)));
-        if (dt == REELS_BF16)
-            q8_gemm_pair_kernel<DT_BF16><<<pgrid, Q8_THREADS, Q8PairGeom::SMEM_BYTES, st>>>(ta, tw, te, a);
-        else
-            q8_gemm_pair_kernel<DT_F16><<<pgrid, Q8_THREADS, Q8PairGeom::SMEM_BYTES, st>>>(ta, tw, te, a);
-    } else {
-        launch_q8(dt, p.mt, p.bn, grid, st, ta, tw, te, a);
-    }
+    launch_q8(dt, p.mt, p.bn, grid, st, ta, tw, te, a);
     REELS_LAUNCHED();
     if (ev_stop) REELS_CUDA(cudaEventRecord(ev_stop, st));
     if (p.split.splits > 1) {
@@ -1081,9 +1021,9 @@ int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64
     if (!info) return fail("null info");
     if (M <= 0 || Nout <= 0 || Kred <= 0) return fail("plan needs positive M, Nout and Kred");
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
-    const Q8Plan p = plan_q8(M, Nout, Kred, sms > 0 ? sms : current_sms(), 0, true,
+    const Q8Plan p = plan_q8(M, Nout, Kred, sms > 0 ? sms : current_sms(), true,
                              act == REELS_ACT_NONE ? ACT_NONE : ACT_GELU_TANH);
-    info[0] = p.ts ? 1 : (p.pair ? 2 : 0);
+    info[0] = p.ts ? 1 : 0;
     info[1] = p.ts ? p.ts : 128 * p.mt;
     info[2] = p.ts ? 64 * p.ts_kb2 : BK;
     info[3] = p.split.splits;

@@ -17,10 +17,11 @@ distributed_sample_indices  :func:`distributed_sample_indices` (data/provider.jl
 ==========================  =========================================================
 
 The reference all-reduces every gradient after the whole backward, then
-synchronises the device.  :class:`OverlappedGradReducer` instead launches one
-fp32 sum all-reduce per layer on a separate stream as soon as that layer's
-dA/dB are written, so the exchange overlaps the backward of earlier layers;
-the 1/world scale follows the sum, as in the reference.  Only the adapter
+synchronises the device.  :class:`OverlappedGradReducer` instead launches the
+fp32 sum all-reduces on a separate stream as soon as a layer's dA/dB (or a
+bucket of layers' gradients) are written, so the exchange overlaps the
+backward of earlier layers; the 1/world scale follows the sum, as in the
+reference.  Only the adapter
 gradients cross NVLink; the int8 weights are replicated and frozen.
 """
 from __future__ import annotations
@@ -175,42 +176,91 @@ def distributed_sample_indices(rng: np.random.Generator, count: int, batch_size:
 
 
 class OverlappedGradReducer:
-    """Per-layer fp32 all-reduce of LoRA gradients on a side stream.
+    """Per-layer (or bucketed) fp32 all-reduce of LoRA gradients on a side
+    stream.
 
     Call :meth:`layer_done` with a layer's flat gradient buffer right after
     its backward kernels were enqueued on the compute stream; the side stream
     waits for them (an event), sums the buffer across ranks and scales it by
-    1/world.  :meth:`finish` makes the compute stream wait for every
-    reduction.  With the gloo backend (CPU tensors) the reductions run
+    1/world.  With ``bucket_bytes > 0`` the buffers are collected until a
+    bucket holds that many bytes and then reduced together: one collective
+    over their span when they are adjacent views of one buffer (as when the
+    caller lays the gradients out in backward order), else one per buffer.
+    :meth:`finish` reduces what is left and makes the compute stream wait for
+    every reduction.  With the gloo backend (CPU tensors) the reductions run
     synchronously, which is what the host-logic tests exercise.
     """
 
-    def __init__(self, rt, device: Optional[torch.device] = None):
+    def __init__(self, rt, device: Optional[torch.device] = None, bucket_bytes: int = 0):
         self.rt = rt
         self.world = 1 if isinstance(rt, SingleProcessRuntime) else rt.world_size
         self.cuda = device is not None and device.type == "cuda" and self.world > 1
         self.stream = torch.cuda.Stream(device=device) if self.cuda else None
         self.pending: List = []
         self.scale = np.float32(1.0 / self.world).item()
+        self.bucket_bytes = int(bucket_bytes)
+        self.bucket: List[torch.Tensor] = []
+        self.bucket_fill = 0
+        self.collectives = 0   # all-reduce launches so far (for tests and reports)
+
+    @staticmethod
+    def _span(tensors: Sequence[torch.Tensor]) -> Optional[torch.Tensor]:
+        """One 1-D view covering ``tensors`` when they are contiguous 1-D views
+        of one storage that together tile an interval; else None."""
+        t0 = tensors[0]
+        if any(t.dim() != 1 or not t.is_contiguous() or t.dtype != t0.dtype for t in tensors):
+            return None
+        st = t0.untyped_storage()
+        if any(t.untyped_storage().data_ptr() != st.data_ptr() for t in tensors):
+            return None
+        iv = sorted((t.storage_offset(), t.storage_offset() + t.numel()) for t in tensors)
+        for (_, e), (b, _) in zip(iv, iv[1:]):
+            if b != e:
+                return None
+        lo, hi = iv[0][0], iv[-1][1]
+        return t0.new_empty(0).set_(st, lo, (hi - lo,), (1,))
+
+    def _reduce(self, tensors: Sequence[torch.Tensor]) -> None:
+        span = self._span(tensors) if len(tensors) > 1 else tensors[0]
+        targets = [span] if span is not None else list(tensors)
+        if self.cuda:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(targets[0].device))
+            with torch.cuda.stream(self.stream):
+                self.stream.wait_event(ev)
+                for t in targets:
+                    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+                    t.mul_(self.scale)
+            for t in targets:
+                t.record_stream(self.stream)
+                self.pending.append(t)
+        else:
+            for t in targets:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM)
+                t.mul_(self.scale)
+        self.collectives += len(targets)
 
     def layer_done(self, flat_grad: torch.Tensor) -> None:
         if self.world == 1:
             return
         _check_open(self.rt)
-        if self.cuda:
-            ev = torch.cuda.Event()
-            ev.record(torch.cuda.current_stream(flat_grad.device))
-            with torch.cuda.stream(self.stream):
-                self.stream.wait_event(ev)
-                dist.all_reduce(flat_grad, op=dist.ReduceOp.SUM)
-                flat_grad.mul_(self.scale)
-            flat_grad.record_stream(self.stream)
-            self.pending.append(flat_grad)
-        else:
-            dist.all_reduce(flat_grad, op=dist.ReduceOp.SUM)
-            flat_grad.mul_(self.scale)
+        if self.bucket_bytes <= 0:
+            self._reduce([flat_grad])
+            return
+        self.bucket.append(flat_grad)
+        self.bucket_fill += flat_grad.numel() * flat_grad.element_size()
+        if self.bucket_fill >= self.bucket_bytes:
+            self._flush()
+
+    def _flush(self) -> None:
+        if self.bucket:
+            self._reduce(self.bucket)
+        self.bucket, self.bucket_fill = [], 0
 
     def finish(self) -> None:
+        if self.world > 1:
+            _check_open(self.rt)
+            self._flush()
         if self.cuda and self.pending:
             torch.cuda.current_stream(self.pending[0].device).wait_stream(self.stream)
         self.pending.clear()

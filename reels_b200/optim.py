@@ -208,67 +208,3 @@ def update_(opt: AdamW, state: AdamWState, params, grads, learning_rate: Optiona
         sumsq.data_ptr() if sumsq is not None else None,
         float(max_gradient_norm) if max_gradient_norm is not None else 0.0, stream))
     return sumsq
-
-
-def _bench():
-    """Time the optimizer step over the adapter tensors of Wan 2.1 14B at
-    rank 32 (40 blocks; per block 8 square 5120 linears and the 13824-wide
-    FFN pair, each an A and a B tensor; 153.4 M parameters in 800 tensors),
-    bf16 parameters, fp32 gradients: the norm launch and the clipped AdamW
-    launch, CUDA-event timed on the launching stream after warm-up.  Prints
-    one JSON line with microseconds and the HBM bandwidth of each, counted as
-    4 bytes per element for the norm and 30 for the update (g, m, v, master
-    read; m, v, master written; the 2-byte parameter written)."""
-    import json
-    import os
-    from . import build as native_build
-    native_build.build()
-    dev = torch.device("cuda", 0)
-    r, d, f = 32, 5120, 13824
-    shapes = []
-    for _ in range(40):
-        shapes += [(r * d, r * d)] * 8 + [(r * d, r * f), (r * f, r * d)]
-    sizes = [n for pair in shapes for n in pair]
-    params = [torch.zeros(n, dtype=torch.bfloat16, device=dev) for n in sizes]
-    grads = [torch.randn(n, device=dev) * 1e-3 for n in sizes]
-    total = sum(sizes)
-    opt = AdamW()
-    state = AdamWState(params)
-    sumsq = torch.empty((), dtype=torch.float32, device=dev)
-    ws = state._prepare(params, grads, None)
-    L = nat.lib()
-    st = torch.cuda.current_stream(dev).cuda_stream
-
-    def norm():
-        nat.check("norm", L.reels_grad_norm_sq(ws.data_ptr(), 1.0, sumsq.data_ptr(), st))
-
-    def upd():
-        nat.check("adamw", L.reels_adamw_update(ws.data_ptr(), 1e-4, 0.9, 0.999, 1e-8, 0.01, 0.1, 0.001, 1.0,
-                                                sumsq.data_ptr(), 1.0, st))
-
-    out = {"params": total, "tensors": len(sizes)}
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    try:
-        with open(os.path.join(root, "MEASURED_PEAKS.json")) as fh:
-            hbm = float(json.load(fh)["hbm_gbs"])
-    except (OSError, KeyError, ValueError):
-        hbm = 6650.0
-    for name, fn, bpe in (("norm", norm, 4), ("adamw", upd, 30)):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(10):
-            fn()
-        e1.record()
-        torch.cuda.synchronize(dev)
-        us = e0.elapsed_time(e1) / 10 * 1e3
-        gbs = bpe * total / (us * 1e-6) / 1e9
-        out[name] = {"us": round(us, 1), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3)}
-    nat.check("device status", L.reels_lowvram_check_device_status(st))
-    print(json.dumps(out), flush=True)
-
-
-if __name__ == "__main__":
-    _bench()

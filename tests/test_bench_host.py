@@ -127,3 +127,33 @@ def test_reference_arm_other_ranks_print_nothing():
                                 {"RANK": "1", "WORLD_SIZE": "2"})
     assert rc == 0, err[-2000:]
     assert lines == []
+
+
+def test_peak_follows_the_timed_region():
+    peaks = {"bf16_tflops": 1678.0, "bf16_tflops_sustained": 1420.7}
+    at_max = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0}
+    p, why = bench.pick_peak(peaks, "measured", 0.15, at_max)
+    assert p == 1678.0 and "burst" in why
+    p, why = bench.pick_peak(peaks, "measured", 5.0, at_max)
+    assert p == 1420.7 and "sustained" in why
+    p, why = bench.pick_peak(peaks, "measured", 0.15, {"sm_mhz": 1400.0, "sm_max_mhz": 1965.0})
+    assert p == 1420.7
+    assert bench.pick_peak(peaks, "measured", 0.15, None)[0] == 1420.7
+
+
+def test_cpu_step_extrapolates_the_sample_affinely(monkeypatch):
+    """The CPU baseline times the token linears at two sample sizes and the
+    context linears once; the full workload's time is the affine
+    extrapolation (a per-call cost plus a per-token cost) plus the context."""
+    wl = dict(name="t", layers=[("a", 1000, 16, 16), ("ctx", 7, 16, 16)], tokens=1000, rank=2, alpha=2.0,
+              context=7, blocks=3)
+    cs = bench.CpuStep(wl, small=100, large=200)
+    assert len(cs.tok) == 1 and len(cs.ctx) == 1 and cs.tok[0][0].shape == (200, 16)
+    cost = {100: 1.0 + 0.01 * 100, 200: 1.0 + 0.01 * 200}
+
+    def fake_run(group, m=None):
+        return cost[m] if m is not None else 0.5
+    monkeypatch.setattr(cs, "_run", fake_run)
+    est, took = cs.sample()
+    assert est == pytest.approx(3 * ((1.0 + 0.01 * 1000) + 0.5))
+    assert took == pytest.approx(2.0 + 3.0 + 0.5)

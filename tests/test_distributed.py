@@ -42,6 +42,19 @@ def _worker(rank, world, port, q):
         red.layer_done(flat)
         red.finish()
         out["flat"] = flat.tolist()
+        # buckets: adjacent views of one buffer in backward order reduce as
+        # one span; a view of another buffer reduces on its own
+        buf = torch.arange(12, dtype=torch.float32) * (rank + 1)
+        other = torch.full((3,), float(rank + 1))
+        red = rd.OverlappedGradReducer(rt, torch.device("cpu"), bucket_bytes=32)
+        red.layer_done(buf[8:12])
+        red.layer_done(buf[4:8])        # 32 bytes: one collective over buf[4:12]
+        red.layer_done(buf[0:4])
+        red.layer_done(other)           # left for finish(): not adjacent, two collectives
+        red.finish()
+        out["bucket_buf"] = buf.tolist()
+        out["bucket_other"] = other.tolist()
+        out["bucket_collectives"] = red.collectives
         out["scalar"] = rd.distributed_mean_scalar(rt, 2.0 * (rank + 1))
         # every rank draws the same permutation and takes a disjoint shard
         out["shard"] = rd.distributed_sample_indices(np.random.default_rng(7), 20, 4, rank, world).tolist()
@@ -69,6 +82,9 @@ def test_two_rank_gloo_runtime():
         assert res[r]["g0"] == [[1.5, 1.5]] * 3
         assert res[r]["g1"] == [0.0, 1.5, 3.0, 4.5, 6.0]
         assert res[r]["flat"] == [15.0] * 7
+        assert res[r]["bucket_buf"] == [1.5 * i for i in range(12)]
+        assert res[r]["bucket_other"] == [1.5] * 3
+        assert res[r]["bucket_collectives"] == 3
         assert res[r]["scalar"] == 3.0
     a, b = set(res[0]["shard"]), set(res[1]["shard"])
     assert len(a) == 4 and len(b) == 4 and not (a & b)

@@ -1,6 +1,6 @@
 """GPU parity of q8 GEMM plans the planner does not pick for these shapes by
-itself: the pair-CTA (cta_group::2) SMEM x SMEM kernel (REELS_Q8_TILE=pair),
-the SMEM x SMEM kernel (REELS_Q8_TS=0) and each token tile of the
+itself: the SMEM x SMEM kernel (REELS_Q8_TS=0, the plan for reduction scales
+that are not 16-byte aligned) and each token tile of the
 weight-in-TMEM kernel (REELS_Q8_TS=256/192/128, and 1282 for 128-token tiles
 with 128-wide pipeline stages).  The overrides are read once
 per process, so each plan runs its cases in a child process."""
@@ -42,7 +42,7 @@ CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1
          (1000, 640, 1152, 32, 1, "f16"), (2048, 1536, 640, 32, 0, "bf16")]
 
 
-@pytest.mark.parametrize("var,val", [("REELS_Q8_TILE", "pair"), ("REELS_Q8_TS", "0"), ("REELS_Q8_TS", "256"),
+@pytest.mark.parametrize("var,val", [("REELS_Q8_TS", "0"), ("REELS_Q8_TS", "256"),
                                      ("REELS_Q8_TS", "192"), ("REELS_Q8_TS", "128"), ("REELS_Q8_TS", "1282")])
 def test_forced_plan_parity(var, val):
     from reels_b200 import build

@@ -65,7 +65,7 @@ def test_committed_fixtures(torch, path):
 
 @pytest.fixture(scope="module")
 def cfg1(torch):
-    # BASELINE config 1: Wan-2.1-1.3B FFN up-proj, M=1280, K=1536, N=8960,
+    # Wan-2.1-1.3B FFN up-proj, M=1280, K=1536, N=8960,
     # r=16, alpha=16, bf16, seed 0.
     c = lc.make_case(1280, 1536, 8960, 16, alpha=16.0, dtype="bf16", layout=0, seed=0, a_std=1.0 / 16)
     return c, lc.oracle_outputs(c)
@@ -260,7 +260,7 @@ def test_autograd_function_matches_explicit_backward(torch):
 
 @pytest.mark.parametrize("M,K,N", [(8192, 1536, 8960), (32760, 1536, 1536)])
 def test_full_size_against_torch_fp32(torch, M, K, N):
-    """At BASELINE sizes the CPU oracle is too slow; compare with an fp32
+    """At the benchmark's full sizes the CPU oracle is too slow; compare with an fp32
     torch computation on the same dequantised weight (this is a floating-
     point kernel) -- Y and dX, r = 32."""
     from reels_b200 import lora_backward, lora_forward, materialize_weight

@@ -3,7 +3,7 @@
 The planners choose kernels, tiles and reduction splits from a time model
 fitted to B200 measurements; the workspace query must cover whatever they
 choose, or a split's fp32 partials would overrun the caller's buffer.  These
-properties are checked over the BASELINE shapes and a seeded spread of
+properties are checked over the benchmark shapes and a seeded spread of
 others."""
 import ctypes
 
@@ -44,7 +44,7 @@ def test_bench_shapes_take_the_256_token_tmem_tiles(lib):
 
 
 def test_small_token_counts_take_the_wide_stage_tiles(lib):
-    # BASELINE config 5 at 128 tokens: one 128-token tile, 128-wide stages
+    # the Wan 2.1 14B FFN up-projection at 128 tokens: one 128-token tile, 128-wide stages
     p = q8(lib, 128, 13824, 5120)
     assert p["kernel"] == 1 and p["tokens"] == 128 and p["stage"] == 128
     assert p["splits"] * p["kb_per"] * p["stage"] >= 5120  # the splits cover the reduction
