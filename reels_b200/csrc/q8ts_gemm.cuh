@@ -76,8 +76,7 @@ struct TsGeom {
     // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done, one pre-activation load per epilogue warp
     static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1 + TS_NEW;
     static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
-    static constexpr int SKTAB_OFF = MISC_OFF + 16;               // stream-K piece table
-    static constexpr int SMEM_BYTES = SKTAB_OFF + 8 * 9 * 4 + 16 + 1024;
+    static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
     static_assert(NACC * BT + NA * ACOLS <= 512, "TMEM plan exceeds 512 columns");
     // Stage ga uses barrier slot ga % NA: kb_full is completed by the
@@ -334,7 +333,6 @@ struct TsTile {
     int give;  // stream-K: a later piece of a cut tile; its accumulator goes to sk_part[blockIdx.x]
     int take;  // stream-K: the first piece of a cut tile; it adds the pieces of the next `take` CTAs
 };
-static_assert(sizeof(TsTile) == 9 * 4, "the stream-K table reserves 36 bytes per piece");
 
 // Tiles run output-column tile fastest, so the CTAs in flight share one
 // activation tile through L2 while the (small) weight stays resident there.
@@ -359,59 +357,45 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
 // First unit of stream-K run b (of g runs over w units).
 __device__ __forceinline__ long long sk_run_start(long long w, int g, int b) { return ((long long)b * w) / g; }
 
-// Stream-K pieces of one CTA.  The whole-tile rounds come first (at most two
-// rounds of tiles remain after them), so a CTA's run covers parts of at most
-// four tiles; TS_SK_MAX leaves room to spare.
-constexpr int TS_SK_MAX = 8;
-
-// Fills `tab` with the stream-K pieces of CTA b and returns their number
-// (one thread, once per CTA, before the roles start).
+// The idx-th piece of CTA b: false when the CTA has no more.  Every role of
+// the CTA walks the same sequence.  Without stream-K a piece is a whole tile
+// (or one reduction split of it), tiles t = b, b + g, ...
 template <int BT, int SK>
-__device__ int ts_sk_pieces(const TsArgs &a, int b, TsTile *tab) {
+__device__ __forceinline__ bool ts_piece(const TsArgs &a, int b, int idx, TsTile &c) {
     const int g = gridDim.x;
-    const long long W = a.sk_w, U = a.sk_units;
-    const long long s = sk_run_start(W, g, b), e = sk_run_start(W, g, b + 1);
-    int n = 0;
-    for (long long tr = s / U; s < e && tr * U < e && n < TS_SK_MAX; ++tr, ++n) {
-        TsTile c = ts_tile<BT, SK>(a, a.sk_tdp + (int)tr);  // splits == 1: the whole reduction and the LoRA blocks
-        const long long lo = (s > tr * U ? s : tr * U) - tr * U;
-        const long long hi = (e < (tr + 1) * U ? e : (tr + 1) * U) - tr * U;
-        const long long kt = a.kb_total;
-        c.kb0 = (int)lo;
-        c.n_main = (int)(lo < kt ? (hi < kt ? hi : kt) - lo : 0);
-        c.e0 = (int)(lo > kt ? lo - kt : 0);
-        c.n_ext = (int)(hi > kt ? hi - (lo > kt ? lo : kt) : 0);
-        c.give = lo > 0 ? 1 : 0;
-        c.take = 0;
-        if (lo == 0 && hi < U) {
-            // the CTA holding this tile's last unit
-            const long long x = (tr + 1) * U - 1;
-            int bl = (int)((x * g) / W);
-            while (bl + 1 < g && sk_run_start(W, g, bl + 1) <= x) ++bl;
-            while (bl > 0 && sk_run_start(W, g, bl) > x) --bl;
-            c.take = bl - b;
-        }
-        tab[n] = c;
-    }
-    return n;
-}
-
-// The idx-th piece of this CTA: false when the CTA has no more.  Every role
-// of the CTA walks the same sequence: whole tiles t = blockIdx.x, +gridDim.x,
-// ... (or one reduction split of them), then with stream-K the CTA's pieces
-// from `tab` (n_sk of them).
-template <int BT, int SK>
-__device__ __forceinline__ bool ts_piece(const TsArgs &a, int idx, const TsTile *tab, int n_sk, TsTile &c) {
-    const int g = gridDim.x;
-    const int whole = a.sk_w == 0 ? a.ntiles * a.mtiles * a.splits : a.sk_tdp;
-    const int t = blockIdx.x + idx * g;
-    if (t < whole) {
+    if (a.sk_w == 0) {
+        const int t = b + idx * g;
+        if (t >= a.ntiles * a.mtiles * a.splits) return false;
         c = ts_tile<BT, SK>(a, t);
         return true;
     }
-    const int k = idx - (whole - (int)blockIdx.x + g - 1) / g;  // index among the stream-K pieces
-    if (a.sk_w == 0 || k >= n_sk) return false;
-    c = tab[k];
+    const int dp = a.sk_tdp / g;  // whole-tile rounds before the stream-K region
+    if (idx < dp) {
+        c = ts_tile<BT, SK>(a, b + idx * g);
+        return true;
+    }
+    const long long W = a.sk_w, U = a.sk_units;
+    const long long s = sk_run_start(W, g, b), e = sk_run_start(W, g, b + 1);
+    const long long tr = s / U + (idx - dp);  // tile within the stream-K region
+    if (s >= e || tr * U >= e) return false;
+    c = ts_tile<BT, SK>(a, a.sk_tdp + (int)tr);  // splits == 1 here: the whole reduction and the LoRA blocks
+    const long long lo = (s > tr * U ? s : tr * U) - tr * U;
+    const long long hi = (e < (tr + 1) * U ? e : (tr + 1) * U) - tr * U;
+    const long long kt = a.kb_total;
+    c.kb0 = (int)lo;
+    c.n_main = (int)(lo < kt ? (hi < kt ? hi : kt) - lo : 0);
+    c.e0 = (int)(lo > kt ? lo - kt : 0);
+    c.n_ext = (int)(hi > kt ? hi - (lo > kt ? lo : kt) : 0);
+    c.give = lo > 0 ? 1 : 0;
+    c.take = 0;
+    if (lo == 0 && hi < U) {
+        // the CTA holding this tile's last unit
+        const long long x = (tr + 1) * U - 1;
+        int bl = (int)((x * g) / W);
+        while (bl + 1 < g && sk_run_start(W, g, bl + 1) <= x) ++bl;
+        while (bl > 0 && sk_run_start(W, g, bl) > x) --bl;
+        c.take = bl - b;
+    }
     return true;
 }
 
@@ -439,8 +423,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     uint64_t *pre_bar = mma_done + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + G::MISC_OFF);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + G::MISC_OFF + 4);
-    int *sk_count = reinterpret_cast<int *>(smem + G::MISC_OFF + 8);
-    TsTile *sk_tab = reinterpret_cast<TsTile *>(smem + G::SKTAB_OFF);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -461,7 +443,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         mbar_init(mma_done, 1);
         for (int i = 0; i < TS_NEW; ++i) mbar_init(&pre_bar[i], 1);
         *abort = 0;
-        *sk_count = args.sk_w > 0 ? ts_sk_pieces<BT, G::SK>(args, blockIdx.x, sk_tab) : 0;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -480,7 +461,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int n_sk = *sk_count;
     griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
 
@@ -490,7 +470,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         // ------------------------------------------------ activation producer
         uint32_t gx = 0;
         TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, pc, sk_tab, n_sk, c); ++pc) {
+        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
             for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
                 const int s = gx % G::SX;
                 if (gx >= (uint32_t)G::SX) {
@@ -531,7 +511,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         uint32_t gw = 0;
         const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
         TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, pc, sk_tab, n_sk, c); ++pc) {
+        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
             for (int it = 0; it < c.n_main; ++it, ++gw) {
                 const int s = gw % G::S8;
                 if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
@@ -562,7 +542,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
         uint32_t ga = 0, local = 0;
         TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, pc, sk_tab, n_sk, c); ++pc, ++local) {
+        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc, ++local) {
             const int acc = local % G::NACC;
             if (!wait_bar_all(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
@@ -623,7 +603,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int g = (warp - 3) / TS_GW;     // group: reduction blocks with ga % TS_NG == g
         uint32_t ga = 0, gw = 0;
         TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, pc, sk_tab, n_sk, c); ++pc) {
+        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
             // Per-lane scales (lanes 32q + 8i + t/4) for SMODE 1.
             float lane_s[4] = {0.f, 0.f, 0.f, 0.f};
             if (args.scale_mode == 1) {
@@ -733,7 +713,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             pre_pending = true;
         };
         TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, pc, sk_tab, n_sk, c); ++pc, ++local) {
+        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc, ++local) {
             const int acc = local % G::NACC;
             if (act == ACT_GELU_TANH_GRAD && !c.give && c.m0 + set * (BT / 2) < args.M) {
                 if (lane == 0)
