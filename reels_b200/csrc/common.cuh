@@ -24,7 +24,6 @@ enum DevErr : unsigned {
     DEVERR_TIMEOUT_W_FULL = 4u,
     DEVERR_TIMEOUT_W_EMPTY = 8u,
     DEVERR_TIMEOUT_ACC = 16u,
-    DEVERR_TIMEOUT_SK = 32u,  // a stream-K piece's hand-over from another CTA did not arrive
     DEVERR_NONFINITE_WEIGHT = 256u,
     DEVERR_OPT_TABLE = 512u,  // an optimizer workspace that was not prepared
     // a row whose max|w| / 127 underflows to 0 holds a zero: 0 / 0 is NaN

@@ -316,16 +316,7 @@ struct Q8Plan {
     int ts_kb2 = 1;     // its pipeline stages cover 64 * ts_kb2 reduction elements
     int64_t ntiles = 1, mtiles = 1;
     Split split;
-    // stream-K (weight-in-TMEM kernel only): sk_w > 0 units of sk_units per
-    // tile after sk_tdp tiles handed out whole, over `grid` CTAs
-    int64_t sk_tdp = 0, sk_units = 0, sk_w = 0;
-    int grid = 0;
 };
-
-// Workspace bytes of a stream-K launch: the hand-over flags (one per
-// epilogue warp per CTA) and one accumulator tile per CTA.
-size_t sk_flag_bytes(int grid) { return ((size_t)grid * TS_NEW * 4 + 255) & ~size_t(255); }
-size_t sk_bytes(int grid, int bt) { return sk_flag_bytes(grid) + (size_t)grid * 128 * bt * 4; }
 
 // Kernel, tile shape and reduction split from a time model fitted to B200
 // measurements (bf16; microseconds per pipeline stage of one tile, plus a
@@ -341,13 +332,9 @@ size_t sk_bytes(int grid, int bt) { return sk_flag_bytes(grid) + (size_t)grid * 
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
 // split reduction adds the write and re-read of fp32 partials (~5 TB/s).
-// Stream-K plans of the weight-in-TMEM kernel cost the rounds of whole
-// tiles, an equal run of the remaining units per CTA, two epilogues and the
-// hand-over of cut tiles' accumulators through L2.
 // REELS_Q8_TILE ("MTxBN") and REELS_Q8_TS (256, 192, 128; 2562,
-// 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements;
-// REELS_Q8_STREAMK=0 leaves out the stream-K plans, =1 keeps only them.
-Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int64_t r, int sms, bool allow_ts, int act) {
+// 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements.
+Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, int act) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128")
         if (!e) return 0;
@@ -361,13 +348,6 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int64_t r, int sms, bool a
         const int v = atoi(e);
         return (v == 256 || v == 192 || v == 128 || v == 2562 || v == 1922 || v == 1282) ? v : 0;
     }();
-    static const int forced_sk = [] {
-        const char *e = getenv("REELS_Q8_STREAMK");  // 0: no stream-K plans, 1: stream-K plans only
-        return e ? (atoi(e) != 0 ? 1 : 0) : -1;
-    }();
-    const bool forced_sk_off = forced_sk == 0;
-    // LoRA blocks a tile appends to its reduction
-    auto ext_blocks = [&](int kb2) -> int64_t { return r > 0 ? cdiv(r, BK * kb2) : 0; };
     struct Cand {
         int mt, bn, ts, kb2;
         double per_kb, epi;  // per_kb: per pipeline stage (64 * kb2 reduction elements)
@@ -393,37 +373,6 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int64_t r, int sms, bool a
         const int64_t ntiles = cd.ts ? cdiv(Nout, 128) : cdiv(Nout, cd.bn);
         const int64_t mtiles = cd.ts ? cdiv(M, cd.ts) : cdiv(M, 128 * cd.mt);
         const int64_t tiles = ntiles * mtiles;
-        // Stream-K (weight-in-TMEM kernel): whole tiles for all but the last
-        // one or two rounds, then every CTA takes an equal run of the
-        // remaining (tile, stage) units; a cut tile's other pieces hand their
-        // accumulators to the CTA that holds its first stages, through L2.
-        if (cd.ts && !forced_sk_off) {
-            const int64_t units = kb + ext_blocks(cd.kb2);
-            const int64_t dp = tiles >= 2 * sms ? tiles / sms - 1 : 0;
-            const int64_t w = (tiles - dp * sms) * units;
-            if (w >= sms) {
-                const double act_epi = act == ACT_NONE ? 0.0 : (cd.ts == 256 ? 1.5 : 0.1);
-                const double hand = 1.5 + (cd.ts == 256 ? 2.0 : 1.0);
-                const double cost = dp * (units * cd.per_kb + cd.epi + act_epi) + cdiv(w, sms) * cd.per_kb +
-                                    2.0 * (cd.epi + act_epi) + hand;
-                if (cost < best * 0.999) {
-                    best = cost;
-                    bestp = Q8Plan();
-                    bestp.mt = 1;
-                    bestp.bn = 128;
-                    bestp.ts = cd.ts;
-                    bestp.ts_kb2 = cd.kb2;
-                    bestp.ntiles = ntiles;
-                    bestp.mtiles = mtiles;
-                    bestp.split.kb_per = (int)kb;  // whole tiles cover the reduction
-                    bestp.sk_tdp = dp * sms;
-                    bestp.sk_units = units;
-                    bestp.sk_w = w;
-                    bestp.grid = sms;
-                }
-            }
-        }
-        if (cd.ts && forced_sk == 1) continue;  // forced stream-K: no whole-tile or split plans
         for (int64_t want = 1; want <= std::max<int64_t>(1, kb / 4); want = want < 4 ? want + 1 : want * 2) {
             Split sp;
             sp.kb_per = (int)cdiv(kb, want);
@@ -433,12 +382,11 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int64_t r, int sms, bool a
             // A fused activation lengthens the epilogue; with one accumulator
             // (256-token tiles) the MMAs wait for it.
             const double act_epi = act == ACT_NONE || sp.splits > 1 ? 0.0 : (cd.ts == 256 ? 1.5 : 0.1);
-            double cost = units * ((sp.kb_per + ext_blocks(cd.kb2)) * cd.per_kb + cd.epi + act_epi);
+            double cost = units * (sp.kb_per * cd.per_kb + cd.epi + act_epi);
             if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
             if (cost < best * 0.999) {
                 best = cost;
                 bestp = Q8Plan();
-                bestp.grid = (int)std::min<int64_t>(tiles * sp.splits, sms);
                 bestp.mt = cd.ts ? 1 : cd.mt;
                 bestp.bn = cd.ts ? 128 : cd.bn;
                 bestp.ts = cd.ts;
@@ -496,9 +444,8 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags,
         // weighs the plans differently
         for (int ts = 0; ts < 2; ++ts)
             for (int act : {(int)ACT_NONE, (int)ACT_GELU_TANH}) {
-                Q8Plan p = plan_q8(rows, cols, red, r, sms, ts == 1, act);
+                Q8Plan p = plan_q8(rows, cols, red, sms, ts == 1, act);
                 if (p.split.splits > 1) part = std::max(part, (size_t)p.split.splits * rows * cols * 4);
-                if (p.sk_w > 0) part = std::max(part, sk_bytes(p.grid, p.ts));
             }
     };
     if (M > 0) {
@@ -834,14 +781,6 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     a.err = ds.status;
     a.epi_act = c.epi_act;
     a.pre = c.pre;
-    if (p.sk_w > 0) {
-        a.sk_tdp = (int)p.sk_tdp;
-        a.sk_units = (int)p.sk_units;
-        a.sk_w = p.sk_w;
-        a.sk_flag = reinterpret_cast<unsigned *>(ws_base + wl.part);
-        a.sk_part = reinterpret_cast<float *>(ws_base + wl.part + sk_flag_bytes(p.grid));
-        REELS_CUDA(cudaMemsetAsync(a.sk_flag, 0, (size_t)p.grid * TS_NEW * 4, st));
-    }
     tp = tx;
     if (!a.epi_partial) {
         // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.
@@ -856,7 +795,8 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     } else {
         to = tx;
     }
-    const dim3 grid((unsigned)p.grid);
+    const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
+    const dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
     cudaEvent_t ev_stop = prof_begin(st, c);
     const int key = (dt == REELS_BF16 ? 10000 : 0) + bt * 10 + p.ts_kb2;
     switch (key) {
@@ -886,7 +826,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
 int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
     // The TMEM-weight kernel loads the reduction scales by TMA (16-byte aligned base).
     const bool ts_ok = aligned16(c.scales);
-    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, c.r, ds.sms, ts_ok, c.epi_act);
+    Q8Plan p = plan_q8(c.M, c.Nout, c.Kred, ds.sms, ts_ok, c.epi_act);
     if (p.ts) return run_q8_ts(c, dt, ds, ws_base, wl, st, p);
     if (c.epi_act != ACT_NONE) {
         // The SMEM-operand kernels have no activation epilogue: the GEMM
@@ -1081,9 +1021,9 @@ int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64
     if (!info) return fail("null info");
     if (M <= 0 || Nout <= 0 || Kred <= 0) return fail("plan needs positive M, Nout and Kred");
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
-    const Q8Plan p = plan_q8(M, Nout, Kred, 0, sms > 0 ? sms : current_sms(), true,
+    const Q8Plan p = plan_q8(M, Nout, Kred, sms > 0 ? sms : current_sms(), true,
                              act == REELS_ACT_NONE ? ACT_NONE : ACT_GELU_TANH);
-    info[0] = p.ts ? (p.sk_w > 0 ? 2 : 1) : 0;
+    info[0] = p.ts ? 1 : 0;
     info[1] = p.ts ? p.ts : 128 * p.mt;
     info[2] = p.ts ? 64 * p.ts_kb2 : BK;
     info[3] = p.split.splits;

@@ -117,30 +117,7 @@ struct TsArgs {
     void *pre;         // the rounded pre-activation [M][Nout]: written (gelu), read (gradient); nullable for gelu
     float *partial;    // [splits][M][Nout]
     unsigned *err;
-    // Stream-K (sk_w > 0): the first sk_tdp tiles are handed out whole, tile
-    // t to CTA t % gridDim.x; the remaining tiles' units (sk_units per tile:
-    // the main reduction stages, then the LoRA blocks) are cut into
-    // gridDim.x contiguous runs, run b going to CTA b.  A tile cut across
-    // runs is finished by the CTA holding its first units: the other pieces
-    // leave their fp32 accumulator fragments in sk_part[b] and raise
-    // sk_flag[b] (zeroed before the launch), and that CTA adds them in its
-    // epilogue.
-    int sk_tdp;
-    int sk_units;
-    long long sk_w;
-    float *sk_part;     // [gridDim.x][128 * BT] fp32, in epilogue fragment order
-    unsigned *sk_flag;  // [gridDim.x]
 };
-
-// Device-side flag helpers for the stream-K hand-over between CTAs.
-__device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -329,9 +306,7 @@ __device__ __forceinline__ void ts_dequant_block(uint32_t w_base, uint32_t sc_ba
 
 
 struct TsTile {
-    int n0, m0, sp, kb0, n_main, e0, n_ext;
-    int give;  // stream-K: a later piece of a cut tile; its accumulator goes to sk_part[blockIdx.x]
-    int take;  // stream-K: the first piece of a cut tile; it adds the pieces of the next `take` CTAs
+    int n0, m0, sp, kb0, n_main, n_ext;
 };
 
 // Tiles run output-column tile fastest, so the CTAs in flight share one
@@ -347,56 +322,8 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
     c.m0 = mt * BT;
     c.kb0 = c.sp * a.kb_per_split;
     c.n_main = max(0, min(a.kb_total, c.kb0 + a.kb_per_split) - c.kb0);
-    c.e0 = 0;
     c.n_ext = (c.sp == a.splits - 1 && a.r > 0) ? (a.r + SK - 1) / SK : 0;
-    c.give = 0;
-    c.take = 0;
     return c;
-}
-
-// First unit of stream-K run b (of g runs over w units).
-__device__ __forceinline__ long long sk_run_start(long long w, int g, int b) { return ((long long)b * w) / g; }
-
-// The idx-th piece of CTA b: false when the CTA has no more.  Every role of
-// the CTA walks the same sequence.  Without stream-K a piece is a whole tile
-// (or one reduction split of it), tiles t = b, b + g, ...
-template <int BT, int SK>
-__device__ __forceinline__ bool ts_piece(const TsArgs &a, int b, int idx, TsTile &c) {
-    const int g = gridDim.x;
-    if (a.sk_w == 0) {
-        const int t = b + idx * g;
-        if (t >= a.ntiles * a.mtiles * a.splits) return false;
-        c = ts_tile<BT, SK>(a, t);
-        return true;
-    }
-    const int dp = a.sk_tdp / g;  // whole-tile rounds before the stream-K region
-    if (idx < dp) {
-        c = ts_tile<BT, SK>(a, b + idx * g);
-        return true;
-    }
-    const long long W = a.sk_w, U = a.sk_units;
-    const long long s = sk_run_start(W, g, b), e = sk_run_start(W, g, b + 1);
-    const long long tr = s / U + (idx - dp);  // tile within the stream-K region
-    if (s >= e || tr * U >= e) return false;
-    c = ts_tile<BT, SK>(a, a.sk_tdp + (int)tr);  // splits == 1 here: the whole reduction and the LoRA blocks
-    const long long lo = (s > tr * U ? s : tr * U) - tr * U;
-    const long long hi = (e < (tr + 1) * U ? e : (tr + 1) * U) - tr * U;
-    const long long kt = a.kb_total;
-    c.kb0 = (int)lo;
-    c.n_main = (int)(lo < kt ? (hi < kt ? hi : kt) - lo : 0);
-    c.e0 = (int)(lo > kt ? lo - kt : 0);
-    c.n_ext = (int)(hi > kt ? hi - (lo > kt ? lo : kt) : 0);
-    c.give = lo > 0 ? 1 : 0;
-    c.take = 0;
-    if (lo == 0 && hi < U) {
-        // the CTA holding this tile's last unit
-        const long long x = (tr + 1) * U - 1;
-        int bl = (int)((x * g) / W);
-        while (bl + 1 < g && sk_run_start(W, g, bl + 1) <= x) ++bl;
-        while (bl > 0 && sk_run_start(W, g, bl) > x) --bl;
-        c.take = bl - b;
-    }
-    return true;
 }
 
 template <int DT, int BT, int KB2, int ACT>
@@ -426,6 +353,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int total_tiles = args.ntiles * args.mtiles * args.splits;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < G::S8; ++i) {
@@ -469,8 +397,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------ activation producer
         uint32_t gx = 0;
-        TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
                 const int s = gx % G::SX;
                 if (gx >= (uint32_t)G::SX) {
@@ -493,7 +421,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     } else {
                         // rank atoms of [64 ranks][BT tokens], tokens contiguous (BT/64 boxes of 64 x 64);
                         // atoms wholly past r are not loaded (the MMA does not read them)
-                        const int e = c.e0 + it - c.n_main;
+                        const int e = it - c.n_main;
                         const int na = min(KB2, (args.r - G::SK * e + 63) / 64);
                         mbar_arrive_expect_tx(full, na * BT * 128);
                         for (int a = 0; a < na; ++a)
@@ -510,8 +438,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         // ------------------------------------------------ int8 weight (+ scale) producer
         uint32_t gw = 0;
         const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
-        TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main; ++it, ++gw) {
                 const int s = gw % G::S8;
                 if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
@@ -541,8 +469,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const uint64_t dmain0 = sdesc_sw128(sbase + G::X_OFF, 16, 1024);
         const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
         uint32_t ga = 0, local = 0;
-        TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc, ++local) {
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
             if (!wait_bar_all(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
                 aborted_here = true;
@@ -571,7 +499,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                                        dmain0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 32) >> 4),
                                        id_main, (it > 0 || kk > 0) ? 1u : 0u);
                     } else {
-                        const int e = c.e0 + it - c.n_main;
+                        const int e = it - c.n_main;
                         const int nk = (min(G::SK, args.r - G::SK * e) + 15) / 16;
                         for (int kk = 0; kk < nk; ++kk)
                             mma_f16_ts(d_tm, a_tm + 8 * kk,
@@ -602,8 +530,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int q = warp & 3;               // TMEM lane quarter
         const int g = (warp - 3) / TS_GW;     // group: reduction blocks with ga % TS_NG == g
         uint32_t ga = 0, gw = 0;
-        TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc) {
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             // Per-lane scales (lanes 32q + 8i + t/4) for SMODE 1.
             float lane_s[4] = {0.f, 0.f, 0.f, 0.f};
             if (args.scale_mode == 1) {
@@ -648,7 +576,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 } else {
                     // LoRA block: rows n0 + lane of the prepared [Nout][rp] operand,
                     // 16-bit pairs already in TMEM column order.
-                    const int e = c.e0 + it - c.n_main;
+                    const int e = it - c.n_main;
                     const uint16_t *src = reinterpret_cast<const uint16_t *>(args.ext_w);
 #pragma unroll
                     for (int h = 0; h < 2 * KB2; ++h)
@@ -712,10 +640,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             }
             pre_pending = true;
         };
-        TsTile c;
-        for (int pc = 0; !aborted_here && ts_piece<BT, G::SK>(args, blockIdx.x, pc, c); ++pc, ++local) {
+        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
+            const TsTile c = ts_tile<BT, G::SK>(args, t);
             const int acc = local % G::NACC;
-            if (act == ACT_GELU_TANH_GRAD && !c.give && c.m0 + set * (BT / 2) < args.M) {
+            if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) {
                 if (lane == 0)
                     for (int ch = 1; ch < BT / 64; ++ch)
                         if (c.m0 + set * (BT / 2) + 32 * ch < args.M)
@@ -729,67 +657,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             tc_fence_after();
             const uint32_t t_base = tmem + ((uint32_t)(32 * q) << 16) + G::acc_col(acc);
             constexpr int NCH = BT / 64;  // 32-column chunks per epilogue set
-            // Stream-K hand-over: this warp's fragments of a piece, 32 fp32 per
-            // thread per chunk, at [ew][chunk][lane] of the CTA's region.
-            auto sk_frag = [&](int cta, int ch) -> float * {
-                return args.sk_part + (size_t)cta * (128 * BT) + ((size_t)(ew * NCH + ch) * 32 + lane) * 32;
-            };
-            if (c.give) {
-                // A later piece of a cut tile: leave the accumulator for the
-                // CTA that finishes the tile, then raise this warp's flag.
-                for (int ch = 0; ch < NCH; ++ch) {
-                    const int j0 = set * (BT / 2) + 32 * ch;
-                    uint32_t r[2][16];
-                    tmem_ld_16x256b_x4(t_base + j0, r[0]);
-                    tmem_ld_16x256b_x4(t_base + (16u << 16) + j0, r[1]);
-                    tmem_wait_ld();
-                    if (ch == NCH - 1) {
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                    }
-                    uint4 *dst = reinterpret_cast<uint4 *>(sk_frag(blockIdx.x, ch));
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        __stcg(dst + u, make_uint4(r[0][4 * u], r[0][4 * u + 1], r[0][4 * u + 2], r[0][4 * u + 3]));
-                        __stcg(dst + 4 + u, make_uint4(r[1][4 * u], r[1][4 * u + 1], r[1][4 * u + 2], r[1][4 * u + 3]));
-                    }
-                }
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) st_release_gpu(args.sk_flag + (size_t)blockIdx.x * TS_NEW + ew, 1u);
-                continue;
-            }
-            if (c.take > 0) {
-                // The first piece of a cut tile: wait (bounded) until the
-                // next c.take CTAs have left this warp's fragments.
-                int okw = 1;
-                if (lane == 0) {
-                    for (int k = 1; k <= c.take && okw; ++k) {
-                        const unsigned *f = args.sk_flag + (size_t)(blockIdx.x + k) * TS_NEW + ew;
-                        const long long t0 = clock64();
-                        while (ld_acquire_gpu(f) == 0u) {
-                            if (*abort) {
-                                okw = 0;
-                                break;
-                            }
-                            if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
-                                *abort = 1;
-                                atomicOr(args.err, DEVERR_TIMEOUT_SK);
-                                okw = 0;
-                                break;
-                            }
-                            __nanosleep(256);
-                        }
-                    }
-                }
-                okw = __shfl_sync(0xffffffffu, okw, 0);
-                __syncwarp();
-                if (!okw) {
-                    aborted_here = true;
-                    break;
-                }
-            }
             if (args.epi_partial) {
                 const int n = c.n0 + 32 * q + lane;
                 const bool n_ok = n < args.Nout;
@@ -837,19 +704,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&acc_empty[acc]);
-                }
-                // the other pieces of a cut tile, in CTA order
-                for (int k = 1; k <= c.take; ++k) {
-                    const uint4 *src = reinterpret_cast<const uint4 *>(sk_frag(blockIdx.x + k, ch));
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const uint4 w = __ldcg(src + u);
-                        uint32_t *rr = u < 4 ? &r[0][4 * u] : &r[1][4 * (u - 4)];
-                        rr[0] = __float_as_uint(__uint_as_float(rr[0]) + __uint_as_float(w.x));
-                        rr[1] = __float_as_uint(__uint_as_float(rr[1]) + __uint_as_float(w.y));
-                        rr[2] = __float_as_uint(__uint_as_float(rr[2]) + __uint_as_float(w.z));
-                        rr[3] = __float_as_uint(__uint_as_float(rr[3]) + __uint_as_float(w.w));
-                    }
                 }
                 const int m_base = c.m0 + j0;
                 const bool rows_ok = m_base < args.M;  // rows past M are clipped by the TMA unit
