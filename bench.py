@@ -382,27 +382,27 @@ def small_m_cases(L, nat, torch, dev, tokens=(128, 512), ranks=(8,), reps=20, N=
             wsn = max(L.reels_q8lora_workspace_bytes(M, K, N, r, dt, p | flag) for p in (0, 1))
             ws = torch.empty((max(wsn, 256),), dtype=torch.uint8, device=dev)
 
-            def fwd():
+            def fwd(stream=st):
                 if dropout > 0:
                     nat.check("forward", L.reels_q8lora_forward_dropout(
                         x.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(), None, M, K, N, r,
-                        alpha, dt, dropout, 1, 0, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, st))
+                        alpha, dt, dropout, 1, 0, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, stream))
                     return
                 nat.check("forward", L.reels_q8lora_forward(
                     x.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(), None, M, K, N, r, alpha,
-                    dt, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, st))
+                    dt, y.data_ptr(), saved.data_ptr(), ws.data_ptr(), wsn, stream))
 
-            def bwd():
+            def bwd(stream=st):
                 if dropout > 0:
                     nat.check("backward", L.reels_q8lora_backward_dropout(
                         x.data_ptr(), dy.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(),
                         saved.data_ptr(), M, K, N, r, alpha, 1.0 / loss_scale, dt, dropout, 1, 0, dx.data_ptr(),
-                        grad.data_ptr(), grad.data_ptr() + 4 * K * r, 0, ws.data_ptr(), wsn, st))
+                        grad.data_ptr(), grad.data_ptr() + 4 * K * r, 0, ws.data_ptr(), wsn, stream))
                     return
                 nat.check("backward", L.reels_q8lora_backward(
                     x.data_ptr(), dy.data_ptr(), q.data_ptr(), s.data_ptr(), 0, A.data_ptr(), B.data_ptr(),
                     saved.data_ptr(), M, K, N, r, alpha, 1.0 / loss_scale, dt, dx.data_ptr(), grad.data_ptr(),
-                    grad.data_ptr() + 4 * K * r, 0, ws.data_ptr(), wsn, st))
+                    grad.data_ptr() + 4 * K * r, 0, ws.data_ptr(), wsn, stream))
 
             res = {}
             for name, fn in (("fwd", fwd), ("bwd", bwd)):
@@ -416,6 +416,28 @@ def small_m_cases(L, nat, torch, dev, tokens=(128, 512), ranks=(8,), reps=20, N=
                 e1.record()
                 torch.cuda.synchronize(dev)
                 res[name] = e0.elapsed_time(e1) / reps * 1e3
+            # The same fwd+bwd captured once in a CUDA graph and replayed: the
+            # device time without the host's per-call launch overhead.
+            us_graph = None
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    gs = torch.cuda.current_stream(dev).cuda_stream
+                    fwd(gs)
+                    bwd(gs)
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                us_graph = e0.elapsed_time(e1) / reps * 1e3
+                del graph
+            except Exception as exc:  # reported, not hidden: the eager figures stand
+                us_graph = f"graph capture failed: {exc}"
             nat.check("device status", L.reels_lowvram_check_device_status(st))
             us = res["fwd"] + res["bwd"]
             e = 2  # bytes per activation element
@@ -427,7 +449,11 @@ def small_m_cases(L, nat, torch, dev, tokens=(128, 512), ranks=(8,), reps=20, N=
             tfl = flops / (us * 1e-6) / 1e12
             out.append({"shape": f"W {N}x{K}", "tokens": M, "rank": r, "dtype": dtype, "loss_scale": loss_scale,
                         "dropout": dropout, "us_fwd": round(res["fwd"], 1), "us_bwd": round(res["bwd"], 1),
-                        "us": round(us, 1), "tflops": round(tfl, 1), "tensor_frac": round(tfl / tf_peak, 3),
+                        "us": round(us, 1),
+                        "us_graph": round(us_graph, 1) if isinstance(us_graph, float) else us_graph,
+                        "hbm_frac_graph": (round(byts / (us_graph * 1e-6) / 1e9 / hbm, 3)
+                                           if isinstance(us_graph, float) else None),
+                        "tflops": round(tfl, 1), "tensor_frac": round(tfl / tf_peak, 3),
                         "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3), "algorithmic_bytes": int(byts),
                         "algorithmic_flops": flops, "peaks": f"hbm_gbs {hbm:.0f}, bf16_tflops {tf_peak:.0f} "
                                                              f"({kind})"})

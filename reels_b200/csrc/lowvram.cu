@@ -690,6 +690,31 @@ cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
     return pr.second;
 }
 
+// L2 prefetch distances of the weight-in-TMEM kernel.  REELS_TS_PF="w,x"
+// sets both for measurements.
+void ts_prefetch(const Q8Plan &p, int64_t M, int &pf_w, int &pf_x) {
+    static const int forced[2] = {-1, -1};
+    static const bool have = [] {
+        const char *e = getenv("REELS_TS_PF");
+        int w = -1, x = -1;
+        if (e && sscanf(e, "%d,%d", &w, &x) == 2 && w >= 0 && x >= 0) {
+            const_cast<int *>(forced)[0] = w;
+            const_cast<int *>(forced)[1] = x;
+            return true;
+        }
+        return false;
+    }();
+    if (have) {
+        pf_w = forced[0];
+        pf_x = forced[1];
+        return;
+    }
+    pf_w = 0;
+    pf_x = 0;
+    (void)p;
+    (void)M;
+}
+
 // The weight-in-TMEM kernel (q8ts_gemm.cuh).
 int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st,
               const Q8Plan &p) {
@@ -781,6 +806,7 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     a.err = ds.status;
     a.epi_act = c.epi_act;
     a.pre = c.pre;
+    ts_prefetch(p, c.M, a.pf_w, a.pf_x);
     tp = tx;
     if (!a.epi_partial) {
         // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.

@@ -117,6 +117,11 @@ struct TsArgs {
     void *pre;         // the rounded pre-activation [M][Nout]: written (gelu), read (gradient); nullable for gelu
     float *partial;    // [splits][M][Nout]
     unsigned *err;
+    // L2 prefetch distances, in pipeline stages, of the weight and activation
+    // tiles (0: none).  The weight stream is latency-bound when few tokens
+    // share a weight tile: a prefetch keeps stages in flight beyond the
+    // shared-memory ring at no shared-memory cost.
+    int pf_w, pf_x;
 };
 
 __device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
@@ -401,6 +406,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
                 const int s = gx % G::SX;
+                if (lane == 0 && args.pf_x > 0) {
+                    // L2 prefetch of activation stages ahead of the ring
+                    for (int j = (it == 0 ? 1 : it + args.pf_x); j <= it + args.pf_x && j < c.n_main; ++j)
+#pragma unroll
+                        for (int a = 0; a < KB2; ++a) tma_prefetch_l2_2d(&tmX, (c.kb0 + j) * G::SK + 64 * a, c.m0);
+                }
                 if (gx >= (uint32_t)G::SX) {
                     const uint32_t j = gx - G::SX;  // the block that last used this X slot
                     if (!wait_bar_all(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
@@ -442,6 +453,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             const TsTile c = ts_tile<BT, G::SK>(args, t);
             for (int it = 0; it < c.n_main; ++it, ++gw) {
                 const int s = gw % G::S8;
+                if (lane == 0 && args.pf_w > 0) {
+                    // L2 prefetch of weight stages ahead of the ring (the first
+                    // call of a tile covers stages 1 .. pf_w)
+                    for (int j = (it == 0 ? 1 : it + args.pf_w); j <= it + args.pf_w && j < c.n_main; ++j) {
+                        const int kb = c.kb0 + j;
+                        if (args.w_rows_red == 0) tma_prefetch_l2_2d(&tmW, kb * G::SK, c.n0);
+                        else tma_prefetch_l2_2d(&tmW, c.n0, kb * G::SK);
+                    }
+                }
                 if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
                     aborted_here = true;
                     break;
