@@ -414,6 +414,8 @@ struct Ws {
 // Rank padding of the prepared LoRA operands: a multiple of the widest
 // pipeline stage (128 reduction elements).
 int64_t rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 128); }
+// The weight-in-TMEM kernel reads its LoRA operand 32 ranks at a time.
+int64_t ts_rank_pad(int64_t r) { return round_up(std::max<int64_t>(r, 1), 32); }
 
 Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags, int sms) {
     Ws w;
@@ -566,56 +568,71 @@ __global__ void prep_ext_fwd_kernel(const T *B, const float *scales, float s, in
     }
 }
 
-// Forward LoRA operand of the TMEM-weight kernel, output-column major:
-// E[n][j] = B[j][n] * s (/ scale[n]), [N][rp].  A block transposes a tile of
-// 32 columns x rp ranks through shared memory: B rows are read along n and E
-// rows written along j, both coalesced.
+// The LoRA operands of one pass in a single launch.  Blocks [0, nb_ext)
+// write the weight-in-TMEM kernel's extension operand:
+//   ext_kind 0 (forward): E[n][j] = B[j][n] * s (/ scale[n]), [nrows = N][rp];
+//     a block transposes 32 output columns through shared memory (B read
+//     along n, E written along j);
+//   ext_kind 1 (dX):      E[k][j] = A[k][j], [nrows = K][rp], eight ranks per
+//     thread and one 16-byte store;
+// columns j >= r are zero.  The other blocks write At = A^T [r][K], the
+// rank-down GEMM's operand (none when gridDim.x == nb_ext).
 template <typename T>
-__global__ void prep_ext_fwd_rows_kernel(const T *B, const float *scales, float s,
-                                         int divide, int r, int rp, int N, T *__restrict__ out) {
+__global__ void prep_lora_kernel(int ext_kind, const T *B, const float *scales, float s, int divide, int r, int rp,
+                                 int nrows, T *__restrict__ ext, int nb_ext, const uint16_t *A, int K,
+                                 uint16_t *__restrict__ At) {
     griddep_wait();
     __shared__ float tile[128][33];
-    const int n0 = blockIdx.x * 32;
-    for (int jb = 0; jb < rp; jb += 128) {
-        // load B[jb .. jb+127][n0 .. n0+31] (zero past r or N)
-        for (int e = threadIdx.x; e < 128 * 32; e += blockDim.x) {
-            const int jj = e >> 5, nn = e & 31;
-            const int j = jb + jj, n = n0 + nn;
-            float v = 0.0f;
-            if (j < r && n < N) {
-                v = to_f32(B[(int64_t)j * N + n]) * s;
-                if (divide) v = v / scales[n];
+    if ((int)blockIdx.x < nb_ext) {
+        if (ext_kind == 0) {
+            const int n0 = blockIdx.x * 32;
+            for (int jb = 0; jb < rp; jb += 128) {
+                for (int e = threadIdx.x; e < 128 * 32; e += blockDim.x) {
+                    const int jj = e >> 5, nn = e & 31;
+                    const int j = jb + jj, n = n0 + nn;
+                    float v = 0.0f;
+                    if (j < r && n < nrows) {
+                        v = to_f32(B[(int64_t)j * nrows + n]) * s;
+                        if (divide) v = v / scales[n];
+                    }
+                    tile[jj][nn] = v;
+                }
+                __syncthreads();
+                const int jw = min(128, rp - jb);
+                for (int e = threadIdx.x; e < 32 * jw; e += blockDim.x) {
+                    const int nn = e / jw, jj = e - nn * jw;
+                    const int n = n0 + nn;
+                    if (n < nrows)
+                        ext[(int64_t)n * rp + jb + jj] =
+                            Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(tile[jj][nn]);
+                }
+                __syncthreads();
             }
-            tile[jj][nn] = v;
-        }
-        __syncthreads();
-        const int jw = min(128, rp - jb);
-        for (int e = threadIdx.x; e < 32 * jw; e += blockDim.x) {
-            const int nn = e / jw, jj = e - nn * jw;
-            const int n = n0 + nn;
-            if (n < N) out[(int64_t)n * rp + jb + jj] = Elem<std::is_same<T, __half>::value ? DT_F16 : DT_BF16>::from_f(tile[jj][nn]);
-        }
-        __syncthreads();
-    }
-}
-
-// dX LoRA operand E[k][j] = A[k][j] (j < r), zero-padded to rp columns.
-// Eight columns per thread, one 16-byte store.
-__global__ void prep_ext_dx_kernel(const uint16_t *A, int K, int r, int rp, uint16_t *__restrict__ out) {
-    griddep_wait();
-    const int per_row = rp / 8;
-    const int total = K * per_row;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int k = i / per_row, j0 = (i - k * per_row) * 8;
-        uint16_t v[8];
+        } else {
+            const uint16_t *a16 = A;
+            uint16_t *e16 = reinterpret_cast<uint16_t *>(ext);
+            const int per_row = rp / 8;
+            const int total = nrows * per_row;
+            for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += nb_ext * blockDim.x) {
+                const int k = i / per_row, j0 = (i - k * per_row) * 8;
+                uint16_t v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = (j0 + u < r) ? A[(int64_t)k * r + j0 + u] : (uint16_t)0;
-        uint4 w;
-        w.x = v[0] | ((uint32_t)v[1] << 16);
-        w.y = v[2] | ((uint32_t)v[3] << 16);
-        w.z = v[4] | ((uint32_t)v[5] << 16);
-        w.w = v[6] | ((uint32_t)v[7] << 16);
-        *reinterpret_cast<uint4 *>(out + (int64_t)k * rp + j0) = w;
+                for (int u = 0; u < 8; ++u) v[u] = (j0 + u < r) ? a16[(int64_t)k * r + j0 + u] : (uint16_t)0;
+                uint4 w;
+                w.x = v[0] | ((uint32_t)v[1] << 16);
+                w.y = v[2] | ((uint32_t)v[3] << 16);
+                w.z = v[4] | ((uint32_t)v[5] << 16);
+                w.w = v[6] | ((uint32_t)v[7] << 16);
+                *reinterpret_cast<uint4 *>(e16 + (int64_t)k * rp + j0) = w;
+            }
+        }
+        return;
+    }
+    const int total = K * r;
+    const int nb = gridDim.x - nb_ext;
+    for (int i = (blockIdx.x - nb_ext) * blockDim.x + threadIdx.x; i < total; i += nb * blockDim.x) {
+        const int j = i / K, k = i - j * K;
+        At[i] = A[k * r + j];
     }
 }
 
@@ -636,6 +653,7 @@ struct Q8Call {
     void *out;
     int epi_act = ACT_NONE;  // fused output activation (act.cuh)
     void *pre = nullptr;     // its rounded pre-activation [M][Nout]
+    bool ext_ready = false;  // the weight-in-TMEM kernel's LoRA operand is already in ext_buf
 };
 
 template <int DT, int MT, int BN>
@@ -715,6 +733,9 @@ void ts_prefetch(const Q8Plan &p, int64_t M, int &pf_w, int &pf_x) {
     (void)M;
 }
 
+int prep_lora(int dt, int ext_kind, const void *B, const float *scales, float s, bool divide, int64_t r, int64_t rp,
+              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st);
+
 // The weight-in-TMEM kernel (q8ts_gemm.cuh).
 int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st,
               const Q8Plan &p) {
@@ -779,24 +800,18 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
         tsc = tx;
     }
     a.r = (int)c.r;
-    if (c.r > 0) {
-        const int64_t rp = rank_pad(c.r);
+    if (c.r > 0 && c.ext_ready) {
         a.ext_w = c.ext_buf;
-        a.ext_ld = (int)rp;
-        if (c.fwd) {
-            if (dt == REELS_BF16)
-                launch_pdl(prep_ext_fwd_rows_kernel<__nv_bfloat16>, dim3((unsigned)cdiv(c.Nout, 32)), dim3(256), 0, st, 
-                    (const __nv_bfloat16 *)c.lora, c.scales, c.ext_scale, ext_divide ? 1 : 0, (int)c.r, (int)rp,
-                    (int)c.Nout, (__nv_bfloat16 *)c.ext_buf);
-            else
-                launch_pdl(prep_ext_fwd_rows_kernel<__half>, dim3((unsigned)cdiv(c.Nout, 32)), dim3(256), 0, st, 
-                    (const __half *)c.lora, c.scales, c.ext_scale, 0, (int)c.r, (int)rp, (int)c.Nout,
-                    (__half *)c.ext_buf);
-        } else {
-            launch_pdl(prep_ext_dx_kernel, dim3(launch_grid(c.Nout * rp / 8)), dim3(256), 0, st, 
-                (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
-        }
-        REELS_LAUNCHED();
+        a.ext_ld = (int)ts_rank_pad(c.r);
+    } else if (c.r > 0) {
+        a.ext_w = c.ext_buf;
+        a.ext_ld = (int)ts_rank_pad(c.r);
+        const int64_t rp = ts_rank_pad(c.r);
+        rc = c.fwd ? prep_lora(dt, 0, c.lora, c.scales, c.ext_scale, ext_divide, c.r, rp, c.Nout, c.ext_buf, nullptr,
+                               0, nullptr, st)
+                   : prep_lora(dt, 1, nullptr, c.scales, 1.0f, false, c.r, rp, c.Nout, c.ext_buf, c.lora, 0, nullptr,
+                               st);
+        if (rc) return rc;
     }
     a.bias = c.bias;
     a.out = c.out;
@@ -942,10 +957,11 @@ int run_q8(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const 
                     (const __half *)c.lora, c.scales, c.ext_scale, 0, c.r, rp, c.Nout, (__half *)c.ext_buf);
         } else {
             a.ext_ld = (int)rp;
-            launch_pdl(prep_ext_dx_kernel, dim3(launch_grid(c.Nout * rp / 8)), dim3(256), 0, st, 
-                (const uint16_t *)c.lora, (int)c.Nout, (int)c.r, (int)rp, (uint16_t *)c.ext_buf);
+            int rc2 = prep_lora(dt, 1, nullptr, c.scales, 1.0f, false, c.r, rp, c.Nout, c.ext_buf, c.lora, 0, nullptr,
+                                st);
+            if (rc2) return rc2;
         }
-        REELS_LAUNCHED();
+        if (c.fwd) REELS_LAUNCHED();
     }
     a.bias = c.bias;
     a.out = c.out;
@@ -995,9 +1011,11 @@ int transpose_rank(const void *A, int64_t K, int64_t r, void *At, cudaStream_t s
 }
 
 int rank_down_tc(const void *x, const void *A, int64_t M, int64_t K, int64_t r, int dt, void *tbuf, void *at,
-                 const DeviceState &ds, char *ws, const Ws &wl, cudaStream_t st) {
-    int rc = transpose_rank(A, K, r, at, st);
-    if (rc) return rc;
+                 const DeviceState &ds, char *ws, const Ws &wl, cudaStream_t st, bool at_ready = false) {
+    if (!at_ready) {
+        int rc = transpose_rank(A, K, r, at, st);
+        if (rc) return rc;
+    }
     SkCall c{};
     c.act = x;
     c.act_inner = K;
@@ -1013,6 +1031,26 @@ int rank_down_tc(const void *x, const void *A, int64_t M, int64_t K, int64_t r, 
     c.out = tbuf;
     c.ldo = ld_tokens(M);
     return run_sk(c, dt, ds, ws, wl, st);
+}
+
+// One launch of prep_lora_kernel: the extension operand of a weight-in-TMEM
+// q8 GEMM (ext != nullptr) and/or A^T (at != nullptr).
+int prep_lora(int dt, int ext_kind, const void *B, const float *scales, float s, bool divide, int64_t r, int64_t rp,
+              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st) {
+    const int nb_ext = ext ? (ext_kind == 0 ? (int)cdiv(nrows, 32) : launch_grid(nrows * rp / 8)) : 0;
+    const int nb_at = at ? launch_grid(K * r) : 0;
+    if (nb_ext + nb_at == 0) return REELS_OK;
+    const dim3 grid((unsigned)(nb_ext + nb_at));
+    if (dt == REELS_BF16)
+        launch_pdl(prep_lora_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, ext_kind, (const __nv_bfloat16 *)B,
+                   scales, s, divide ? 1 : 0, (int)r, (int)rp, (int)nrows, (__nv_bfloat16 *)ext, nb_ext,
+                   (const uint16_t *)A, (int)K, (uint16_t *)at);
+    else
+        launch_pdl(prep_lora_kernel<__half>, grid, dim3(256), 0, st, ext_kind, (const __half *)B, scales, s,
+                   divide ? 1 : 0, (int)r, (int)rp, (int)nrows, (__half *)ext, nb_ext, (const uint16_t *)A, (int)K,
+                   (uint16_t *)at);
+    REELS_LAUNCHED();
+    return REELS_OK;
 }
 
 }  // namespace
@@ -1243,8 +1281,17 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
     }
 
     if (tc_eligible(K, N, dt, {x, q, y, B, saved})) {
+        // With the weight-in-TMEM plan, one launch prepares both LoRA
+        // operands (A^T for the rank-down GEMM, the scaled B for the q8 GEMM).
+        const int epi = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH : ACT_NONE;
+        const bool ts_prep = r > 0 && plan_q8(M, N, K, ds->sms, aligned16(scales), epi).ts > 0;
+        if (ts_prep) {
+            rc = prep_lora(dt, 0, B, scales, s, dt == REELS_BF16, r, ts_rank_pad(r), N, ws + wl.ext, A, K, ws + wl.at,
+                           st);
+            if (rc) return rc;
+        }
         if (r > 0) {
-            rc = rank_down_tc(ax, A, M, K, r, dt, tbuf, ws + wl.at, *ds, ws, wl, st);
+            rc = rank_down_tc(ax, A, M, K, r, dt, tbuf, ws + wl.at, *ds, ws, wl, st, ts_prep);
             if (rc) return rc;
         }
         Q8Call c{};
@@ -1265,8 +1312,9 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
         c.ext_buf = ws + wl.ext;
         c.bias = bias;
         c.out = y;
-        c.epi_act = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH : ACT_NONE;
+        c.epi_act = epi;
         c.pre = act == REELS_ACT_NONE ? nullptr : pre;
+        c.ext_ready = ts_prep;
         rc = run_q8(c, dt, *ds, ws, wl, st);
         if (rc) return rc;
         return ok(REELS_PATH_TENSORCORE);
@@ -1388,9 +1436,18 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
     };
 
     if (tc_eligible(K, N, dt, {x, dy, q, dx, B, saved})) {
+        // With the weight-in-TMEM plan for dX, one launch prepares its LoRA
+        // operand (A, zero-padded) and, when A*x is recomputed, A^T.
+        const int epi = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH_GRAD : ACT_NONE;
+        const bool ts_prep = r > 0 && dx && !drop && plan_q8(M, K, N, ds->sms, aligned16(scales), epi).ts > 0;
+        if (ts_prep) {
+            rc = prep_lora(dt, 1, nullptr, scales, 1.0f, false, r, ts_rank_pad(r), K, ws + wl.ext, A, K,
+                           saved ? nullptr : ws + wl.at, st);
+            if (rc) return rc;
+        }
         if (r > 0) {
             if (!saved) {
-                rc = rank_down_tc(ax, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st);
+                rc = rank_down_tc(ax, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st, ts_prep);
                 if (rc) return rc;
             }
             // g' = s * (B' * dy), stored [r][ldm]
@@ -1430,8 +1487,9 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             c.ext_buf = ws + wl.ext;
             c.bias = nullptr;
             c.out = dx;
-            c.epi_act = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH_GRAD : ACT_NONE;
+            c.epi_act = epi;
             c.pre = act == REELS_ACT_NONE ? nullptr : const_cast<void *>(pre_x);
+            c.ext_ready = ts_prep;
             rc = run_q8(c, dt, *ds, ws, wl, st);
             if (rc) return rc;
             if (drop) {

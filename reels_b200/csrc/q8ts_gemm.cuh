@@ -106,7 +106,7 @@ struct TsArgs {
     int wscale_len;
     const float *wscale;
     int r;             // LoRA rank (0: none)
-    int ext_ld;        // row pitch (elements) of ext_w, which is [Nout][rp]
+    int ext_ld;        // row pitch (elements) of ext_w, which is [Nout][rp], rp = r rounded up to 32
     const void *ext_w;
     int epi_partial;
     const float *col_scale;  // per output column, applied in the epilogue
@@ -598,8 +598,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     // 16-bit pairs already in TMEM column order.
                     const int e = it - c.n_main;
                     const uint16_t *src = reinterpret_cast<const uint16_t *>(args.ext_w);
+                    // 32 ranks per h; the MMAs read ceil(ranks / 16) K-steps of 8 columns
+                    const int nh = min(2 * KB2, (min(G::SK, args.r - G::SK * e) + 31) / 32);
 #pragma unroll
                     for (int h = 0; h < 2 * KB2; ++h)
+                        if (h < nh)
 #pragma unroll
                         for (int half = 0; half < 2; ++half) {
                             uint32_t v[8];
