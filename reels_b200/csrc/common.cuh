@@ -97,8 +97,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
 #ifndef REELS_SUSPEND_HINT_NS
 #define REELS_SUSPEND_HINT_NS 1000000u
 #endif
+// REELS_WAIT_FORM selects how a pipeline wait blocks: 0 try_wait with the
+// suspend hint above, 1 try_wait with the system's own time limit.
+#ifndef REELS_WAIT_FORM
+#define REELS_WAIT_FORM 0
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
+#if REELS_WAIT_FORM == 1
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+#else
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
@@ -106,6 +120,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
         : "memory");
+#endif
     return ok != 0;
 }
 
@@ -134,10 +149,17 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned *err, unsigned code) {
     if (mbar_test_wait(bar, parity)) return true;
+#if REELS_WAIT_FORM == 2
+    // spin on the non-blocking probe (no suspension)
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_test_wait(bar, parity)) return true;
+#else
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
+#endif
         if (*abort) return false;
         if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
             *abort = 1;

@@ -708,31 +708,6 @@ cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
     return pr.second;
 }
 
-// L2 prefetch distances of the weight-in-TMEM kernel.  REELS_TS_PF="w,x"
-// sets both for measurements.
-void ts_prefetch(const Q8Plan &p, int64_t M, int &pf_w, int &pf_x) {
-    static const int forced[2] = {-1, -1};
-    static const bool have = [] {
-        const char *e = getenv("REELS_TS_PF");
-        int w = -1, x = -1;
-        if (e && sscanf(e, "%d,%d", &w, &x) == 2 && w >= 0 && x >= 0) {
-            const_cast<int *>(forced)[0] = w;
-            const_cast<int *>(forced)[1] = x;
-            return true;
-        }
-        return false;
-    }();
-    if (have) {
-        pf_w = forced[0];
-        pf_x = forced[1];
-        return;
-    }
-    pf_w = 0;
-    pf_x = 0;
-    (void)p;
-    (void)M;
-}
-
 int prep_lora(int dt, int ext_kind, const void *B, const float *scales, float s, bool divide, int64_t r, int64_t rp,
               int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st);
 
@@ -821,7 +796,6 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     a.err = ds.status;
     a.epi_act = c.epi_act;
     a.pre = c.pre;
-    ts_prefetch(p, c.M, a.pf_w, a.pf_x);
     tp = tx;
     if (!a.epi_partial) {
         // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.
@@ -1922,6 +1896,19 @@ int reels_q8_weight_transpose_mul(const void *dy, const int8_t *q, const float *
 }
 
 }  // extern "C"
+
+#ifdef REELS_TS_TRACE
+// Debug builds only: copy out and clear the weight-in-TMEM kernel's per-role
+// cycle counters (q8ts_gemm.cuh, g_ts_trace).
+extern "C" int reels_ts_trace_read(unsigned long long *dst, size_t n) {
+    static unsigned long long zero[256 * (TS_THREADS / 32) * 4];
+    n = std::min(n, sizeof(zero) / 8);
+    REELS_CUDA(cudaDeviceSynchronize());
+    if (dst) REELS_CUDA(cudaMemcpyFromSymbol(dst, g_ts_trace, n * 8));
+    REELS_CUDA(cudaMemcpyToSymbol(g_ts_trace, zero, sizeof(zero)));
+    return REELS_OK;
+}
+#endif
 
 // =====================================================================
 // Forward with library-owned scratch, for callers that cannot allocate

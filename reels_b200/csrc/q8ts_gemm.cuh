@@ -42,6 +42,26 @@ constexpr int TS_GW = TS_NDW / TS_NG;  // warps per group
 constexpr int TS_NEW = 8;  // epilogue warps
 constexpr int TS_THREADS = 32 * (3 + TS_NDW + TS_NEW);
 
+// Debug builds only (-DREELS_TS_TRACE, never the shipped library): per CTA and
+// warp, clock64 cycles spent in each wait and in the work between them,
+// summed into g_ts_trace[cta][warp][4] (CTAs < 256).
+#ifdef REELS_TS_TRACE
+__device__ unsigned long long g_ts_trace[256 * (TS_THREADS / 32) * 4];
+#define TSW(k, expr)                                   \
+    ([&]() {                                           \
+        const long long t0_ = clock64();               \
+        const bool r_ = (expr);                        \
+        tr_[k] += (unsigned long long)(clock64() - t0_); \
+        return r_;                                     \
+    }())
+#define TS_MARK(v) const long long v = clock64()
+#define TS_ADD(k, v) tr_[k] += (unsigned long long)(clock64() - (v))
+#else
+#define TSW(k, expr) (expr)
+#define TS_MARK(v)
+#define TS_ADD(k, v)
+#endif
+
 // A pipeline stage covers SK = 64*KB2 reduction elements: KB2 = 1 for the
 // 256- and 192-token tiles, 2 for 128-token tiles (the MMA warp's
 // per-stage synchronisation is then spread over twice the weight bytes,
@@ -117,11 +137,6 @@ struct TsArgs {
     void *pre;         // the rounded pre-activation [M][Nout]: written (gelu), read (gradient); nullable for gelu
     float *partial;    // [splits][M][Nout]
     unsigned *err;
-    // L2 prefetch distances, in pipeline stages, of the weight and activation
-    // tiles (0: none).  The weight stream is latency-bound when few tokens
-    // share a weight tile: a prefetch keeps stages in flight beyond the
-    // shared-memory ring at no shared-memory cost.
-    int pf_w, pf_x;
 };
 
 __device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
@@ -396,31 +411,30 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     const uint32_t tmem = *tmem_slot;
     griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
+#ifdef REELS_TS_TRACE
+    unsigned long long tr_[4] = {0, 0, 0, 0};
+    const long long tr_start = clock64();
+#endif
 
     // Producer and MMA warps run converged; one lane issues the TMA copies,
     // MMAs and commits.
     if (warp == 0) {
         // ------------------------------------------------ activation producer
-        uint32_t gx = 0;
-        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT, G::SK>(args, t);
-            for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
-                const int s = gx % G::SX;
-                if (lane == 0 && args.pf_x > 0) {
-                    // L2 prefetch of activation stages ahead of the ring
-                    for (int j = (it == 0 ? 1 : it + args.pf_x); j <= it + args.pf_x && j < c.n_main; ++j)
-#pragma unroll
-                        for (int a = 0; a < KB2; ++a) tma_prefetch_l2_2d(&tmX, (c.kb0 + j) * G::SK + 64 * a, c.m0);
-                }
-                if (gx >= (uint32_t)G::SX) {
-                    const uint32_t j = gx - G::SX;  // the block that last used this X slot
-                    if (!wait_bar_all(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
-                                      DEVERR_TIMEOUT_AB_EMPTY)) {
-                        aborted_here = true;
-                        break;
+        // One lane runs the loop: no warp-wide votes or syncs per stage.
+        if (lane == 0) {
+            uint32_t gx = 0;
+            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+                const TsTile c = ts_tile<BT, G::SK>(args, t);
+                for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
+                    const int s = gx % G::SX;
+                    if (gx >= (uint32_t)G::SX) {
+                        const uint32_t j = gx - G::SX;  // the block that last used this X slot
+                        if (!TSW(0, wait_bar(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
+                                             DEVERR_TIMEOUT_AB_EMPTY))) {
+                            aborted_here = true;
+                            break;
+                        }
                     }
-                }
-                if (lane == 0) {
                     uint8_t *dst = smem + G::X_OFF + s * G::X_BYTES;
                     uint64_t *full = &kb_full[gx % G::NA];
                     if (it < c.n_main) {
@@ -442,31 +456,23 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                                             G::SK * e + 64 * a, full);
                     }
                 }
-                __syncwarp();
             }
         }
+        __syncwarp();
     } else if (warp == 2) {
         // ------------------------------------------------ int8 weight (+ scale) producer
-        uint32_t gw = 0;
-        const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
-        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT, G::SK>(args, t);
-            for (int it = 0; it < c.n_main; ++it, ++gw) {
-                const int s = gw % G::S8;
-                if (lane == 0 && args.pf_w > 0) {
-                    // L2 prefetch of weight stages ahead of the ring (the first
-                    // call of a tile covers stages 1 .. pf_w)
-                    for (int j = (it == 0 ? 1 : it + args.pf_w); j <= it + args.pf_w && j < c.n_main; ++j) {
-                        const int kb = c.kb0 + j;
-                        if (args.w_rows_red == 0) tma_prefetch_l2_2d(&tmW, kb * G::SK, c.n0);
-                        else tma_prefetch_l2_2d(&tmW, c.n0, kb * G::SK);
+        if (lane == 0) {
+            uint32_t gw = 0;
+            const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
+            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
+                const TsTile c = ts_tile<BT, G::SK>(args, t);
+                for (int it = 0; it < c.n_main; ++it, ++gw) {
+                    const int s = gw % G::S8;
+                    if (!TSW(0, wait_bar(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err,
+                                         DEVERR_TIMEOUT_W_EMPTY))) {
+                        aborted_here = true;
+                        break;
                     }
-                }
-                if (!wait_bar_all(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_W_EMPTY)) {
-                    aborted_here = true;
-                    break;
-                }
-                if (lane == 0) {
                     uint8_t *dst = smem + G::W_OFF + s * G::W_BYTES;
                     mbar_arrive_expect_tx(&w_full[s], bytes);
                     const int kb = c.kb0 + it;
@@ -475,41 +481,44 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     if (args.scale_mode == 2)
                         tma_load_2d(smem + G::SC_OFF + s * G::SC_BYTES, &tmS, kb * G::SK, 0, &w_full[s]);
                 }
-                __syncwarp();
             }
         }
+        __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        // Lane 0 issues; the wait for block ga + 1 comes right after block
-        // ga's MMAs so its latency overlaps the queued tensor-core work.
-        const int ab = (DT == DT_BF16) ? 1 : 0;
-        const uint32_t id_main = idesc_f16(ab, 0, 0, 128, BT);
-        const uint32_t id_ext = idesc_f16(ab, 0, 1, 128, BT);
-        // Descriptors of X stage 0; a stage or K offset adds (bytes >> 4) to the address field.
-        const uint64_t dmain0 = sdesc_sw128(sbase + G::X_OFF, 16, 1024);
-        const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
-        uint32_t ga = 0, local = 0;
-        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
-            const TsTile c = ts_tile<BT, G::SK>(args, t);
-            const int acc = local % G::NACC;
-            if (!wait_bar_all(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
-                aborted_here = true;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t d_tm = tmem + G::acc_col(acc);
-            const int n_iter = c.n_main + c.n_ext;
-            if (n_iter > 0 &&
-                !wait_bar_all(&kb_full[ga % G::NA], (ga / G::NA) & 1, abort, args.err, DEVERR_TIMEOUT_AB_FULL)) {
-                aborted_here = true;
-                break;
-            }
-            for (int it = 0; it < n_iter; ++it, ++ga) {
+        // One lane runs the loop.  Each stage's MMAs are queued, then its
+        // commit (releasing the stage once they complete), then the wait for
+        // the next stage: the tensor pipe keeps the queued work while the
+        // thread waits, and no warp-wide vote or sync sits between stages.
+        if (lane == 0) {
+            const int ab = (DT == DT_BF16) ? 1 : 0;
+            const uint32_t id_main = idesc_f16(ab, 0, 0, 128, BT);
+            const uint32_t id_ext = idesc_f16(ab, 0, 1, 128, BT);
+            // Descriptors of X stage 0; a stage or K offset adds (bytes >> 4) to the address field.
+            const uint64_t dmain0 = sdesc_sw128(sbase + G::X_OFF, 16, 1024);
+            const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
+            uint32_t ga = 0, local = 0;
+            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
+                const TsTile c = ts_tile<BT, G::SK>(args, t);
+                const int acc = local % G::NACC;
+                if (!TSW(0, wait_bar(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err,
+                                     DEVERR_TIMEOUT_ACC))) {
+                    aborted_here = true;
+                    break;
+                }
                 tc_fence_after();
-                const int sx = ga % G::SX, sa = ga % G::NA;
-                const uint32_t a_tm = tmem + G::a_col(sa);
-                const uint64_t xoff = (uint64_t)((sx * G::X_BYTES) >> 4);
-                if (lane == 0) {
+                const uint32_t d_tm = tmem + G::acc_col(acc);
+                const int n_iter = c.n_main + c.n_ext;
+                for (int it = 0; it < n_iter; ++it, ++ga) {
+                    const int sx = ga % G::SX, sa = ga % G::NA;
+                    if (!TSW(1, wait_bar(&kb_full[sa], (ga / G::NA) & 1, abort, args.err, DEVERR_TIMEOUT_AB_FULL))) {
+                        aborted_here = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    TS_MARK(tr_issue);
+                    const uint32_t a_tm = tmem + G::a_col(sa);
+                    const uint64_t xoff = (uint64_t)((sx * G::X_BYTES) >> 4);
                     // K step kk reads atom kk/4 of the stage (BT*128 bytes each):
                     // 32 bytes per step inside a K-major atom, 2048 inside a rank atom.
                     if (it < c.n_main) {
@@ -526,24 +535,14 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                                        dext0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 2048) >> 4),
                                        id_ext, (it > 0 || kk > 0) ? 1u : 0u);
                     }
+                    mma_commit(&kb_empty[sa]);
+                    TS_ADD(2, tr_issue);
                 }
-                __syncwarp();
-                bool ok = true;
-                if (it + 1 < n_iter)
-                    ok = wait_bar_all(&kb_full[(ga + 1) % G::NA], ((ga + 1) / G::NA) & 1, abort, args.err,
-                                      DEVERR_TIMEOUT_AB_FULL);
-                if (lane == 0) mma_commit(&kb_empty[sa]);
-                __syncwarp();
-                if (!ok) {
-                    aborted_here = true;
-                    break;
-                }
+                if (aborted_here) break;
+                mma_commit(&acc_full[acc]);
             }
-            if (aborted_here) break;
-            if (lane == 0) mma_commit(&acc_full[acc]);
-            __syncwarp();
+            mma_commit(mma_done);
         }
-        if (lane == 0) mma_commit(mma_done);
         __syncwarp();
     } else if (warp < 3 + TS_NDW) {
         // ------------------------------------------------ dequant warps
@@ -569,16 +568,17 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 if ((int)(ga % TS_NG) != g) continue;
                 const int sw = gw_this % G::S8;
                 if (main_blk &&
-                    !wait_bar_all(&w_full[sw], (gw_this / G::S8) & 1, abort, args.err, DEVERR_TIMEOUT_W_FULL)) {
+                    !TSW(0, wait_bar_all(&w_full[sw], (gw_this / G::S8) & 1, abort, args.err, DEVERR_TIMEOUT_W_FULL))) {
                     aborted_here = true;
                     break;
                 }
                 const int sa = ga % G::NA;
-                if (!wait_bar_all(&kb_empty[sa], ((ga / G::NA) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY)) {
+                if (!TSW(1, wait_bar_all(&kb_empty[sa], ((ga / G::NA) & 1) ^ 1, abort, args.err, DEVERR_TIMEOUT_AB_EMPTY))) {
                     aborted_here = true;
                     break;
                 }
                 tc_fence_after();
+                TS_MARK(tr_work);
                 const uint32_t a_tm = tmem + G::a_col(sa);
                 if (main_blk) {
                     const uint32_t w_base = sbase + G::W_OFF + sw * G::W_BYTES;
@@ -625,6 +625,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&kb_full[sa]);
+                TS_ADD(2, tr_work);
             }
         }
     } else {
@@ -673,7 +674,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                             tma_prefetch_l2_2d(&tmP, c.n0 + 32 * q, c.m0 + set * (BT / 2) + 32 * ch);
                 load_pre(c, set * (BT / 2));
             }
-            if (!wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC)) {
+            if (!TSW(0, wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC))) {
                 aborted_here = true;
                 break;
             }
@@ -813,6 +814,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         __syncwarp();
     }
 
+#ifdef REELS_TS_TRACE
+    tr_[3] = (unsigned long long)(clock64() - tr_start);
+    if (lane == 0 && blockIdx.x < 256)
+        for (int k = 0; k < 4; ++k) atomicAdd(&g_ts_trace[((size_t)blockIdx.x * (TS_THREADS / 32) + warp) * 4 + k], tr_[k]);
+#endif
     if (aborted_here && (warp == 0 || warp == 2)) {
         for (int i = 0; i < 64; ++i) __nanosleep(2000);
     }
