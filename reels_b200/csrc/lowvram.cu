@@ -319,15 +319,15 @@ struct Q8Plan {
 };
 
 // Kernel, tile shape and reduction split from a time model fitted to B200
-// measurements (bf16; microseconds per pipeline stage of one tile, plus a
-// per-tile epilogue cost the kernel cannot overlap):
+// measurements (microseconds per pipeline stage of one tile, plus a per-tile
+// epilogue cost the kernel cannot overlap; least squares over whole-tile
+// rounds of the Wan 1.3B/14B linears at 512..32760 tokens):
 //   weight-in-TMEM kernel (q8ts_gemm.cuh), 128 output columns x bt tokens,
-//   stages of 64 reduction elements: bt 256: 0.49 + 1.1 per tile (single
-//       accumulator), bt 192: 0.44 + 0.4, bt 128: 0.48 + 0.4;
-//   stages of 128: bt 128: 0.60 + 0.4, bt 256: 1.07 + 1.1, bt 192: 1.02 + 0.4.
-//   The MMA warp's per-stage synchronisation costs about the same whatever
-//   the stage width, so 128-wide stages stream the weight twice as fast when
-//   there are few tokens; with many tokens the 256-token tiles win.
+//   stages of 64 reduction elements: bt 256: 0.49 + 0.49 per tile (single
+//       accumulator), bt 192: 0.44 + 0.28, bt 128: 0.42 + 0.36;
+//   stages of 128: bt 256: 0.91 + 0.70, bt 192: 0.77 + 0.28, bt 128: 0.62 + 0.11.
+//   The MMA warp's per-stage waits and commit cost about the same whatever
+//   the stage width, so 128-wide stages move more weight per round trip.
 //   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
@@ -353,8 +353,8 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
         double per_kb, epi;  // per_kb: per pipeline stage (64 * kb2 reduction elements)
     };
     const Cand cands[] = {
-        {0, 0, 256, 1, 0.49, 1.1}, {0, 0, 192, 1, 0.44, 0.4}, {0, 0, 128, 1, 0.48, 0.4}, {0, 0, 128, 2, 0.60, 0.4},
-        {0, 0, 256, 2, 1.07, 1.1}, {0, 0, 192, 2, 1.02, 0.4},
+        {0, 0, 256, 1, 0.49, 0.49}, {0, 0, 192, 1, 0.44, 0.28}, {0, 0, 128, 1, 0.42, 0.36}, {0, 0, 128, 2, 0.62, 0.11},
+        {0, 0, 256, 2, 0.91, 0.70}, {0, 0, 192, 2, 0.77, 0.28},
         {2, 256, 0, 1, 1.18, 4.0}, {2, 128, 0, 1, 0.85, 1.5}, {1, 256, 0, 1, 1.0, 1.5}, {1, 128, 0, 1, 0.75, 1.5},
     };
     double best = 1e300;
