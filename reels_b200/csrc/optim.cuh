@@ -60,6 +60,7 @@ __device__ __forceinline__ bool opt_header_ok(const OptHeader *h, unsigned *err)
 // Per-block fp64 partial sums of (gs * g)^2.
 __global__ void __launch_bounds__(OPT_THREADS) grad_sumsq_kernel(const char *ws, float gs, double *partials,
                                                                    unsigned *err) {
+    griddep_wait();
     const OptHeader *h = reinterpret_cast<const OptHeader *>(ws);
     __shared__ double red[OPT_THREADS / 32];
     double acc = 0.0;
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(OPT_THREADS) grad_sumsq_kernel(const char *ws,
 // One block: the partials in a fixed order, rounded to fp32.
 __global__ void __launch_bounds__(OPT_MAX_BLOCKS) grad_sumsq_final_kernel(const double *partials, int n,
                                                                            float *sumsq) {
+    griddep_wait();
     __shared__ double red[OPT_MAX_BLOCKS];
     red[threadIdx.x] = threadIdx.x < n ? partials[threadIdx.x] : 0.0;
     __syncthreads();
@@ -147,6 +149,7 @@ __device__ __forceinline__ void store_param(void *p, int64_t i, int dt, float w)
 }
 
 __global__ void __launch_bounds__(OPT_THREADS) adamw_kernel(const char *ws, AdamArgs a, unsigned *err) {
+    griddep_wait();
     const OptHeader *h = reinterpret_cast<const OptHeader *>(ws);
     if (!opt_header_ok(h, err)) return;
     // Clip (wan_runner.jl:215-221): gradient_norm = Float32(sqrt(norm_squared)).
