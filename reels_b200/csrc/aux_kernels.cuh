@@ -184,6 +184,52 @@ __global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, in
     }
 }
 
+// Sum skinny partials [splits][rows][npad] and apply epi 0 (transposed
+// store, act dtype) or epi 1 (fp32 accumulate into out[row*rs + j*cs]).
+// The outputs are few and the splits many, so the sum is latency-bound: four
+// threads share an output, thread t of the four adds the splits s = t mod 4
+// in order with eight loads in flight, and the four partial sums are
+// combined in a fixed order (deterministic from run to run).
+__global__ void sk_reduce_kernel(const float *partial, int splits, int64_t rows, int npad, int ncols,
+                                 int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
+                                 int64_t cs) {
+    griddep_wait();
+    const int64_t total = rows * (int64_t)ncols;
+    const int lane = threadIdx.x & 31, sl = lane & 3;
+    const int64_t stride = rows * (int64_t)npad;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w * 8 < total; w += nw) {
+        const int64_t o = w * 8 + (lane >> 2);  // consecutive outputs: consecutive columns of a row
+        float acc = 0.0f;
+        int64_t row = 0, j = 0;
+        if (o < total) {
+            row = o / ncols;
+            j = o % ncols;
+            const float *p = partial + row * npad + j;
+            int s = sl;
+            for (; s + 28 < splits; s += 32) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (int64_t)(s + 4 * u) * stride);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc += v[u];
+            }
+            for (; s < splits; s += 4) acc += __ldcg(p + (int64_t)s * stride);
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (sl == 0 && o < total) {
+            if (epi == 0) {
+                store_act(out, j * ldo + row, dt, alpha * acc);
+            } else {
+                float *o32 = reinterpret_cast<float *>(out);
+                const int64_t idx = row * rs + j * cs;
+                o32[idx] = (accumulate ? o32[idx] : 0.0f) + alpha * acc;
+            }
+        }
+    }
+}
+
 // The fused activation as a separate pass, for the kernels without it in
 // their epilogue: gelu reads the GEMM output from `pre` and writes `out`;
 // the gradient rescales `out` in place by gelu'(pre).

@@ -384,18 +384,7 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask
 // tests), a failure that waiting alone does not show and whose cause is not
 // established.  Data written by an earlier kernel is read through L2
 // (__ldcg), not through the SM's L1 or the read-only path.
-#ifndef REELS_PDL_TRIGGER
-#define REELS_PDL_TRIGGER 0
-#endif
-__device__ __forceinline__ void griddep_wait() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-#if REELS_PDL_TRIGGER
-    // Let the next kernel in the stream be scheduled once every CTA of this
-    // one has passed its own wait: its prologue then overlaps this kernel,
-    // and its griddep_wait() still holds it until this grid has completed.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-#endif
-}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // 32-byte global stores (sm_100): one instruction per 16 bf16/fp16 or 8 fp32.
 __device__ __forceinline__ void st_global_v8(void *p, uint4 a, uint4 b) {

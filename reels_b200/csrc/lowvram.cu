@@ -408,11 +408,7 @@ Split plan_sk(int64_t rows, int64_t red, int sms, int64_t r) {
 
 // Workspace layout shared by the forward and backward passes.
 struct Ws {
-    size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, zbuf = 0, part = 0, cnt = 0, total = 0;
-    // counters of the skinny GEMMs' in-kernel split reductions, one region
-    // per launch of a pass (A*x, B'*dy, dA, dB), 4 per 128-row tile
-    size_t cnt_off[4] = {0, 0, 0, 0};
-    size_t cnt_bytes = 0;
+    size_t at = 0, tbuf = 0, gbuf = 0, ext = 0, zbuf = 0, part = 0, total = 0;
 };
 
 // Rank padding of the prepared LoRA operands: a multiple of the widest
@@ -469,17 +465,6 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags,
     }
     w.part = off;
     off += align256(part);
-    w.cnt = off;
-    if (r > 0 && M > 0) {
-        const int64_t rows[4] = {M, M, K, N};
-        size_t c = 0;
-        for (int i = 0; i < 4; ++i) {
-            w.cnt_off[i] = c;
-            c += (size_t)cdiv(rows[i], 128) * 4 * sizeof(unsigned);
-        }
-        w.cnt_bytes = c;
-        off += align256(c);
-    }
     w.total = off;
     return w;
 }
@@ -513,7 +498,6 @@ struct SkCall {
     int accumulate;
     void *out;
     int64_t ldo, rs, cs;
-    int cnt_slot;        // its split-reduction counters: 0 A*x, 1 B'*dy, 2 dA, 3 dB
 };
 
 int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
@@ -547,24 +531,17 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.err = ds.status;
     a.epi = s.splits > 1 ? 2 : c.epi_final;
     a.splits = s.splits;
-    // The split reduction runs inside the kernel (the last split of each
-    // tile quarter sums them), on counters the pass zeroed at its start.
-    a.cnt = s.splits > 1 ? reinterpret_cast<unsigned *>(ws_base + wl.cnt + wl.cnt_off[c.cnt_slot]) : nullptr;
-    a.epi_final = c.epi_final;
-    a.dt_out = dt;
     // persistent CTAs, one per SM at most (200 KB of ring each)
     const dim3 grid((unsigned)std::min<int64_t>(cdiv(c.rows, 128) * s.splits, ds.sms));
     if (dt == REELS_BF16) launch_pdl(sk_gemm_kernel<DT_BF16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     else launch_pdl(sk_gemm_kernel<DT_F16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     REELS_LAUNCHED();
-    return REELS_OK;
-}
-
-// Zero the split-reduction counters of a pass (when no operand-prep launch
-// does it): the kernels leave them at zero, but a pass that gave up midway
-// (a bounded wait that timed out) would not.
-int zero_counters(char *ws, const Ws &wl, cudaStream_t st) {
-    if (wl.cnt_bytes) REELS_CUDA(cudaMemsetAsync(ws + wl.cnt, 0, wl.cnt_bytes, st));
+    if (s.splits > 1) {
+        launch_pdl(sk_reduce_kernel, dim3(launch_grid(c.rows * c.r * 4)), dim3(256), 0, st, a.partial, s.splits, c.rows, np, (int)c.r,
+                                                                    c.epi_final, c.alpha, c.accumulate, dt, c.out,
+                                                                    c.ldo, c.rs, c.cs);
+        REELS_LAUNCHED();
+    }
     return REELS_OK;
 }
 
@@ -599,15 +576,12 @@ __global__ void prep_ext_fwd_kernel(const T *B, const float *scales, float s, in
 //   ext_kind 1 (dX):      E[k][j] = A[k][j], [nrows = K][rp], eight ranks per
 //     thread and one 16-byte store;
 // columns j >= r are zero.  The other blocks write At = A^T [r][K], the
-// rank-down GEMM's operand (none when gridDim.x == nb_ext).  The first ncnt
-// words of cnt (the pass's split-reduction counters) are zeroed.
+// rank-down GEMM's operand (none when gridDim.x == nb_ext).
 template <typename T>
 __global__ void prep_lora_kernel(int ext_kind, const T *B, const float *scales, float s, int divide, int r, int rp,
                                  int nrows, T *__restrict__ ext, int nb_ext, const uint16_t *A, int K,
-                                 uint16_t *__restrict__ At, unsigned *cnt, int ncnt) {
+                                 uint16_t *__restrict__ At) {
     griddep_wait();
-    // the pass's split-reduction counters start at zero
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0u;
     __shared__ float tile[128][33];
     if ((int)blockIdx.x < nb_ext) {
         if (ext_kind == 0) {
@@ -735,8 +709,7 @@ cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
 }
 
 int prep_lora(int dt, int ext_kind, const void *B, const float *scales, float s, bool divide, int64_t r, int64_t rp,
-              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st, void *cnt = nullptr,
-              size_t cnt_bytes = 0);
+              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st);
 
 // The weight-in-TMEM kernel (q8ts_gemm.cuh).
 int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st,
@@ -1037,24 +1010,19 @@ int rank_down_tc(const void *x, const void *A, int64_t M, int64_t K, int64_t r, 
 // One launch of prep_lora_kernel: the extension operand of a weight-in-TMEM
 // q8 GEMM (ext != nullptr) and/or A^T (at != nullptr).
 int prep_lora(int dt, int ext_kind, const void *B, const float *scales, float s, bool divide, int64_t r, int64_t rp,
-              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st, void *cnt,
-              size_t cnt_bytes) {
+              int64_t nrows, void *ext, const void *A, int64_t K, void *at, cudaStream_t st) {
     const int nb_ext = ext ? (ext_kind == 0 ? (int)cdiv(nrows, 32) : launch_grid(nrows * rp / 8)) : 0;
     const int nb_at = at ? launch_grid(K * r) : 0;
-    const int ncnt = (int)(cnt_bytes / sizeof(unsigned));
-    if (nb_ext + nb_at == 0) {
-        if (ncnt) REELS_CUDA(cudaMemsetAsync(cnt, 0, cnt_bytes, st));
-        return REELS_OK;
-    }
+    if (nb_ext + nb_at == 0) return REELS_OK;
     const dim3 grid((unsigned)(nb_ext + nb_at));
     if (dt == REELS_BF16)
         launch_pdl(prep_lora_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, ext_kind, (const __nv_bfloat16 *)B,
                    scales, s, divide ? 1 : 0, (int)r, (int)rp, (int)nrows, (__nv_bfloat16 *)ext, nb_ext,
-                   (const uint16_t *)A, (int)K, (uint16_t *)at, (unsigned *)cnt, ncnt);
+                   (const uint16_t *)A, (int)K, (uint16_t *)at);
     else
         launch_pdl(prep_lora_kernel<__half>, grid, dim3(256), 0, st, ext_kind, (const __half *)B, scales, s,
                    divide ? 1 : 0, (int)r, (int)rp, (int)nrows, (__half *)ext, nb_ext, (const uint16_t *)A, (int)K,
-                   (uint16_t *)at, (unsigned *)cnt, ncnt);
+                   (uint16_t *)at);
     REELS_LAUNCHED();
     return REELS_OK;
 }
@@ -1293,10 +1261,7 @@ static int q8lora_forward_impl(const void *x, const int8_t *q, const float *scal
         const bool ts_prep = r > 0 && plan_q8(M, N, K, ds->sms, aligned16(scales), epi).ts > 0;
         if (ts_prep) {
             rc = prep_lora(dt, 0, B, scales, s, dt == REELS_BF16, r, ts_rank_pad(r), N, ws + wl.ext, A, K, ws + wl.at,
-                           st, ws + wl.cnt, wl.cnt_bytes);
-            if (rc) return rc;
-        } else if (r > 0) {
-            rc = zero_counters(ws, wl, st);
+                           st);
             if (rc) return rc;
         }
         if (r > 0) {
@@ -1451,10 +1416,7 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
         const bool ts_prep = r > 0 && dx && !drop && plan_q8(M, K, N, ds->sms, aligned16(scales), epi).ts > 0;
         if (ts_prep) {
             rc = prep_lora(dt, 1, nullptr, scales, 1.0f, false, r, ts_rank_pad(r), K, ws + wl.ext, A, K,
-                           saved ? nullptr : ws + wl.at, st, ws + wl.cnt, wl.cnt_bytes);
-            if (rc) return rc;
-        } else if (r > 0) {
-            rc = zero_counters(ws, wl, st);
+                           saved ? nullptr : ws + wl.at, st);
             if (rc) return rc;
         }
         if (r > 0) {
@@ -1464,7 +1426,6 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             }
             // g' = s * (B' * dy), stored [r][ldm]
             SkCall g{};
-            g.cnt_slot = 1;
             g.act = dy;
             g.act_inner = N;
             g.act_outer = M;
@@ -1513,7 +1474,6 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
         if (r > 0) {
             // dA[k][j] = grad_scale * sum_m g'[j][m] z[m][k]  (z = x without dropout)
             SkCall da{};
-            da.cnt_slot = 2;
             da.act = ax;
             da.act_inner = K;
             da.act_outer = M;
@@ -1533,7 +1493,6 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             if (rc) return rc;
             // dB[j][n] = grad_scale * s * sum_m dy[m][n] t[j][m]
             SkCall db{};
-            db.cnt_slot = 3;
             db.act = dy;
             db.act_inner = N;
             db.act_outer = M;

@@ -58,13 +58,6 @@ struct SkArgs {
     long long rs, cs;  // epi 1: out[row*rs + j*cs]
     float *partial;    // epi 2: [splits][rows][npad]
     unsigned *err;
-    // Split reduction inside the kernel (cnt != nullptr, epi 2): per tile and
-    // 32-row quarter a counter, zero at launch; the epilogue warp that brings
-    // it to `splits` sums the quarter's partials in split order and applies
-    // epi_final (0 transposed store, 1 fp32 accumulate) itself.
-    unsigned *cnt;
-    int epi_final;
-    int dt_out;  // element type of out for epi_final 0
 };
 
 struct SkUnit {
@@ -77,50 +70,6 @@ __device__ __forceinline__ SkUnit sk_unit(const SkArgs &a, int tiles, int u) {
     w.kb0 = w.sp * a.kb_per_split;
     w.n_iter = max(0, min(a.kb_total, w.kb0 + a.kb_per_split) - w.kb0);
     return w;
-}
-
-// One row of the in-kernel split reduction: out[row][j] for j < ncols from
-// the partials of every split, summed in split order (four columns at a time,
-// four splits in flight).
-__device__ __forceinline__ void sk_reduce_rows(const SkArgs &a, int row) {
-    const long long stride = (long long)a.rows * a.npad;
-    const float *p = a.partial + (long long)row * a.npad;
-    for (int c = 0; c < a.ncols; c += 4) {
-        float4 acc = __ldcg(reinterpret_cast<const float4 *>(p + c));
-        int s = 1;
-        for (; s + 3 < a.splits; s += 4) {
-            float4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4 *>(p + (s + u) * stride + c));
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                acc.x += v[u].x;
-                acc.y += v[u].y;
-                acc.z += v[u].z;
-                acc.w += v[u].w;
-            }
-        }
-        for (; s < a.splits; ++s) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p + s * stride + c));
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
-        }
-        const float r4[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-            const int j = c + t;
-            if (j >= a.ncols) break;
-            if (a.epi_final == 0) {
-                store_act(a.out, (long long)j * a.ldo + row, a.dt_out, a.alpha * r4[t]);
-            } else {
-                float *o = reinterpret_cast<float *>(a.out);
-                const long long idx = (long long)row * a.rs + (long long)j * a.cs;
-                o[idx] = (a.accumulate ? o[idx] : 0.0f) + a.alpha * r4[t];
-            }
-        }
-    }
 }
 
 template <int DT>
@@ -291,21 +240,6 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
                             o[idx] = prev + args.alpha * __uint_as_float(v[t]);
                         }
                     }
-                }
-            }
-            if (args.epi == 2 && args.cnt) {
-                // This warp's partial rows are stored: count them in; the
-                // last of the splits reduces the quarter (no wait on anyone).
-                __threadfence();
-                __syncwarp();
-                unsigned *ctr = args.cnt + (size_t)(w.row0 / 128) * 4 + q;
-                unsigned old = 0;
-                if (lane == 0) old = atomicAdd(ctr, 1u);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == (unsigned)args.splits - 1) {
-                    __threadfence();
-                    if (lane == 0) *ctr = 0u;  // ready for the next launch on this workspace
-                    if (row < args.rows) sk_reduce_rows(args, row);
                 }
             }
         }
