@@ -250,6 +250,24 @@ __device__ __forceinline__ void i8x4_convert(uint32_t v, const float *s, uint32_
     }
 }
 
+// fp16 with a scale: Float16(q) * Float16(s) rounded to fp16, the
+// reference's own fp16 dequantisation (src/layers/quantization.jl:61-62):
+// the exact int8 -> fp16 conversion, then one packed fp16 multiply by the
+// scale pair (s01 = scales of elements 0, 1; s23 of elements 2, 3).
+__device__ __forceinline__ void i8x4_f16_scaled(uint32_t v, uint32_t s01, uint32_t s23, uint32_t &w0,
+                                                uint32_t &w1) {
+    const uint32_t a = v ^ 0x80808080u;
+    uint32_t q0 = bytes01_to_f16x2(a, 0x4140u), q1 = bytes01_to_f16x2(a, 0x4342u);
+    __half2 p0 = __hmul2(*reinterpret_cast<__half2 *>(&q0), *reinterpret_cast<const __half2 *>(&s01));
+    __half2 p1 = __hmul2(*reinterpret_cast<__half2 *>(&q1), *reinterpret_cast<const __half2 *>(&s23));
+    w0 = *reinterpret_cast<uint32_t *>(&p0);
+    w1 = *reinterpret_cast<uint32_t *>(&p1);
+}
+__device__ __forceinline__ uint32_t half2_bits(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
 // 64 reduction indices (sub-block h2 of the stage) into TMEM columns 32*h2 .. 32*h2 + 31.
 template <int DT, int ROWS_RED, int SMODE, int SK>
 __device__ __forceinline__ void ts_dequant_sub(uint32_t w_base, uint32_t sc_base, uint32_t a_tm, int q, int lane,
@@ -271,9 +289,16 @@ __device__ __forceinline__ void ts_dequant_sub(uint32_t w_base, uint32_t sc_base
         }
     }
     // raw[j][i]: lanes 32q + 8i + t/4, reduction 16j + 4(t%4) .. +3
+    // fp16 with a scale: the scales as fp16 pairs (per lane for SMODE 1)
+    uint32_t ls2[4];
+    if constexpr (DT == DT_F16 && SMODE == 1) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ls2[i] = half2_bits(lane_s[i], lane_s[i]);
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {  // reduction indices 32h .. 32h+31 = TMEM columns 16h .. 16h+15
         float rs[2][4];
+        uint32_t rh[2][2];
         if constexpr (SMODE == 2) {
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
@@ -283,6 +308,10 @@ __device__ __forceinline__ void ts_dequant_sub(uint32_t w_base, uint32_t sc_base
                 rs[jj][1] = s4.y;
                 rs[jj][2] = s4.z;
                 rs[jj][3] = s4.w;
+                if constexpr (DT == DT_F16) {
+                    rh[jj][0] = half2_bits(s4.x, s4.y);
+                    rh[jj][1] = half2_bits(s4.z, s4.w);
+                }
             }
         }
 #pragma unroll
@@ -293,15 +322,22 @@ __device__ __forceinline__ void ts_dequant_sub(uint32_t w_base, uint32_t sc_base
 #pragma unroll
                 for (int u = 0; u < 2; ++u) {
                     const int i = 2 * half + u;
-                    float sc[4];
-                    if constexpr (SMODE == 1) sc[0] = sc[1] = sc[2] = sc[3] = lane_s[i];
-                    if constexpr (SMODE == 2) {
-                        sc[0] = rs[jj][0];
-                        sc[1] = rs[jj][1];
-                        sc[2] = rs[jj][2];
-                        sc[3] = rs[jj][3];
+                    if constexpr (DT == DT_F16 && SMODE == 1) {
+                        i8x4_f16_scaled(raw[2 * h + jj][i], ls2[i], ls2[i], v[4 * jj + 2 * u], v[4 * jj + 2 * u + 1]);
+                    } else if constexpr (DT == DT_F16 && SMODE == 2) {
+                        i8x4_f16_scaled(raw[2 * h + jj][i], rh[jj][0], rh[jj][1], v[4 * jj + 2 * u],
+                                        v[4 * jj + 2 * u + 1]);
+                    } else {
+                        float sc[4];
+                        if constexpr (SMODE == 1) sc[0] = sc[1] = sc[2] = sc[3] = lane_s[i];
+                        if constexpr (SMODE == 2) {
+                            sc[0] = rs[jj][0];
+                            sc[1] = rs[jj][1];
+                            sc[2] = rs[jj][2];
+                            sc[3] = rs[jj][3];
+                        }
+                        i8x4_convert<DT, SMODE>(raw[2 * h + jj][i], sc, v[4 * jj + 2 * u], v[4 * jj + 2 * u + 1]);
                     }
-                    i8x4_convert<DT, SMODE>(raw[2 * h + jj][i], sc, v[4 * jj + 2 * u], v[4 * jj + 2 * u + 1]);
                 }
             tmem_st_16x256b_x2(a_tm + ((uint32_t)(32 * q + 16 * half) << 16) + 32u * h2 + 16u * h, v);
         }
