@@ -190,22 +190,33 @@ __global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, in
 // threads share an output, thread t of the four adds the splits s = t mod 4
 // in order with eight loads in flight, and the four partial sums are
 // combined in a fixed order (deterministic from run to run).
+// pcol selects the partials' layout and the order of the outputs, so that
+// both follow the output's contiguous dimension: pcol = 0, partials
+// [splits][rows][npad] and consecutive outputs are consecutive columns j of a
+// row (out[row*rs + j] with cs = 1); pcol = 1, partials [splits][npad][rows]
+// and consecutive outputs are consecutive rows (the transposed store
+// out[j*ldo + row], or out[row + j*cs] with rs = 1).
 __global__ void sk_reduce_kernel(const float *partial, int splits, int64_t rows, int npad, int ncols,
                                  int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
-                                 int64_t cs) {
+                                 int64_t cs, int pcol) {
     griddep_wait();
     const int64_t total = rows * (int64_t)ncols;
     const int lane = threadIdx.x & 31, sl = lane & 3;
     const int64_t stride = rows * (int64_t)npad;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w * 8 < total; w += nw) {
-        const int64_t o = w * 8 + (lane >> 2);  // consecutive outputs: consecutive columns of a row
+        const int64_t o = w * 8 + (lane >> 2);  // eight consecutive outputs per warp
         float acc = 0.0f;
         int64_t row = 0, j = 0;
         if (o < total) {
-            row = o / ncols;
-            j = o % ncols;
-            const float *p = partial + row * npad + j;
+            if (pcol) {
+                j = o / rows;
+                row = o % rows;
+            } else {
+                row = o / ncols;
+                j = o % ncols;
+            }
+            const float *p = pcol ? partial + j * rows + row : partial + row * npad + j;
             int s = sl;
             for (; s + 28 < splits; s += 32) {
                 float v[8];

@@ -531,6 +531,8 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     a.err = ds.status;
     a.epi = s.splits > 1 ? 2 : c.epi_final;
     a.splits = s.splits;
+    // split partials follow the output's contiguous dimension
+    a.pcol = (c.epi_final == 0 || c.rs == 1) ? 1 : 0;
     // persistent CTAs, one per SM at most (200 KB of ring each)
     const dim3 grid((unsigned)std::min<int64_t>(cdiv(c.rows, 128) * s.splits, ds.sms));
     if (dt == REELS_BF16) launch_pdl(sk_gemm_kernel<DT_BF16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
@@ -539,7 +541,7 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     if (s.splits > 1) {
         launch_pdl(sk_reduce_kernel, dim3(launch_grid(c.rows * c.r * 4)), dim3(256), 0, st, a.partial, s.splits, c.rows, np, (int)c.r,
                                                                     c.epi_final, c.alpha, c.accumulate, dt, c.out,
-                                                                    c.ldo, c.rs, c.cs);
+                                                                    c.ldo, c.rs, c.cs, a.pcol);
         REELS_LAUNCHED();
     }
     return REELS_OK;

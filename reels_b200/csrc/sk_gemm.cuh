@@ -56,8 +56,9 @@ struct SkArgs {
     void *out;
     long long ldo;     // epi 0: row pitch of out[j][row]
     long long rs, cs;  // epi 1: out[row*rs + j*cs]
-    float *partial;    // epi 2: [splits][rows][npad]
+    float *partial;    // epi 2: [splits][rows][npad], or [splits][npad][rows] with pcol
     unsigned *err;
+    int pcol;          // partial layout with rows contiguous (see sk_reduce_kernel)
 };
 
 struct SkUnit {
@@ -215,7 +216,12 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
 #pragma unroll
                     for (int t = 0; t < 16; ++t) v[t] = 0u;
                 }
-                if (args.epi == 2) {
+                if (args.epi == 2 && args.pcol) {
+                    // rows contiguous: lanes (consecutive rows) write 128 bytes per column
+                    float *dst = args.partial + ((long long)w.sp * args.npad + c) * args.rows + row;
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) dst[(long long)t * args.rows] = __uint_as_float(v[t]);
+                } else if (args.epi == 2) {
                     float *dst = args.partial + ((long long)w.sp * args.rows + row) * args.npad + c;
 #pragma unroll
                     for (int t = 0; t < 16; t += 4)
