@@ -29,6 +29,8 @@ The ``--mode`` measurements print one JSON line per case:
   norm   fused LayerNorm + modulation against the same expression as
          separate PyTorch kernels
   adamw  gradient norm + clipped AdamW over the 40-block Wan 14B adapters
+  trace  per-role cycle counters of the weight-in-TMEM GEMM (needs a library
+         built with -DREELS_TS_TRACE)
 """
 from __future__ import annotations
 
@@ -970,6 +972,76 @@ def mode_adamw(args):
     print(json.dumps(out), flush=True)
 
 
+def mode_trace(args):
+    """Per-role cycle counters of the weight-in-TMEM GEMM, from a debug build
+    of the library (nvcc ... -DREELS_TS_TRACE, loaded through
+    REELS_LOWVRAM_LIBRARY; the shipped library has no counters).  For each
+    case, one launch of _weight_mul (fwd) or _weight_transpose_mul (dx) after
+    three warm-up launches; per role (X producer, MMA, W producer, dequant,
+    epilogue) the average cycles per CTA in [wait 0, wait 1, work, total]."""
+    import ctypes
+    import torch
+    from reels_b200 import _native as nat
+    L = nat.lib()
+    if not hasattr(L, "reels_ts_trace_read"):
+        raise SystemExit("the loaded library has no counters: build it with -DREELS_TS_TRACE and point "
+                         "REELS_LOWVRAM_LIBRARY at it")
+    L.reels_ts_trace_read.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    nw = 19
+    buf = (ctypes.c_ulonglong * (256 * nw * 4))()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    roles = {0: "xprod", 1: "mma", 2: "wprod"}
+    roles.update({w: "deq" for w in range(3, 11)})
+    roles.update({w: "epi" for w in range(11, 19)})
+    cases = [(128, 5120, 13824, "f16", True), (128, 5120, 13824, "f16", False), (512, 5120, 13824, "f16", True),
+             (32760, 1536, 1536, "bf16", True), (32760, 1536, 1536, "bf16", False), (8192, 1536, 8960, "bf16", True)]
+    for (M, K, N, dtn, fwd) in cases:
+        tdt, dt = (torch.float16, nat.F16) if dtn == "f16" else (torch.bfloat16, nat.BF16)
+        x = torch.randn(M, K, device=dev).to(tdt)
+        dy = torch.randn(M, N, device=dev).to(tdt)
+        q = torch.randint(-127, 128, (K, N), device=dev, dtype=torch.int8)
+        s = torch.rand(N, device=dev) * 1e-3 + 1e-4
+        y = torch.empty(M, N, device=dev, dtype=tdt)
+        dx = torch.empty(M, K, device=dev, dtype=tdt)
+        wsn = max(L.reels_q8lora_workspace_bytes(M, K, N, 0, dt, p) for p in (0, 1))
+        ws = torch.empty(max(wsn, 256), dtype=torch.uint8, device=dev)
+        st = torch.cuda.current_stream(dev).cuda_stream
+
+        def run():
+            if fwd:
+                nat.check("fwd", L.reels_q8_weight_mul(x.data_ptr(), q.data_ptr(), s.data_ptr(), 0, None, M, K, N,
+                                                       dt, y.data_ptr(), ws.data_ptr(), wsn, st))
+            else:
+                nat.check("dx", L.reels_q8_weight_transpose_mul(dy.data_ptr(), q.data_ptr(), s.data_ptr(), 0, M, K,
+                                                                N, dt, dx.data_ptr(), ws.data_ptr(), wsn, st))
+        for _ in range(3):
+            run()
+        L.reels_ts_trace_read(None, 0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3
+        L.reels_ts_trace_read(buf, len(buf))
+        info = (ctypes.c_int64 * 7)()
+        L.reels_q8_plan(M, N if fwd else K, K if fwd else N, 0, 0, info)
+        ctas = [c for c in range(256) if buf[(c * nw + 1) * 4 + 3] > 0]
+        agg = {}
+        for c in ctas:
+            for w in range(nw):
+                a = agg.setdefault(roles[w], [0, 0, 0, 0, 0])
+                for k in range(4):
+                    a[k] += buf[(c * nw + w) * 4 + k]
+                a[4] += 1
+        out = {"shape": [M, K, N, dtn, "fwd" if fwd else "dx"], "us": round(us, 1), "plan": list(info),
+               "ctas": len(ctas)}
+        for role, a in agg.items():
+            out[role] = [round(a[k] / a[4]) for k in range(4)]
+        print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -982,7 +1054,7 @@ def main():
     ap.add_argument("--no-small-m", action="store_true", help="skip the small-token record of the default line")
     ap.add_argument("--bucket-mb", type=float, default=None,
                     help="all-reduce bucket size (default: per linear, 64 MB for the 40-block stack)")
-    ap.add_argument("--mode", default="step", choices=["step", "sweep", "gemm", "norm", "adamw"])
+    ap.add_argument("--mode", default="step", choices=["step", "sweep", "gemm", "norm", "adamw", "trace"])
     # measurement modes
     ap.add_argument("--N", type=int, default=13824)
     ap.add_argument("--K", type=int, default=5120)
@@ -1003,7 +1075,8 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.mode != "step":
-        {"sweep": mode_sweep, "gemm": mode_gemm, "norm": mode_norm, "adamw": mode_adamw}[args.mode](args)
+        {"sweep": mode_sweep, "gemm": mode_gemm, "norm": mode_norm, "adamw": mode_adamw,
+         "trace": mode_trace}[args.mode](args)
         return
     if args.impl == "reference":
         run_reference(args)
