@@ -97,22 +97,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
 #ifndef REELS_SUSPEND_HINT_NS
 #define REELS_SUSPEND_HINT_NS 1000000u
 #endif
-// REELS_WAIT_FORM selects how a pipeline wait blocks: 0 try_wait with the
-// suspend hint above, 1 try_wait with the system's own time limit.
-#ifndef REELS_WAIT_FORM
-#define REELS_WAIT_FORM 0
-#endif
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
-#if REELS_WAIT_FORM == 1
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-#else
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
@@ -120,7 +106,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
         : "memory");
-#endif
     return ok != 0;
 }
 
@@ -149,17 +134,10 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort,
                                          unsigned *err, unsigned code) {
     if (mbar_test_wait(bar, parity)) return true;
-#if REELS_WAIT_FORM == 2
-    // spin on the non-blocking probe (no suspension)
-    long long t0 = clock64();
-    while (true) {
-        if (mbar_test_wait(bar, parity)) return true;
-#else
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-#endif
         if (*abort) return false;
         if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
             *abort = 1;
@@ -282,108 +260,17 @@ __device__ __forceinline__ uint2 ld_shared_v2(uint32_t addr) {
     return v;
 }
 
-// ------------------------------------------------------------ clusters
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-// Address of the same shared-memory offset in CTA `rank` of this cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-    uint32_t d;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
-    return d;
-}
-// Arrive on an mbarrier in another CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// try_wait that acquires at cluster scope (for phases completed by a peer CTA).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool wait_bar_cluster(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *err,
-                                                 unsigned code) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    long long t0 = clock64();
-    while (true) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (*abort) return false;
-        if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
-            *abort = 1;
-            if (err) atomicOr(err, code);
-            return false;
-        }
-    }
-}
-// TMA load issued by either CTA of a cta_group::2 pair whose completion is
-// counted on an mbarrier that may live in the peer CTA (`bar_cluster` is a
-// shared::cluster address, e.g. from mapa).  No multicast: the data lands
-// only in this CTA's shared memory.
-__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, int x, int y,
-                                                 uint32_t bar_cluster) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_cluster)
-        : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_cluster() {
-    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Pair-CTA (cta_group::2) tensor-core forms: the leader CTA issues the MMA for
-// both CTAs; A and D rows are split between them, B columns too.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-                 "r"(ncols)
-                 : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                                uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// Arrive once on `bar` in every CTA of `cta_mask` when the pair's MMAs issued
-// so far are done.
-__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {
-    asm volatile(
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-            smem_u32(bar)),
-        "h"(cta_mask)
-        : "memory");
-}
-
 // Programmatic dependent launch.  A kernel launched with programmatic stream
 // serialization is queued early; griddep_wait() blocks until the previous
 // kernel in the stream has completed and its memory is visible, so every such
-// kernel calls it before its first global-memory access (read or write).
-// The kernels do not signal griddepcontrol.launch_dependents: with that early
-// trigger the dX GEMM on 128x192 tiles produced wrong results on B200 (parity
-// tests), a failure that waiting alone does not show and whose cause is not
-// established.  Data written by an earlier kernel is read through L2
-// (__ldcg), not through the SM's L1 or the read-only path.
+// kernel calls it before its first global-memory access (read or write), on
+// every path: a kernel whose CTAs could all exit without waiting would finish
+// ahead of its predecessor and release the next kernel early, so the
+// stream's order is transitive only if every kernel waits.  The kernels do
+// not signal griddepcontrol.launch_dependents: with every kernel waiting an
+// early trigger is correct, but it measured no faster.  Data written by an
+// earlier kernel is read through L2 (__ldcg), not through the SM's L1 or the
+// read-only path.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // 32-byte global stores (sm_100): one instruction per 16 bf16/fp16 or 8 fp32.
