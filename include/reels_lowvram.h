@@ -105,6 +105,14 @@ int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64
  * info[0] splits, info[1] 64-element blocks per split. */
 int reels_sk_plan(int64_t rows, int64_t red, int64_t r, int sms, int64_t *info);
 
+/* Plan of the backward's one pass over dy, which computes G = s*B'*dy and dB
+ * together (no reference counterpart; the reference computes them as two
+ * products, lora.jl:112-114).  info[0] 1 when the backward uses it (else G
+ * and dB are separate passes), info[1] token ranges, info[2] feature
+ * ranges, info[3] TMEM columns per CTA, info[4] and info[5] bytes of fp32
+ * partials for G and dB. */
+int reels_sk_dual_plan(int64_t M, int64_t N, int64_t r, int sms, int64_t *info);
+
 /* Path taken by the last successful compute call on this thread. */
 int reels_lowvram_last_path(void);
 

@@ -40,6 +40,7 @@ SIGNATURES = {
     "reels_lowvram_last_path": (_int, []),
     "reels_q8_plan": (_int, [_i64, _i64, _i64, _int, _int, ctypes.POINTER(ctypes.c_int64)]),
     "reels_sk_plan": (_int, [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_int64)]),
+    "reels_sk_dual_plan": (_int, [_i64, _i64, _i64, _int, ctypes.POINTER(ctypes.c_int64)]),
     "reels_lowvram_check_device_status": (_int, [_vp]),
     "reels_lowvram_profile_enable": (_int, [_int]),
     "reels_lowvram_profile_read": (_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64),

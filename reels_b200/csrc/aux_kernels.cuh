@@ -196,48 +196,124 @@ __global__ void q8_reduce_kernel(const float *partial, int splits, int64_t M, in
 // row (out[row*rs + j] with cs = 1); pcol = 1, partials [splits][npad][rows]
 // and consecutive outputs are consecutive rows (the transposed store
 // out[j*ldo + row], or out[row + j*cs] with rs = 1).
-__global__ void sk_reduce_kernel(const float *partial, int splits, int64_t rows, int npad, int ncols,
-                                 int epi, float alpha, int accumulate, int dt, void *out, int64_t ldo, int64_t rs,
-                                 int64_t cs, int pcol) {
+// With few splits (vec = 1: pcol layout, rows % 4 == 0, 16-byte aligned
+// output) a lane instead owns four consecutive outputs, adds the splits in
+// order with float4 loads and writes the four results at once: a warp covers
+// 128 outputs per step instead of eight.
+// One launch sums one or two such jobs (G and dB of the one-pass dy kernel):
+// the warps take the first job's groups of outputs, then the second's.
+struct RedJob {
+    const float *partial;
+    int splits;
+    int64_t rows;
+    int npad, ncols, epi;
+    float alpha;
+    int accumulate;
+    void *out;
+    int64_t ldo, rs, cs;
+    int pcol;
+    int vec;
+};
+
+constexpr int RED_VEC_MAX = 8;  // most splits of the vector path
+
+__device__ __forceinline__ int64_t red_groups(const RedJob &J) {
+    const int64_t total = J.rows * (int64_t)J.ncols;
+    return J.vec ? (total + 127) / 128 : (total + 7) / 8;
+}
+
+__device__ __forceinline__ void reduce_group_vec(const RedJob &J, int64_t w, int lane, int dt) {
+    const int64_t o = w * 128 + 4 * lane;  // four consecutive rows of one column j
+    if (o >= J.rows * (int64_t)J.ncols) return;
+    const int64_t j = o / J.rows, row = o % J.rows;
+    const int64_t stride = J.rows * (int64_t)J.npad;
+    const float *p = J.partial + j * J.rows + row;
+    float4 v[RED_VEC_MAX];
+#pragma unroll
+    for (int s = 0; s < RED_VEC_MAX; ++s)  // every load in flight, then the sum in split order
+        if (s < J.splits) v[s] = __ldcg(reinterpret_cast<const float4 *>(p + (int64_t)s * stride));
+    float4 acc = v[0];
+#pragma unroll
+    for (int s = 1; s < RED_VEC_MAX; ++s) {
+        if (s < J.splits) {
+            acc.x += v[s].x;
+            acc.y += v[s].y;
+            acc.z += v[s].z;
+            acc.w += v[s].w;
+        }
+    }
+    if (J.epi == 0) {
+        const int64_t idx = j * J.ldo + row;
+        if (dt == DT_BF16) {
+            *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(J.out) + idx) =
+                make_uint2(Elem<DT_BF16>::pack2(J.alpha * acc.x, J.alpha * acc.y),
+                           Elem<DT_BF16>::pack2(J.alpha * acc.z, J.alpha * acc.w));
+        } else {
+            *reinterpret_cast<uint2 *>(reinterpret_cast<__half *>(J.out) + idx) =
+                make_uint2(Elem<DT_F16>::pack2(J.alpha * acc.x, J.alpha * acc.y),
+                           Elem<DT_F16>::pack2(J.alpha * acc.z, J.alpha * acc.w));
+        }
+    } else {
+        float4 *o4 = reinterpret_cast<float4 *>(reinterpret_cast<float *>(J.out) + row + j * J.cs);
+        float4 prev = J.accumulate ? *o4 : make_float4(0.f, 0.f, 0.f, 0.f);
+        prev.x += J.alpha * acc.x;
+        prev.y += J.alpha * acc.y;
+        prev.z += J.alpha * acc.z;
+        prev.w += J.alpha * acc.w;
+        *o4 = prev;
+    }
+}
+
+__device__ __forceinline__ void reduce_group(const RedJob &J, int64_t w, int lane, int dt) {
+    const int sl = lane & 3;
+    const int64_t total = J.rows * (int64_t)J.ncols;
+    const int64_t stride = J.rows * (int64_t)J.npad;
+    const int64_t o = w * 8 + (lane >> 2);  // eight consecutive outputs per warp
+    float acc = 0.0f;
+    int64_t row = 0, j = 0;
+    if (o < total) {
+        if (J.pcol) {
+            j = o / J.rows;
+            row = o % J.rows;
+        } else {
+            row = o / J.ncols;
+            j = o % J.ncols;
+        }
+        const float *p = J.pcol ? J.partial + j * J.rows + row : J.partial + row * J.npad + j;
+        int s = sl;
+        for (; s + 28 < J.splits; s += 32) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (int64_t)(s + 4 * u) * stride);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc += v[u];
+        }
+        for (; s < J.splits; s += 4) acc += __ldcg(p + (int64_t)s * stride);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (sl == 0 && o < total) {
+        if (J.epi == 0) {
+            store_act(J.out, j * J.ldo + row, dt, J.alpha * acc);
+        } else {
+            float *o32 = reinterpret_cast<float *>(J.out);
+            const int64_t idx = row * J.rs + j * J.cs;
+            o32[idx] = (J.accumulate ? o32[idx] : 0.0f) + J.alpha * acc;
+        }
+    }
+}
+
+__global__ void sk_reduce_kernel(const RedJob j0, const RedJob j1, int njobs, int dt) {
     griddep_wait();
-    const int64_t total = rows * (int64_t)ncols;
-    const int lane = threadIdx.x & 31, sl = lane & 3;
-    const int64_t stride = rows * (int64_t)npad;
+    const int lane = threadIdx.x & 31;
+    const int64_t g0 = red_groups(j0);
+    const int64_t g1 = njobs > 1 ? red_groups(j1) : 0;
     const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w * 8 < total; w += nw) {
-        const int64_t o = w * 8 + (lane >> 2);  // eight consecutive outputs per warp
-        float acc = 0.0f;
-        int64_t row = 0, j = 0;
-        if (o < total) {
-            if (pcol) {
-                j = o / rows;
-                row = o % rows;
-            } else {
-                row = o / ncols;
-                j = o % ncols;
-            }
-            const float *p = pcol ? partial + j * rows + row : partial + row * npad + j;
-            int s = sl;
-            for (; s + 28 < splits; s += 32) {
-                float v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (int64_t)(s + 4 * u) * stride);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) acc += v[u];
-            }
-            for (; s < splits; s += 4) acc += __ldcg(p + (int64_t)s * stride);
-        }
-        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-        if (sl == 0 && o < total) {
-            if (epi == 0) {
-                store_act(out, j * ldo + row, dt, alpha * acc);
-            } else {
-                float *o32 = reinterpret_cast<float *>(out);
-                const int64_t idx = row * rs + j * cs;
-                o32[idx] = (accumulate ? o32[idx] : 0.0f) + alpha * acc;
-            }
-        }
+    for (int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < g0 + g1; w += nw) {
+        const RedJob &J = w < g0 ? j0 : j1;
+        const int64_t wl = w < g0 ? w : w - g0;
+        if (J.vec) reduce_group_vec(J, wl, lane, dt);
+        else reduce_group(J, wl, lane, dt);
     }
 }
 

@@ -230,6 +230,10 @@ int bind_device(const void *ptr, DeviceState **out, DeviceScope &scope) {
                                         SK_SMEM_BYTES));
         REELS_CUDA(cudaFuncSetAttribute(sk_gemm_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         SK_SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(sk_dual_kernel<DT_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        DU_SMEM_BYTES));
+        REELS_CUDA(cudaFuncSetAttribute(sk_dual_kernel<DT_F16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        DU_SMEM_BYTES));
         if (!g_encode) {
             void *fn = nullptr;
             cudaDriverEntryPointQueryResult qr;
@@ -405,6 +409,70 @@ Split plan_sk(int64_t rows, int64_t red, int sms, int64_t r) {
     return plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4, npad_of(r));
 }
 
+// Grid of the one-pass dy kernel (sk_dual_kernel): splits_m token ranges x
+// splits_n feature ranges, one CTA each.  Cost, in units of 16 KB streamed
+// into one SM: the largest CTA's stages (each a 128 x 128 tile of dy, 32 KB,
+// plus 128 columns of B and 128 tokens of T, npad x 256 B each), plus the
+// fp32 partials written and read back (G's when the features are split, dB's
+// when the tokens are), spread over the SMs, plus a fixed charge for the
+// reduce launch.  The separate G and dB passes are costed the same way
+// (plan_split; each 16 KB block of dy brings npad x 128 B of B or T); the
+// cheaper plan wins.  Ranks above 128 leave no TMEM for the dB accumulators:
+// separate passes.
+struct DualPlan {
+    bool use = false;
+    int splits_m = 1, splits_n = 1, tmem_cols = 0;
+    int64_t part_g = 0, part_db = 0;  // partial bytes
+};
+
+DualPlan plan_dual(int64_t M, int64_t N, int64_t r, int sms) {
+    DualPlan best;
+    const int np = npad_of(r);
+    const int kmax = np <= 128 ? du_max_ftiles(np) : 0;
+    if (kmax < 1 || M <= 0 || N <= 0 || r <= 0) return best;
+    if (const char *e = getenv("REELS_SK_DUAL"))
+        if (atoi(e) == 0) return best;
+    const int64_t TM = cdiv(M, 128), TN = cdiv(N, 128);
+    const double blk = 16384.0 * sms;  // bytes the GPU streams per block round
+    double best_cost = 1e300;
+    for (int64_t sn = cdiv(TN, kmax); sn <= std::min<int64_t>(TN, sms); ++sn) {
+        const int64_t kn = cdiv(TN, sn);
+        if (kn > kmax) continue;
+        const int64_t sm_max = std::min<int64_t>(TM, sms / sn);
+        for (int64_t smm = 1; smm <= sm_max; ++smm) {
+            const double part_g = sn > 1 ? (double)sn * M * np * 4 : 0.0;
+            const double part_db = smm > 1 ? (double)smm * N * np * 4 : 0.0;
+            double cost = (2.0 + np / 32.0) * (double)(cdiv(TM, smm) * kn) + 2.0 * (part_g + part_db) / blk;
+            if (sn > 1 || smm > 1) cost += 2.0;
+            if (cost < best_cost * 0.999) {
+                best_cost = cost;
+                best.splits_m = (int)smm;
+                best.splits_n = (int)sn;
+                best.part_g = (int64_t)part_g;
+                best.part_db = (int64_t)part_db;
+            }
+        }
+    }
+    // the separate passes: G (rows = tokens, reduction = features) and dB
+    // (rows = features, reduction = tokens), each with its own split
+    auto sep = [&](int64_t rows, int64_t red) {
+        const Split s = plan_split(cdiv(rows, 128), cdiv(red, BK), sms, 4, np);
+        double c = (double)cdiv(cdiv(rows, 128) * s.splits, sms) * s.kb_per * (1.0 + np / 128.0);
+        if (s.splits > 1) c += 2.0 * 128.0 * np * 4.0 * (double)(cdiv(rows, 128) * s.splits) / blk + 2.0;
+        return c + 2.0;  // launch
+    };
+    const double sep_cost = sep(M, N) + sep(N, M);
+    if (best_cost + 2.0 < sep_cost) {
+        best.use = true;
+        const int64_t kn = cdiv(TN, best.splits_n);
+        const int need = (int)(2 + kn) * du_acc_cols(np);
+        int cols = 32;
+        while (cols < need) cols <<= 1;
+        best.tmem_cols = cols;
+    }
+    return best;
+}
+
 
 // Workspace layout shared by the forward and backward passes.
 struct Ws {
@@ -459,6 +527,8 @@ Ws ws_layout(int64_t M, int64_t K, int64_t N, int64_t r, int dt, int pass_flags,
                 sk_part(M, N);  // B'*dy
                 sk_part(K, M);  // dA
                 sk_part(N, M);  // dB
+                const DualPlan d = plan_dual(M, N, r, sms);  // G and dB in one pass over dy
+                if (d.use) part = std::max(part, align256((size_t)d.part_g) + (size_t)d.part_db);
             }
             q8_part(M, K, N);
         }
@@ -500,6 +570,16 @@ struct SkCall {
     int64_t ldo, rs, cs;
 };
 
+// The reduction's vector path (four consecutive outputs per lane, float4
+// partial loads): few splits, rows-contiguous partials and outputs whose
+// four-row groups are aligned (8 B for 16-bit stores, 16 B for fp32).
+int red_vec_ok(const RedJob &j) {
+    if (!j.pcol || j.splits > RED_VEC_MAX || j.rows % 4 != 0) return 0;
+    const uintptr_t o = reinterpret_cast<uintptr_t>(j.out);
+    if (j.epi == 0) return (o % 8 == 0 && j.ldo % 4 == 0) ? 1 : 0;
+    return (j.rs == 1 && o % 16 == 0 && j.cs % 4 == 0) ? 1 : 0;
+}
+
 int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const Ws &wl, cudaStream_t st) {
     CUtensorMap ta, tb;
     int rc;
@@ -539,9 +619,64 @@ int run_sk(const SkCall &c, int dt, const DeviceState &ds, char *ws_base, const 
     else launch_pdl(sk_gemm_kernel<DT_F16>, dim3(grid), dim3(SK_THREADS), SK_SMEM_BYTES, st, ta, tb, a);
     REELS_LAUNCHED();
     if (s.splits > 1) {
-        launch_pdl(sk_reduce_kernel, dim3(launch_grid(c.rows * c.r * 4)), dim3(256), 0, st, a.partial, s.splits, c.rows, np, (int)c.r,
-                                                                    c.epi_final, c.alpha, c.accumulate, dt, c.out,
-                                                                    c.ldo, c.rs, c.cs, a.pcol);
+        RedJob j{a.partial, s.splits, c.rows, np, (int)c.r, c.epi_final, c.alpha, c.accumulate, c.out,
+                 c.ldo, c.rs, c.cs, a.pcol, 0};
+        j.vec = red_vec_ok(j);
+        launch_pdl(sk_reduce_kernel, dim3(launch_grid(c.rows * c.r * 4)), dim3(256), 0, st, j, j, 1, dt);
+        REELS_LAUNCHED();
+    }
+    return REELS_OK;
+}
+
+// G = s*(B'*dy) into gbuf ([r][ldm], 16-bit) and dB = alpha_db * T*dy (fp32
+// [r][N], accumulated when asked) from one pass over dy (sk_dual_kernel), then
+// one reduce launch for whichever of the two was split.
+int run_dual(const DualPlan &d, const void *dy, const void *B, const void *tbuf, int64_t M, int64_t N, int64_t r,
+             float s, float alpha_db, int accumulate, void *gbuf, float *dB, int dt, const DeviceState &ds,
+             char *ws_base, const Ws &wl, cudaStream_t st) {
+    CUtensorMap tdy, tb, tt;
+    const int np = npad_of(r);
+    const int64_t ldm = ld_tokens(M);
+    int rc = tmap_2d(&tdy, dy, tma_act_type(dt), N, M, (uint64_t)N * 2, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = tmap_2d(&tb, B, tma_act_type(dt), N, r, (uint64_t)N * 2, 64, np, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = tmap_2d(&tt, tbuf, tma_act_type(dt), M, r, (uint64_t)ldm * 2, 64, np, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    if (align256((size_t)d.part_g) + (size_t)d.part_db > wl.total - wl.part)
+        return fail("workspace partial region too small for the one-pass dy plan");
+    SkDualArgs a;
+    a.M = (int)M;
+    a.N = (int)N;
+    a.tm_tiles = (int)cdiv(M, 128);
+    a.tn_tiles = (int)cdiv(N, 128);
+    a.splits_m = d.splits_m;
+    a.splits_n = d.splits_n;
+    a.npad = np;
+    a.ncols = (int)r;
+    a.tmem_cols = d.tmem_cols;
+    a.g_out = gbuf;
+    a.ldm = ldm;
+    a.g_alpha = s;
+    float *part = reinterpret_cast<float *>(ws_base + wl.part);
+    a.g_part = part;
+    a.db_out = dB;
+    a.db_alpha = alpha_db;
+    a.accumulate = accumulate;
+    a.db_part = reinterpret_cast<float *>(reinterpret_cast<char *>(part) + align256((size_t)d.part_g));
+    a.err = ds.status;
+    const dim3 grid((unsigned)(d.splits_m * d.splits_n));
+    if (dt == REELS_BF16) launch_pdl(sk_dual_kernel<DT_BF16>, grid, dim3(SK_THREADS), DU_SMEM_BYTES, st, tdy, tb, tt, a);
+    else launch_pdl(sk_dual_kernel<DT_F16>, grid, dim3(SK_THREADS), DU_SMEM_BYTES, st, tdy, tb, tt, a);
+    REELS_LAUNCHED();
+    RedJob jobs[2];
+    int n = 0;
+    if (d.splits_n > 1) jobs[n++] = RedJob{a.g_part, d.splits_n, M, np, (int)r, 0, s, 0, gbuf, ldm, 0, 0, 1, 0};
+    if (d.splits_m > 1) jobs[n++] = RedJob{a.db_part, d.splits_m, N, np, (int)r, 1, alpha_db, accumulate, dB, 0, 1, N, 1, 0};
+    for (int i = 0; i < n; ++i) jobs[i].vec = red_vec_ok(jobs[i]);
+    if (n > 0) {
+        const int64_t outs = (n > 1 ? M + N : (d.splits_n > 1 ? M : N)) * r;
+        launch_pdl(sk_reduce_kernel, dim3(launch_grid(outs * 4)), dim3(256), 0, st, jobs[0], jobs[n - 1], n, dt);
         REELS_LAUNCHED();
     }
     return REELS_OK;
@@ -1082,6 +1217,19 @@ int reels_sk_plan(int64_t rows, int64_t red, int64_t r, int sms, int64_t *info) 
     return REELS_OK;
 }
 
+int reels_sk_dual_plan(int64_t M, int64_t N, int64_t r, int sms, int64_t *info) {
+    if (!info) return fail("null info");
+    if (M <= 0 || N <= 0 || r <= 0 || r > 256) return fail("plan needs positive M, N and 0 < r <= 256");
+    const DualPlan d = plan_dual(M, N, r, sms > 0 ? sms : current_sms());
+    info[0] = d.use ? 1 : 0;
+    info[1] = d.splits_m;
+    info[2] = d.splits_n;
+    info[3] = d.tmem_cols;
+    info[4] = d.part_g;
+    info[5] = d.part_db;
+    return REELS_OK;
+}
+
 int reels_lowvram_profile_enable(int enable) {
     t_prof.on = enable != 0;
     t_prof.used = 0;
@@ -1416,6 +1564,7 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
         // operand (A, zero-padded) and, when A*x is recomputed, A^T.
         const int epi = act == REELS_ACT_GELU_TANH ? ACT_GELU_TANH_GRAD : ACT_NONE;
         const bool ts_prep = r > 0 && dx && !drop && plan_q8(M, K, N, ds->sms, aligned16(scales), epi).ts > 0;
+        const DualPlan dual = plan_dual(M, N, r, ds->sms);
         if (ts_prep) {
             rc = prep_lora(dt, 1, nullptr, scales, 1.0f, false, r, ts_rank_pad(r), K, ws + wl.ext, A, K,
                            saved ? nullptr : ws + wl.at, st);
@@ -1426,23 +1575,29 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
                 rc = rank_down_tc(ax, A, M, K, r, dt, ws + wl.tbuf, ws + wl.at, *ds, ws, wl, st, ts_prep);
                 if (rc) return rc;
             }
-            // g' = s * (B' * dy), stored [r][ldm]
-            SkCall g{};
-            g.act = dy;
-            g.act_inner = N;
-            g.act_outer = M;
-            g.a_mn = false;
-            g.bop = B;
-            g.bop_pitch = N;
-            g.rows = M;
-            g.red = N;
-            g.r = r;
-            g.epi_final = 0;
-            g.alpha = s;
-            g.out = gbuf;
-            g.ldo = ldm;
-            rc = run_sk(g, dt, *ds, ws, wl, st);
-            if (rc) return rc;
+            if (dual.use) {
+                // g' and dB from one pass over dy
+                rc = run_dual(dual, dy, B, tbuf, M, N, r, s, grad_scale * s, accumulate, gbuf, dB, dt, *ds, ws, wl, st);
+                if (rc) return rc;
+            } else {
+                // g' = s * (B' * dy), stored [r][ldm]
+                SkCall g{};
+                g.act = dy;
+                g.act_inner = N;
+                g.act_outer = M;
+                g.a_mn = false;
+                g.bop = B;
+                g.bop_pitch = N;
+                g.rows = M;
+                g.red = N;
+                g.r = r;
+                g.epi_final = 0;
+                g.alpha = s;
+                g.out = gbuf;
+                g.ldo = ldm;
+                rc = run_sk(g, dt, *ds, ws, wl, st);
+                if (rc) return rc;
+            }
         }
         if (dx) {
             Q8Call c{};
@@ -1493,6 +1648,8 @@ static int q8lora_backward_impl(const void *x, const void *dy, const int8_t *q, 
             da.cs = 1;
             rc = run_sk(da, dt, *ds, ws, wl, st);
             if (rc) return rc;
+        }
+        if (r > 0 && !dual.use) {
             // dB[j][n] = grad_scale * s * sum_m dy[m][n] t[j][m]
             SkCall db{};
             db.act = dy;

@@ -62,10 +62,9 @@ __device__ unsigned long long g_ts_trace[256 * (TS_THREADS / 32) * 4];
 #define TS_ADD(k, v)
 #endif
 
-// A pipeline stage covers SK = 64*KB2 reduction elements: KB2 = 1 for the
-// 256- and 192-token tiles, 2 for 128-token tiles (the MMA warp's
-// per-stage synchronisation is then spread over twice the weight bytes,
-// which is what bounds weight streaming at small token counts).
+// A pipeline stage covers SK = 64*KB2 reduction elements, KB2 = 1 or 2 as the
+// planner picks per shape: a 128-wide stage spreads the MMA warp's per-stage
+// synchronisation over twice the tensor work and weight bytes.
 // TMEM (512 columns): NACC accumulators of BT columns and NA A-operand stages
 // of SK/2 columns.  BT = 256 leaves room for one accumulator only; BT <= 192
 // double-buffers it so the epilogue overlaps the next tile's MMAs.
@@ -75,7 +74,6 @@ struct TsGeom {
     static constexpr int NACC = BT == 256 ? 1 : 2;
     static constexpr int ACOLS = SK / 2;
     static constexpr int NA = (BT == 192 ? 4 : 8) / KB2;
-    static constexpr int X_BYTES = KB2 * BT * 128;  // activation tile: KB2 SW128 atoms of BT rows x 64 K
     static constexpr int W_BYTES = 128 * SK;        // int8 tile: 128 output columns x SK
     static constexpr int SC_BYTES = 4 * SK;         // SK fp32 reduction scales
     static constexpr int EPI_BYTES = 4096;          // per epilogue warp: two 32 x 32 16-bit staging tiles
@@ -88,23 +86,44 @@ struct TsGeom {
     static constexpr int SX = REELS_TS_SX ? REELS_TS_SX
                                           : (KB2 == 2 ? (BT == 128 ? 4 : 2) : (BT == 128 ? 6 : 4));
     static constexpr int S8 = REELS_TS_S8 ? REELS_TS_S8 : (KB2 == 2 ? 3 : (BT == 256 ? 6 : 8));
+    // The activation ring holds SXA slots of one 64-wide atom (BT x 64
+    // elements) each; stage ga reads atoms ga*KB2 .. ga*KB2 + KB2 - 1, atom ax
+    // in slot ax % SXA.
+    static constexpr int XA_BYTES = BT * 128;
+    static constexpr int SXA = SX * KB2;
+    // Atom release: with 128-wide stages on a double-buffered ring, a slot is
+    // handed back as soon as the MMAs that read its atom are done (x_empty),
+    // not when the whole stage is, so the refill of one atom overlaps the
+    // multiplication of the next.  With an even ring a stage's last atom
+    // always sits in an odd slot and is released by the stage's kb_empty
+    // commit, so only the first atom costs an extra commit.  Deep rings (the
+    // 128-token tiles) and 64-wide stages release whole stages through kb_empty.
+    static constexpr bool ATOM_REL = KB2 == 2 && BT != 128;
+    static constexpr bool LAST_VIA_KB = ATOM_REL && (SXA % KB2 == 0);
+    static constexpr int SXS = SXA / KB2;  // whole stages in the ring (when released by kb_empty)
+    static_assert(ATOM_REL || SXA == SX * KB2, "stage-level release needs stage-aligned atom slots");
+    static constexpr int NXE = ATOM_REL ? SXA : 0;  // x_empty barriers
     static constexpr int X_OFF = 0;
-    static constexpr int W_OFF = X_OFF + SX * X_BYTES;
+    static constexpr int W_OFF = X_OFF + SXA * XA_BYTES;
     static constexpr int SC_OFF = W_OFF + S8 * W_BYTES;
     static constexpr int EPI_OFF = (SC_OFF + S8 * SC_BYTES + 1023) / 1024 * 1024;
     static constexpr int BAR_OFF = EPI_OFF + TS_NEW * EPI_BYTES;
-    // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done, one pre-activation load per epilogue warp
-    static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1 + TS_NEW;
+    // w_full, w_empty, kb_full, kb_empty, acc_full, acc_empty, mma_done, one
+    // pre-activation load per epilogue warp, x_empty
+    static constexpr int NBAR = 2 * S8 + 2 * NA + 2 * NACC + 1 + TS_NEW + NXE;
     static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;
     static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
     static_assert(NACC * BT + NA * ACOLS <= 512, "TMEM plan exceeds 512 columns");
     // Stage ga uses barrier slot ga % NA: kb_full is completed by the
-    // activation TMA and the dequant group, kb_empty by the MMA commit once the
-    // stage's MMAs are done.  The activation producer reuses X slot ga % SX
-    // after stage ga - SX is consumed; with SX <= NA that stage's kb_empty
-    // phase cannot have been overtaken, so its parity is unambiguous.
-    static_assert(SX <= NA, "activation ring deeper than the stage barrier ring");
+    // activation TMA and the dequant group, kb_empty (which frees the TMEM A
+    // stage) by the MMA commit once the stage's MMAs are done.  The producer
+    // arrives on kb_full[ga % NA] only after the slot of the stage's first
+    // atom was released by its previous occupant, an atom of stage
+    // ga - ceil(SXA / KB2) or later; with ceil(SXA / KB2) <= NA, stage
+    // ga - NA's kb_full phase has then completed, so the arrival cannot land
+    // in an older phase.
+    static_assert((SXA + KB2 - 1) / KB2 <= NA, "activation ring deeper than the stage barrier ring");
 
     // Accumulator a starts at column 256 * a; A stages fill the columns left over.
     static __device__ __forceinline__ uint32_t acc_col(int a) { return 256u * a; }
@@ -404,6 +423,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     uint64_t *acc_empty = acc_full + G::NACC;
     uint64_t *mma_done = acc_empty + G::NACC;
     uint64_t *pre_bar = mma_done + 1;
+    uint64_t *x_empty = pre_bar + TS_NEW;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + G::MISC_OFF);
     volatile int *abort = reinterpret_cast<volatile int *>(smem + G::MISC_OFF + 4);
 
@@ -426,6 +446,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         }
         mbar_init(mma_done, 1);
         for (int i = 0; i < TS_NEW; ++i) mbar_init(&pre_bar[i], 1);
+        for (int i = 0; i < G::NXE; ++i) mbar_init(&x_empty[i], 1);  // one MMA commit per use
         *abort = 0;
         fence_mbar_init();
     }
@@ -461,35 +482,43 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             uint32_t gx = 0;
             for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
                 const TsTile c = ts_tile<BT, G::SK>(args, t);
-                for (int it = 0; it < c.n_main + c.n_ext; ++it, ++gx) {
-                    const int s = gx % G::SX;
-                    if (gx >= (uint32_t)G::SX) {
-                        const uint32_t j = gx - G::SX;  // the block that last used this X slot
-                        if (!TSW(0, wait_bar(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
-                                             DEVERR_TIMEOUT_AB_EMPTY))) {
+                for (int it = 0; it < c.n_main + c.n_ext && !aborted_here; ++it, ++gx) {
+                    uint64_t *full = &kb_full[gx % G::NA];
+                    // main: KB2 K-major atoms of [BT tokens][64 K]; ext: rank atoms of
+                    // [64 ranks][BT tokens], tokens contiguous (BT/64 boxes of 64 x 64),
+                    // atoms wholly past r not loaded (the MMA does not read them)
+                    const int e = it - c.n_main;
+                    const int na = it < c.n_main ? KB2 : min(KB2, (args.r - G::SK * e + 63) / 64);
+#pragma unroll
+                    for (int a = 0; a < KB2; ++a) {
+                        const uint32_t ax = gx * KB2 + a;
+                        const int slot = ax % G::SXA;
+                        // Wait for the slot's previous atom to be released; every slot is
+                        // waited for and released once per use, loaded or not.
+                        bool ok = true;
+                        if (G::ATOM_REL && (a < KB2 - 1 || !G::LAST_VIA_KB)) {
+                            if (ax >= (uint32_t)G::SXA)
+                                ok = TSW(0, wait_bar(&x_empty[slot], ((ax / G::SXA) & 1) ^ 1, abort, args.err,
+                                                     DEVERR_TIMEOUT_AB_EMPTY));
+                        } else if (a == (G::ATOM_REL ? KB2 - 1 : 0) && gx >= (uint32_t)G::SXS) {
+                            const uint32_t j = gx - G::SXS;  // the stage that last used these slots
+                            ok = TSW(0, wait_bar(&kb_empty[j % G::NA], (j / G::NA) & 1, abort, args.err,
+                                                 DEVERR_TIMEOUT_AB_EMPTY));
+                        }
+                        if (!ok) {
                             aborted_here = true;
                             break;
                         }
-                    }
-                    uint8_t *dst = smem + G::X_OFF + s * G::X_BYTES;
-                    uint64_t *full = &kb_full[gx % G::NA];
-                    if (it < c.n_main) {
-                        // KB2 K-major atoms of [BT tokens][64 K]
-                        mbar_arrive_expect_tx(full, G::X_BYTES);
-#pragma unroll
-                        for (int a = 0; a < KB2; ++a)
-                            tma_load_2d(dst + a * BT * 128, &tmX, (c.kb0 + it) * G::SK + 64 * a, c.m0, full);
-                    } else {
-                        // rank atoms of [64 ranks][BT tokens], tokens contiguous (BT/64 boxes of 64 x 64);
-                        // atoms wholly past r are not loaded (the MMA does not read them)
-                        const int e = it - c.n_main;
-                        const int na = min(KB2, (args.r - G::SK * e + 63) / 64);
-                        mbar_arrive_expect_tx(full, na * BT * 128);
-                        for (int a = 0; a < na; ++a)
+                        if (a == 0) mbar_arrive_expect_tx(full, na * BT * 128);
+                        if (a >= na) continue;
+                        uint8_t *dst = smem + G::X_OFF + slot * G::XA_BYTES;
+                        if (it < c.n_main) {
+                            tma_load_2d(dst, &tmX, (c.kb0 + it) * G::SK + 64 * a, c.m0, full);
+                        } else {
 #pragma unroll
                             for (int b = 0; b < BT / 64; ++b)
-                                tma_load_2d(dst + a * BT * 128 + b * 8192, &tmE, c.m0 + 64 * b,
-                                            G::SK * e + 64 * a, full);
+                                tma_load_2d(dst + b * 8192, &tmE, c.m0 + 64 * b, G::SK * e + 64 * a, full);
+                        }
                     }
                 }
             }
@@ -546,7 +575,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 const uint32_t d_tm = tmem + G::acc_col(acc);
                 const int n_iter = c.n_main + c.n_ext;
                 for (int it = 0; it < n_iter; ++it, ++ga) {
-                    const int sx = ga % G::SX, sa = ga % G::NA;
+                    const int sa = ga % G::NA;
                     if (!TSW(1, wait_bar(&kb_full[sa], (ga / G::NA) & 1, abort, args.err, DEVERR_TIMEOUT_AB_FULL))) {
                         aborted_here = true;
                         break;
@@ -554,22 +583,29 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     tc_fence_after();
                     TS_MARK(tr_issue);
                     const uint32_t a_tm = tmem + G::a_col(sa);
-                    const uint64_t xoff = (uint64_t)((sx * G::X_BYTES) >> 4);
-                    // K step kk reads atom kk/4 of the stage (BT*128 bytes each):
-                    // 32 bytes per step inside a K-major atom, 2048 inside a rank atom.
+                    // atom slot of K step kk: (ga * KB2 + kk / 4) % SXA; 32 bytes per step
+                    // inside a K-major atom, 2048 inside a rank atom
+                    auto xslot = [&](int a) { return (int)((ga * KB2 + a) % G::SXA); };
+                    auto xoff = [&](int a) { return (uint64_t)((xslot(a) * G::XA_BYTES) >> 4); };
+                    auto release = [&](int a) {
+                        if (G::ATOM_REL && (a < KB2 - 1 || !G::LAST_VIA_KB)) mma_commit(&x_empty[xslot(a)]);
+                    };
                     if (it < c.n_main) {
 #pragma unroll
-                        for (int kk = 0; kk < 4 * KB2; ++kk)
-                            mma_f16_ts(d_tm, a_tm + 8 * kk,
-                                       dmain0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 32) >> 4),
+                        for (int kk = 0; kk < 4 * KB2; ++kk) {
+                            mma_f16_ts(d_tm, a_tm + 8 * kk, dmain0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 32) >> 4),
                                        id_main, (it > 0 || kk > 0) ? 1u : 0u);
+                            if ((kk & 3) == 3) release(kk >> 2);  // this atom has been read
+                        }
                     } else {
                         const int e = it - c.n_main;
                         const int nk = (min(G::SK, args.r - G::SK * e) + 15) / 16;
                         for (int kk = 0; kk < nk; ++kk)
                             mma_f16_ts(d_tm, a_tm + 8 * kk,
-                                       dext0 + xoff + (uint64_t)(((kk >> 2) * BT * 128 + (kk & 3) * 2048) >> 4),
-                                       id_ext, (it > 0 || kk > 0) ? 1u : 0u);
+                                       dext0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 2048) >> 4), id_ext,
+                                       (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                        for (int a = 0; a < KB2; ++a) release(a);
                     }
                     mma_commit(&kb_empty[sa]);
                     TS_ADD(2, tr_issue);
@@ -603,6 +639,18 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 if (main_blk) ++gw;
                 if ((int)(ga % TS_NG) != g) continue;
                 const int sw = gw_this % G::S8;
+                // The groups share the int8 ring, so the slot's previous use may
+                // belong to the other group.  Waiting for that use to be released
+                // first (w_empty) means w_full can only be in this use's phase:
+                // otherwise, with the previous use's load still in flight, a
+                // parity wait for this use would see that older phase's parity
+                // and pass at once.
+                if (main_blk && gw_this >= (uint32_t)G::S8 &&
+                    !TSW(0, wait_bar_all(&w_empty[sw], ((gw_this / G::S8) & 1) ^ 1, abort, args.err,
+                                         DEVERR_TIMEOUT_W_EMPTY))) {
+                    aborted_here = true;
+                    break;
+                }
                 if (main_blk &&
                     !TSW(0, wait_bar_all(&w_full[sw], (gw_this / G::S8) & 1, abort, args.err, DEVERR_TIMEOUT_W_FULL))) {
                     aborted_here = true;

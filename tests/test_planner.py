@@ -88,7 +88,50 @@ def test_workspace_covers_every_split(lib):
                     splits, _ = sk(lib, rows, red, r)
                     if splits > 1:
                         need = max(need, splits * rows * np_ * 4)
+                if pas == nat.PASS_BACKWARD and M > 0:
+                    d = dual(lib, M, N, r)
+                    if d["use"]:  # G's and dB's partials are live together
+                        need = max(need, -(-d["part_g"] // 256) * 256 + d["part_db"])
             assert ws >= need, (M, K, N, r, pas, ws, need)
+
+
+def dual(lib, M, N, r):
+    info = (ctypes.c_int64 * 6)()
+    assert lib.reels_sk_dual_plan(M, N, r, SMS, info) == 0
+    return dict(zip(["use", "splits_m", "splits_n", "tmem_cols", "part_g", "part_db"], list(info)))
+
+
+def test_dy_pass_plans_fit_the_sm_count_and_tmem():
+    """The one-pass dy kernel runs one CTA per (token range, feature range),
+    all resident at once; each CTA holds two G accumulators and one dB
+    accumulator per feature tile of its range in 512 TMEM columns, and every
+    range is non-empty."""
+    native_build.build()
+    lib = nat.lib()
+    rng = np.random.default_rng(2)
+    shapes = [(32760, 1536, 32), (32760, 8960, 32), (128, 13824, 8), (512, 13824, 64), (4000, 256, 128)]
+    for _ in range(300):
+        shapes.append((int(rng.integers(1, 40000)), 16 * int(rng.integers(1, 1000)), int(rng.integers(1, 257))))
+    used = small = 0
+    for M, N, r in shapes:
+        d = dual(lib, M, N, r)
+        small += r <= 64
+        if not d["use"]:
+            continue
+        used += r <= 64
+        np_ = max(16, -(-r // 16) * 16)
+        acc = 32 if np_ <= 32 else 64 if np_ <= 64 else 128
+        tm, tn = -(-M // 128), -(-N // 128)
+        sm, sn = d["splits_m"], d["splits_n"]
+        assert r <= 128 and 1 <= sm <= tm and 1 <= sn <= tn and sm * sn <= SMS, (M, N, r, d)
+        kn = -(-tn // sn)
+        cols = d["tmem_cols"]
+        assert cols & (cols - 1) == 0 and (2 + kn) * acc <= cols <= 512, (M, N, r, d)
+        assert d["part_g"] == (sn * M * np_ * 4 if sn > 1 else 0)
+        assert d["part_db"] == (sm * N * np_ * 4 if sm > 1 else 0)
+    assert used >= 0.95 * small  # up to rank 64 the one pass is almost always the cheaper plan
+    for r in (129, 200, 256):
+        assert dual(lib, 32760, 1536, r)["use"] == 0
 
 
 def test_plan_queries_reject_bad_arguments(lib):
@@ -97,3 +140,5 @@ def test_plan_queries_reject_bad_arguments(lib):
     assert lib.reels_q8_plan(16, 16, 16, 5, SMS, info) == nat.EINVAL
     assert lib.reels_q8_plan(16, 16, 16, 0, SMS, None) == nat.EINVAL
     assert lib.reels_sk_plan(16, 16, 300, SMS, info) == nat.EINVAL
+    assert lib.reels_sk_dual_plan(16, 16, 300, SMS, info) == nat.EINVAL
+    assert lib.reels_sk_dual_plan(0, 16, 8, SMS, info) == nat.EINVAL
