@@ -327,11 +327,13 @@ struct Q8Plan {
 // epilogue cost the kernel cannot overlap; least squares over whole-tile
 // rounds of the Wan 1.3B/14B linears at 512..32760 tokens):
 //   weight-in-TMEM kernel (q8ts_gemm.cuh), 128 output columns x bt tokens,
-//   stages of 64 reduction elements: bt 256: 0.49 + 0.49 per tile (single
-//       accumulator), bt 192: 0.44 + 0.28, bt 128: 0.42 + 0.36;
-//   stages of 128: bt 256: 0.91 + 0.70, bt 192: 0.77 + 0.28, bt 128: 0.62 + 0.11.
+//   stages of 64 reduction elements: bt 256: 0.51 + 0.54 per tile (single
+//       accumulator), bt 192: 0.47 + 0.23, bt 128: 0.46 + 0.37;
+//   stages of 128: bt 256: 0.84 + 1.14, bt 192: 0.79 + 0.28, bt 128: 0.64 + 0.20.
 //   The MMA warp's per-stage waits and commit cost about the same whatever
-//   the stage width, so 128-wide stages move more weight per round trip.
+//   the stage width, so 128-wide stages move more weight per round trip; the
+//   256-token tiles' 128-wide stages also hand their activation atoms back
+//   one at a time (q8ts_gemm.cuh), which hides most of their refill.
 //   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
@@ -357,8 +359,8 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
         double per_kb, epi;  // per_kb: per pipeline stage (64 * kb2 reduction elements)
     };
     const Cand cands[] = {
-        {0, 0, 256, 1, 0.49, 0.49}, {0, 0, 192, 1, 0.44, 0.28}, {0, 0, 128, 1, 0.42, 0.36}, {0, 0, 128, 2, 0.62, 0.11},
-        {0, 0, 256, 2, 0.91, 0.70}, {0, 0, 192, 2, 0.77, 0.28},
+        {0, 0, 256, 1, 0.51, 0.54}, {0, 0, 192, 1, 0.47, 0.23}, {0, 0, 128, 1, 0.46, 0.37}, {0, 0, 128, 2, 0.64, 0.20},
+        {0, 0, 256, 2, 0.84, 1.14}, {0, 0, 192, 2, 0.79, 0.28},
         {2, 256, 0, 1, 1.18, 4.0}, {2, 128, 0, 1, 0.85, 1.5}, {1, 256, 0, 1, 1.0, 1.5}, {1, 128, 0, 1, 0.75, 1.5},
     };
     double best = 1e300;
