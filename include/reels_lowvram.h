@@ -93,7 +93,8 @@ int reels_lowvram_abi_version(void);
 
 /* The plan the q8 GEMM takes for D[M][Nout] over a reduction of Kred, for
  * diagnostics and tests; no device work.  info (7 entries):
- *   [0] kernel: 1 weight-in-TMEM, 0 both operands in shared memory
+ *   [0] kernel: 1 weight-in-TMEM, 2 weight-in-TMEM on CTA pairs (tiles of
+ *       256 output columns on two SMs), 0 both operands in shared memory
  *   [1] tokens per tile  [2] reduction elements per pipeline stage
  *   [3] reduction splits [4] pipeline stages per split
  *   [5] output-column tiles  [6] token tiles

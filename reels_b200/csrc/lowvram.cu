@@ -93,6 +93,32 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// The same with a cluster of `cx` CTAs along x (the CTA pairs of the
+// weight-in-TMEM kernel); the grid is a multiple of cx.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cx,
+                               Args... args) {
+    static const bool pdl = [] {
+        const char *e = getenv("REELS_NO_PDL");
+        return !(e && atoi(e) != 0);
+    }();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)cx;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ------------------------------------------------------------ device state
 constexpr int kMaxDevices = 64;
 struct DeviceState {
@@ -135,6 +161,19 @@ cudaError_t set_ts_attr() {
     return cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, TsGeom<BT, KB2>::SMEM_BYTES);
 }
+template <int DT, int BT, int KB2>
+cudaError_t set_ts_pair_attr() {
+    using G = TsGeom<BT, KB2, 1>;
+    cudaError_t e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE, 1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH, 1>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD, 1>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM_BYTES);
+}
+
 template <int DT>
 cudaError_t set_ts_attrs() {
     cudaError_t e;
@@ -143,7 +182,9 @@ cudaError_t set_ts_attrs() {
     if ((e = set_ts_attr<DT, 128, 1>()) != cudaSuccess) return e;
     if ((e = set_ts_attr<DT, 256, 2>()) != cudaSuccess) return e;
     if ((e = set_ts_attr<DT, 192, 2>()) != cudaSuccess) return e;
-    return set_ts_attr<DT, 128, 2>();
+    if ((e = set_ts_attr<DT, 128, 2>()) != cudaSuccess) return e;
+    if ((e = set_ts_pair_attr<DT, 256, 2>()) != cudaSuccess) return e;
+    return set_ts_pair_attr<DT, 128, 2>();
 }
 
 // The calling thread's current context is restored when an entry point
@@ -318,6 +359,7 @@ struct Q8Plan {
     int mt = 1, bn = 256;
     int ts = 0;         // > 0: weight-in-TMEM kernel, 128 output columns x ts tokens
     int ts_kb2 = 1;     // its pipeline stages cover 64 * ts_kb2 reduction elements
+    int pair = 0;       // 1: CTA pairs (cta_group::2), 256 output columns per tile
     int64_t ntiles = 1, mtiles = 1;
     Split split;
 };
@@ -334,6 +376,9 @@ struct Q8Plan {
 //   the stage width, so 128-wide stages move more weight per round trip; the
 //   256-token tiles' 128-wide stages also hand their activation atoms back
 //   one at a time (q8ts_gemm.cuh), which hides most of their refill.
+//   CTA pairs (256 output columns per tile on two SMs, 74 tiles in flight):
+//   bt 256: 0.80 + 1.05, bt 128: 0.62 + 0.30 (128-wide stages; the ratios
+//   to the single-CTA plans measured on one box, 3-7% and 2-5% faster).
 //   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
@@ -354,19 +399,30 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
         const int v = atoi(e);
         return (v == 256 || v == 192 || v == 128 || v == 2562 || v == 1922 || v == 1282) ? v : 0;
     }();
+    // REELS_Q8_PAIR: 1 runs the plans that have a CTA-pair variant on pairs,
+    // 0 never; unset, the model decides.
+    static const int pair_env = [] {
+        const char *e = getenv("REELS_Q8_PAIR");
+        return e ? (atoi(e) == 1 ? 1 : 0) : -1;
+    }();
     struct Cand {
         int mt, bn, ts, kb2;
         double per_kb, epi;  // per_kb: per pipeline stage (64 * kb2 reduction elements)
+        int pair;            // CTA pair: 256 output columns per tile on two SMs
     };
     const Cand cands[] = {
-        {0, 0, 256, 1, 0.51, 0.54}, {0, 0, 192, 1, 0.47, 0.23}, {0, 0, 128, 1, 0.46, 0.37}, {0, 0, 128, 2, 0.64, 0.20},
-        {0, 0, 256, 2, 0.84, 1.14}, {0, 0, 192, 2, 0.79, 0.28},
-        {2, 256, 0, 1, 1.18, 4.0}, {2, 128, 0, 1, 0.85, 1.5}, {1, 256, 0, 1, 1.0, 1.5}, {1, 128, 0, 1, 0.75, 1.5},
+        {0, 0, 256, 1, 0.51, 0.54, 0}, {0, 0, 192, 1, 0.47, 0.23, 0}, {0, 0, 128, 1, 0.46, 0.37, 0},
+        {0, 0, 128, 2, 0.64, 0.20, 0}, {0, 0, 256, 2, 0.84, 1.14, 0}, {0, 0, 192, 2, 0.79, 0.28, 0},
+        {0, 0, 256, 2, 0.80, 1.05, 1}, {0, 0, 128, 2, 0.62, 0.30, 1},
+        {2, 256, 0, 1, 1.18, 4.0, 0}, {2, 128, 0, 1, 0.85, 1.5, 0}, {1, 256, 0, 1, 1.0, 1.5, 0},
+        {1, 128, 0, 1, 0.75, 1.5, 0},
     };
     double best = 1e300;
     Q8Plan bestp;
     for (const Cand &cd : cands) {
         const int64_t kb = cdiv(Kred, BK * cd.kb2);
+        if (cd.pair && pair_env == 0) continue;
+        if (!cd.pair && cd.ts && pair_env == 1 && cd.kb2 == 2 && (cd.ts == 256 || cd.ts == 128)) continue;
         if (cd.ts) {
             if (!allow_ts || forced || forced_ts == 0) continue;
             if (forced_ts > 0 && forced_ts != cd.ts * 10 + cd.kb2 && forced_ts != cd.ts) continue;
@@ -376,7 +432,8 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
             if (forced && forced != cd.mt * 1000 + cd.bn) continue;
             if (!forced && cd.mt == 2 && M < 256) continue;
         }
-        const int64_t ntiles = cd.ts ? cdiv(Nout, 128) : cdiv(Nout, cd.bn);
+        const int64_t ntiles = cd.ts ? cdiv(Nout, cd.pair ? 256 : 128) : cdiv(Nout, cd.bn);
+        const int slots = cd.pair ? sms / 2 : sms;  // tiles in flight
         const int64_t mtiles = cd.ts ? cdiv(M, cd.ts) : cdiv(M, 128 * cd.mt);
         const int64_t tiles = ntiles * mtiles;
         for (int64_t want = 1; want <= std::max<int64_t>(1, kb / 4); want = want < 4 ? want + 1 : want * 2) {
@@ -384,7 +441,7 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
             sp.kb_per = (int)cdiv(kb, want);
             sp.splits = (int)cdiv(kb, sp.kb_per);
             if (want > 1 && sp.splits == 1) continue;
-            const double units = (double)cdiv(tiles * sp.splits, sms);
+            const double units = (double)cdiv(tiles * sp.splits, slots);
             // A fused activation lengthens the epilogue; with one accumulator
             // (256-token tiles) the MMAs wait for it.
             const double act_epi = act == ACT_NONE || sp.splits > 1 ? 0.0 : (cd.ts == 256 ? 1.5 : 0.1);
@@ -397,11 +454,12 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
                 bestp.bn = cd.ts ? 128 : cd.bn;
                 bestp.ts = cd.ts;
                 bestp.ts_kb2 = cd.kb2;
+                bestp.pair = cd.pair;
                 bestp.ntiles = ntiles;
                 bestp.mtiles = mtiles;
                 bestp.split = sp;
             }
-            if (tiles >= sms) break;  // enough tiles: never split
+            if (tiles >= slots) break;  // enough tiles: never split
         }
     }
     return bestp;
@@ -832,6 +890,22 @@ void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtens
         launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE>, dim3(grid), dim3(TS_THREADS), TsGeom<BT, KB2>::SMEM_BYTES,
                    st, tx, tw, te, tsc, to, tp, a);
 }
+template <int DT, int BT, int KB2>
+void launch_ts_pair_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw,
+                      const CUtensorMap &te, const CUtensorMap &tsc, const CUtensorMap &to, const CUtensorMap &tp,
+                      const TsArgs &a) {
+    using G = TsGeom<BT, KB2, 1>;
+    const int act = a.epi_partial ? ACT_NONE : a.epi_act;
+    if (act == ACT_GELU_TANH)
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH, 1>, grid, dim3(TS_THREADS), G::SMEM_BYTES, st,
+                           2, tx, tw, te, tsc, to, tp, a);
+    else if (act == ACT_GELU_TANH_GRAD)
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD, 1>, grid, dim3(TS_THREADS),
+                           G::SMEM_BYTES, st, 2, tx, tw, te, tsc, to, tp, a);
+    else
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE, 1>, grid, dim3(TS_THREADS), G::SMEM_BYTES, st, 2,
+                           tx, tw, te, tsc, to, tp, a);
+}
 
 // Profiling hook shared by both q8 launch paths: events around the GEMM.
 cudaEvent_t prof_begin(cudaStream_t st, const Q8Call &c) {
@@ -856,7 +930,8 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     const int bt = p.ts;
     const int sk = 64 * p.ts_kb2;  // reduction elements per pipeline stage
     CUtensorMap tx, tw, te, tsc, to, tp;
-    int rc = tmap_2d(&tx, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, bt,
+    // a CTA of a pair loads half of the token tile
+    int rc = tmap_2d(&tx, c.act, tma_act_type(dt), c.Kred, c.M, (uint64_t)c.Kred * 2, 64, p.pair ? bt / 2 : bt,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     const uint64_t w_inner = c.layout == REELS_W_OUT_CONTIGUOUS ? c.N_w : c.K_w;
@@ -950,10 +1025,19 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
         to = tx;
     }
     const int64_t total_tiles = p.ntiles * p.mtiles * p.split.splits;
-    const dim3 grid((unsigned)std::min<int64_t>(total_tiles, ds.sms));
+    const dim3 grid(p.pair ? 2u * (unsigned)std::min<int64_t>(total_tiles, ds.sms / 2)
+                           : (unsigned)std::min<int64_t>(total_tiles, ds.sms));
     cudaEvent_t ev_stop = prof_begin(st, c);
     const int key = (dt == REELS_BF16 ? 10000 : 0) + bt * 10 + p.ts_kb2;
-    switch (key) {
+    if (p.pair) {
+        switch (key) {
+            case 12562: launch_ts_pair_t<DT_BF16, 256, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+            case 11282: launch_ts_pair_t<DT_BF16, 128, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+            case 2562: launch_ts_pair_t<DT_F16, 256, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+            case 1282: launch_ts_pair_t<DT_F16, 128, 2>(grid, st, tx, tw, te, tsc, to, tp, a); break;
+            default: return fail("no CTA-pair variant of this tile plan");
+        }
+    } else switch (key) {
         case 12561: launch_ts_t<DT_BF16, 256, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
         case 11921: launch_ts_t<DT_BF16, 192, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
         case 11281: launch_ts_t<DT_BF16, 128, 1>(grid, st, tx, tw, te, tsc, to, tp, a); break;
@@ -1200,7 +1284,7 @@ int reels_q8_plan(int64_t M, int64_t Nout, int64_t Kred, int act, int sms, int64
     if (act != REELS_ACT_NONE && act != REELS_ACT_GELU_TANH) return fail("unknown activation");
     const Q8Plan p = plan_q8(M, Nout, Kred, sms > 0 ? sms : current_sms(), true,
                              act == REELS_ACT_NONE ? ACT_NONE : ACT_GELU_TANH);
-    info[0] = p.ts ? 1 : 0;
+    info[0] = p.ts ? (p.pair ? 2 : 1) : 0;
     info[1] = p.ts ? p.ts : 128 * p.mt;
     info[2] = p.ts ? 64 * p.ts_kb2 : BK;
     info[3] = p.split.splits;

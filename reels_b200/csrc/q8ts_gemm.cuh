@@ -68,7 +68,9 @@ __device__ unsigned long long g_ts_trace[256 * (TS_THREADS / 32) * 4];
 // TMEM (512 columns): NACC accumulators of BT columns and NA A-operand stages
 // of SK/2 columns.  BT = 256 leaves room for one accumulator only; BT <= 192
 // double-buffers it so the epilogue overlaps the next tile's MMAs.
-template <int BT, int KB2>
+// PAIR = 1: the tile is shared by a CTA pair (see the pair helpers above);
+// this CTA holds XT = BT/2 tokens of each activation atom.
+template <int BT, int KB2, int PAIR = 0>
 struct TsGeom {
     static constexpr int SK = 64 * KB2;
     static constexpr int NACC = BT == 256 ? 1 : 2;
@@ -83,13 +85,16 @@ struct TsGeom {
 #ifndef REELS_TS_S8
 #define REELS_TS_S8 0
 #endif
-    static constexpr int SX = REELS_TS_SX ? REELS_TS_SX
-                                          : (KB2 == 2 ? (BT == 128 ? 4 : 2) : (BT == 128 ? 6 : 4));
+    static constexpr int XT = PAIR ? BT / 2 : BT;  // tokens of the activation tile in this CTA
+    // A pair's half-height atoms leave room for a ring as deep as the TMEM stages.
+    static constexpr int SX = PAIR ? NA
+                                   : (REELS_TS_SX ? REELS_TS_SX
+                                                  : (KB2 == 2 ? (BT == 128 ? 4 : 2) : (BT == 128 ? 6 : 4)));
     static constexpr int S8 = REELS_TS_S8 ? REELS_TS_S8 : (KB2 == 2 ? 3 : (BT == 256 ? 6 : 8));
     // The activation ring holds SXA slots of one 64-wide atom (BT x 64
     // elements) each; stage ga reads atoms ga*KB2 .. ga*KB2 + KB2 - 1, atom ax
     // in slot ax % SXA.
-    static constexpr int XA_BYTES = BT * 128;
+    static constexpr int XA_BYTES = XT * 128;
     static constexpr int SXA = SX * KB2;
     // Atom release: with 128-wide stages on a double-buffered ring, a slot is
     // handed back as soon as the MMAs that read its atom are done (x_empty),
@@ -98,7 +103,7 @@ struct TsGeom {
     // always sits in an odd slot and is released by the stage's kb_empty
     // commit, so only the first atom costs an extra commit.  Deep rings (the
     // 128-token tiles) and 64-wide stages release whole stages through kb_empty.
-    static constexpr bool ATOM_REL = KB2 == 2 && BT != 128;
+    static constexpr bool ATOM_REL = !PAIR && KB2 == 2 && BT != 128;
     static constexpr bool LAST_VIA_KB = ATOM_REL && (SXA % KB2 == 0);
     static constexpr int SXS = SXA / KB2;  // whole stages in the ring (when released by kb_empty)
     static_assert(ATOM_REL || SXA == SX * KB2, "stage-level release needs stage-aligned atom slots");
@@ -239,6 +244,103 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr)
+        : "memory");
+}
+
+// ------------------------------------------------------------ CTA pairs
+// The pair variant (PAIR = 1) runs each tile on a cluster of two CTAs on
+// neighbouring SMs with tcgen05.mma.cta_group::2: one MMA covers both CTAs'
+// 128 weight rows (M = 256; each CTA's rows in its own TMEM) against the
+// token tile, whose first half lives in the leader's shared memory and the
+// second in the peer's.  Loads stay plain TMA loads into the issuing CTA's
+// own shared memory (no multicast); the .cta_group::2 form only lets their
+// completion count on the leader's barrier.  Commits go to both CTAs.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+// Arrive on a barrier of another CTA of the cluster.  The arrivals that use it
+// follow tcgen05.wait::st + tcgen05.fence::before_thread_sync (the TMEM
+// stores are complete) or tcgen05.ld completion, so the default CTA-scope
+// release suffices; a cluster-scope release would also order every earlier
+// global and shared write of the warp, and costs far more.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait that acquires at cluster scope (phases completed by the peer CTA).
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(REELS_SUSPEND_HINT_NS)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool wait_bar_cl(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned *err,
+                                            unsigned code) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait_cl(bar, parity)) return true;
+        if (*abort) return false;
+        if (clock64() - t0 > REELS_WAIT_LIMIT_CYCLES) {
+            *abort = 1;
+            if (err) atomicOr(err, code);
+            return false;
+        }
+    }
+}
+// Every thread of both CTAs.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc] over both CTAs of the pair, issued by the leader.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on `bar` in both CTAs of the pair when the pair MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+// TMA load into this CTA's shared memory whose completion counts on the
+// leader's mbarrier (`bar_leader`, a shared::cluster address from mapa).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tmap, int x, int y,
+                                                 uint32_t bar_leader) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_leader)
         : "memory");
 }
 
@@ -386,14 +488,16 @@ struct TsTile {
 
 // Tiles run output-column tile fastest, so the CTAs in flight share one
 // activation tile through L2 while the (small) weight stays resident there.
-template <int BT, int SK>
-__device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
+// With a CTA pair, a tile covers 256 output columns and `rank` picks this
+// CTA's 128 (ntiles then counts 256-column tiles).
+template <int BT, int SK, int PAIR = 0>
+__device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t, uint32_t rank = 0) {
     TsTile c;
     const int nt = t % a.ntiles;
     const int rest = t / a.ntiles;
     const int mt = rest % a.mtiles;
     c.sp = rest / a.mtiles;
-    c.n0 = nt * 128;
+    c.n0 = PAIR ? nt * 256 + 128 * (int)rank : nt * 128;
     c.m0 = mt * BT;
     c.kb0 = c.sp * a.kb_per_split;
     c.n_main = max(0, min(a.kb_total, c.kb0 + a.kb_per_split) - c.kb0);
@@ -401,13 +505,13 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t) {
     return c;
 }
 
-template <int DT, int BT, int KB2, int ACT>
+template <int DT, int BT, int KB2, int ACT, int PAIR = 0>
 __global__ void __launch_bounds__(TS_THREADS, 1)
     q8ts_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmS,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmP,
                      const TsArgs args) {
-    using G = TsGeom<BT, KB2>;
+    using G = TsGeom<BT, KB2, PAIR>;
     using E = Elem<DT>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -430,6 +534,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int total_tiles = args.ntiles * args.mtiles * args.splits;
+    // A pair walks the tiles together; the leader (rank 0) issues the MMAs and
+    // owns the barriers both CTAs' producers complete.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int t_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int t_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < G::S8; ++i) {
@@ -437,12 +547,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             mbar_init(&w_empty[i], TS_GW);
         }
         for (int i = 0; i < G::NA; ++i) {
-            mbar_init(&kb_full[i], 1 + TS_GW);  // activation TMA (expect_tx) + one dequant group
+            // activation TMA (expect_tx) + one dequant group (of each CTA of a pair)
+            mbar_init(&kb_full[i], 1 + (PAIR ? 2 : 1) * TS_GW);
             mbar_init(&kb_empty[i], 1);
         }
         for (int i = 0; i < G::NACC; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], TS_NEW);
+            mbar_init(&acc_empty[i], (PAIR ? 2 : 1) * TS_NEW);
         }
         mbar_init(mma_done, 1);
         for (int i = 0; i < TS_NEW; ++i) mbar_init(&pre_bar[i], 1);
@@ -459,15 +570,34 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         if (!args.epi_partial && args.epi_act != ACT_NONE && args.pre) tma_prefetch_desc(&tmP);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 512);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 512);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     griddep_wait();  // the previous kernel's outputs are complete from here on
     bool aborted_here = false;
+    // arrive on the leader's copy of a barrier (local for the leader)
+    auto arrive_leader = [&](uint64_t *bar) {
+        if (!PAIR || leader) mbar_arrive(bar);
+        else mbar_arrive_cluster(mapa_shared(smem_u32(bar), 0));
+    };
+    // MMA-side waits see the peer's arrivals at cluster scope
+    auto wait_mma = [&](uint64_t *bar, uint32_t parity, unsigned code) {
+        return PAIR ? wait_bar_cl(bar, parity, abort, args.err, code) : wait_bar(bar, parity, abort, args.err, code);
+    };
+    auto commit = [&](uint64_t *bar) {
+        if (PAIR) mma_commit_pair(bar);
+        else mma_commit(bar);
+    };
 #ifdef REELS_TS_TRACE
     unsigned long long tr_[4] = {0, 0, 0, 0};
     const long long tr_start = clock64();
@@ -480,8 +610,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         // One lane runs the loop: no warp-wide votes or syncs per stage.
         if (lane == 0) {
             uint32_t gx = 0;
-            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-                const TsTile c = ts_tile<BT, G::SK>(args, t);
+            for (int t = t_first; t < total_tiles && !aborted_here; t += t_step) {
+                const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
                 for (int it = 0; it < c.n_main + c.n_ext && !aborted_here; ++it, ++gx) {
                     uint64_t *full = &kb_full[gx % G::NA];
                     // main: KB2 K-major atoms of [BT tokens][64 K]; ext: rank atoms of
@@ -509,15 +639,21 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                             aborted_here = true;
                             break;
                         }
-                        if (a == 0) mbar_arrive_expect_tx(full, na * BT * 128);
+                        // the stage's bytes (both CTAs' halves for a pair) on the leader's barrier
+                        if (a == 0 && (!PAIR || leader)) mbar_arrive_expect_tx(full, na * BT * 128);
                         if (a >= na) continue;
                         uint8_t *dst = smem + G::X_OFF + slot * G::XA_BYTES;
+                        const int xm0 = c.m0 + (int)rank * G::XT;  // this CTA's tokens
+                        auto load = [&](void *d, const CUtensorMap *m, int x, int y) {
+                            if (PAIR) tma_load_2d_pair(d, m, x, y, mapa_shared(smem_u32(full), 0));
+                            else tma_load_2d(d, m, x, y, full);
+                        };
                         if (it < c.n_main) {
-                            tma_load_2d(dst, &tmX, (c.kb0 + it) * G::SK + 64 * a, c.m0, full);
+                            load(dst, &tmX, (c.kb0 + it) * G::SK + 64 * a, xm0);
                         } else {
 #pragma unroll
-                            for (int b = 0; b < BT / 64; ++b)
-                                tma_load_2d(dst + b * 8192, &tmE, c.m0 + 64 * b, G::SK * e + 64 * a, full);
+                            for (int b = 0; b < G::XT / 64; ++b)
+                                load(dst + b * 8192, &tmE, xm0 + 64 * b, G::SK * e + 64 * a);
                         }
                     }
                 }
@@ -529,8 +665,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         if (lane == 0) {
             uint32_t gw = 0;
             const uint32_t bytes = G::W_BYTES + (args.scale_mode == 2 ? G::SC_BYTES : 0);
-            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-                const TsTile c = ts_tile<BT, G::SK>(args, t);
+            for (int t = t_first; t < total_tiles && !aborted_here; t += t_step) {
+                const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
                 for (int it = 0; it < c.n_main; ++it, ++gw) {
                     const int s = gw % G::S8;
                     if (!TSW(0, wait_bar(&w_empty[s], ((gw / G::S8) & 1) ^ 1, abort, args.err,
@@ -555,19 +691,22 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         // commit (releasing the stage once they complete), then the wait for
         // the next stage: the tensor pipe keeps the queued work while the
         // thread waits, and no warp-wide vote or sync sits between stages.
-        if (lane == 0) {
+        if (lane == 0 && (!PAIR || leader)) {
             const int ab = (DT == DT_BF16) ? 1 : 0;
-            const uint32_t id_main = idesc_f16(ab, 0, 0, 128, BT);
-            const uint32_t id_ext = idesc_f16(ab, 0, 1, 128, BT);
+            const uint32_t id_main = idesc_f16(ab, 0, 0, PAIR ? 256 : 128, BT);
+            const uint32_t id_ext = idesc_f16(ab, 0, 1, PAIR ? 256 : 128, BT);
+            auto mma = [&](uint32_t d, uint32_t a_t, uint64_t b, uint32_t id, uint32_t acc) {
+                if (PAIR) mma_f16_ts_pair(d, a_t, b, id, acc);
+                else mma_f16_ts(d, a_t, b, id, acc);
+            };
             // Descriptors of X stage 0; a stage or K offset adds (bytes >> 4) to the address field.
             const uint64_t dmain0 = sdesc_sw128(sbase + G::X_OFF, 16, 1024);
             const uint64_t dext0 = sdesc_sw128(sbase + G::X_OFF, 8192, 1024);
             uint32_t ga = 0, local = 0;
-            for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
-                const TsTile c = ts_tile<BT, G::SK>(args, t);
+            for (int t = t_first; t < total_tiles && !aborted_here; t += t_step, ++local) {
+                const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
                 const int acc = local % G::NACC;
-                if (!TSW(0, wait_bar(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, abort, args.err,
-                                     DEVERR_TIMEOUT_ACC))) {
+                if (!TSW(0, wait_mma(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, DEVERR_TIMEOUT_ACC))) {
                     aborted_here = true;
                     break;
                 }
@@ -576,7 +715,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 const int n_iter = c.n_main + c.n_ext;
                 for (int it = 0; it < n_iter; ++it, ++ga) {
                     const int sa = ga % G::NA;
-                    if (!TSW(1, wait_bar(&kb_full[sa], (ga / G::NA) & 1, abort, args.err, DEVERR_TIMEOUT_AB_FULL))) {
+                    if (!TSW(1, wait_mma(&kb_full[sa], (ga / G::NA) & 1, DEVERR_TIMEOUT_AB_FULL))) {
                         aborted_here = true;
                         break;
                     }
@@ -593,27 +732,26 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     if (it < c.n_main) {
 #pragma unroll
                         for (int kk = 0; kk < 4 * KB2; ++kk) {
-                            mma_f16_ts(d_tm, a_tm + 8 * kk, dmain0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 32) >> 4),
-                                       id_main, (it > 0 || kk > 0) ? 1u : 0u);
+                            mma(d_tm, a_tm + 8 * kk, dmain0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 32) >> 4), id_main,
+                                (it > 0 || kk > 0) ? 1u : 0u);
                             if ((kk & 3) == 3) release(kk >> 2);  // this atom has been read
                         }
                     } else {
                         const int e = it - c.n_main;
                         const int nk = (min(G::SK, args.r - G::SK * e) + 15) / 16;
                         for (int kk = 0; kk < nk; ++kk)
-                            mma_f16_ts(d_tm, a_tm + 8 * kk,
-                                       dext0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 2048) >> 4), id_ext,
-                                       (it > 0 || kk > 0) ? 1u : 0u);
+                            mma(d_tm, a_tm + 8 * kk, dext0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 2048) >> 4),
+                                id_ext, (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                         for (int a = 0; a < KB2; ++a) release(a);
                     }
-                    mma_commit(&kb_empty[sa]);
+                    commit(&kb_empty[sa]);
                     TS_ADD(2, tr_issue);
                 }
                 if (aborted_here) break;
-                mma_commit(&acc_full[acc]);
+                commit(&acc_full[acc]);
             }
-            mma_commit(mma_done);
+            commit(mma_done);
         }
         __syncwarp();
     } else if (warp < 3 + TS_NDW) {
@@ -621,8 +759,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const int q = warp & 3;               // TMEM lane quarter
         const int g = (warp - 3) / TS_GW;     // group: reduction blocks with ga % TS_NG == g
         uint32_t ga = 0, gw = 0;
-        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x) {
-            const TsTile c = ts_tile<BT, G::SK>(args, t);
+        for (int t = t_first; t < total_tiles && !aborted_here; t += t_step) {
+            const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
             // Per-lane scales (lanes 32q + 8i + t/4) for SMODE 1.
             float lane_s[4] = {0.f, 0.f, 0.f, 0.f};
             if (args.scale_mode == 1) {
@@ -708,7 +846,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&kb_full[sa]);
+                if (lane == 0) arrive_leader(&kb_full[sa]);
                 TS_ADD(2, tr_work);
             }
         }
@@ -748,8 +886,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             }
             pre_pending = true;
         };
-        for (int t = blockIdx.x; t < total_tiles && !aborted_here; t += gridDim.x, ++local) {
-            const TsTile c = ts_tile<BT, G::SK>(args, t);
+        for (int t = t_first; t < total_tiles && !aborted_here; t += t_step, ++local) {
+            const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
             const int acc = local % G::NACC;
             if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) {
                 if (lane == 0)
@@ -776,7 +914,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     if (ch == NCH - 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                        if (lane == 0) arrive_leader(&acc_empty[acc]);
                     }
                     const int m_base = c.m0 + j0;
                     float *dst = args.partial + ((long long)c.sp * args.M + m_base) * args.Nout + n;
@@ -811,7 +949,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     // all of this warp's accumulator columns are in registers
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+                    if (lane == 0) arrive_leader(&acc_empty[acc]);
                 }
                 const int m_base = c.m0 + j0;
                 const bool rows_ok = m_base < args.M;  // rows past M are clipped by the TMA unit
@@ -920,7 +1058,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             }
         }
         __syncwarp();
-        tmem_dealloc(tmem, 512);
+    }
+    // A pair's CTAs read each other's shared memory (the MMA) and barriers
+    // (remote arrivals): neither leaves before both are done.
+    if (PAIR) cluster_sync_all();
+    if (warp == 1) {
+        if (PAIR) tmem_dealloc_pair(tmem, 512);
+        else tmem_dealloc(tmem, 512);
     }
 }
 

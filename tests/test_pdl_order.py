@@ -1,7 +1,7 @@
 """Static check of the programmatic-dependent-launch rule (CPU, no device).
 
-Kernels launched with programmatic stream serialization (`launch_pdl` in
-reels_b200/csrc/lowvram.cu) may be scheduled before the kernel ahead of them
+Kernels launched with programmatic stream serialization (`launch_pdl` and
+`launch_pdl_cluster` in reels_b200/csrc/lowvram.cu) may be scheduled before the kernel ahead of them
 in the stream has finished.  Each must therefore execute
 `griddepcontrol.wait` (griddep_wait) before touching global memory, and must
 execute it on every path: a kernel whose CTAs could all exit without waiting
@@ -44,7 +44,7 @@ def _kernel_body(src, name):
 def test_every_pdl_kernel_waits_before_anything_else():
     srcs = _sources()
     launcher = srcs["lowvram.cu"]
-    names = set(re.findall(r"launch_pdl\(\s*([A-Za-z_][A-Za-z_0-9]*)", launcher))
+    names = set(re.findall(r"launch_pdl(?:_cluster)?\(\s*([A-Za-z_][A-Za-z_0-9]*)", launcher))
     names -= {"kern", "void"}
     assert names, "no launch_pdl call sites found"
     checked = 0

@@ -39,14 +39,15 @@ def test_bench_shapes_take_the_256_token_tmem_tiles(lib):
     for M, K, N in [(32760, 1536, 1536), (32760, 1536, 8960), (32760, 8960, 1536)]:
         for Nout, Kred in ((N, K), (K, N)):
             p = q8(lib, M, Nout, Kred)
-            assert p["kernel"] == 1 and p["tokens"] == 256 and p["splits"] == 1, (M, Nout, Kred, p)
-            assert p["ntiles"] == -(-Nout // 128) and p["mtiles"] == -(-M // 256)
+            assert p["kernel"] in (1, 2) and p["tokens"] == 256 and p["splits"] == 1, (M, Nout, Kred, p)
+            cols = 256 if p["kernel"] == 2 else 128  # a CTA pair covers 256 output columns
+            assert p["ntiles"] == -(-Nout // cols) and p["mtiles"] == -(-M // 256)
 
 
 def test_small_token_counts_take_the_wide_stage_tiles(lib):
     # the Wan 2.1 14B FFN up-projection at 128 tokens: one 128-token tile, 128-wide stages
     p = q8(lib, 128, 13824, 5120)
-    assert p["kernel"] == 1 and p["tokens"] == 128 and p["stage"] == 128
+    assert p["kernel"] in (1, 2) and p["tokens"] == 128 and p["stage"] == 128
     assert p["splits"] * p["kb_per"] * p["stage"] >= 5120  # the splits cover the reduction
 
 
