@@ -26,6 +26,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volati
 // the epilogue of one unit overlaps the MMAs of the next: the pipeline fill
 // and the epilogue are paid once per CTA, not once per tile.
 constexpr int SK_THREADS = 192;  // warp0 TMA, warp1 MMA, warps 2..5 epilogue
+// The activation (or dy) tile SK_PF stages ahead of each TMA load is
+// prefetched into L2: more DRAM requests in flight per SM than the shared-
+// memory ring holds.  8 measured ~1.5% faster on the block step than none
+// (4: no change).
+constexpr int SK_PF = 8;
 constexpr int SK_A_BYTES = 128 * 128;
 constexpr int SK_MAX_STAGES = 8;
 // Ring buffer for the stages; the stage count is chosen per launch from the
@@ -148,6 +153,16 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
                         tma_load_2d(a_dst, &tmA, kb * BK, w.row0, &full[s]);
                     }
                     tma_load_2d(b_dst, &tmB, kb * BK, 0, &full[s]);
+                    if (SK_PF > 0 && it + SK_PF < w.n_iter) {
+                        // the activation block SK_PF stages ahead, into L2 only
+                        const int kp = kb + SK_PF;
+                        if (args.a_mn) {
+                            tma_prefetch_l2_2d(&tmA, w.row0, kp * BK);
+                            tma_prefetch_l2_2d(&tmA, w.row0 + 64, kp * BK);
+                        } else {
+                            tma_prefetch_l2_2d(&tmA, kp * BK, w.row0);
+                        }
+                    }
                 }
             }
         }
@@ -399,6 +414,16 @@ __global__ void __launch_bounds__(SK_THREADS, 1)
                     tma_load_2d(st + DU_DY_BYTES + bbox, &tmB, nt * 128 + 64, 0, &full[s]);
                     tma_load_2d(st + DU_DY_BYTES + 2 * bbox, &tmT, t * 128, 0, &full[s]);
                     tma_load_2d(st + DU_DY_BYTES + 3 * bbox, &tmT, t * 128 + 64, 0, &full[s]);
+                    if (SK_PF > 0) {
+                        // the dy tile SK_PF stages ahead, into L2 only
+                        const int kn = tn1 - tn0;
+                        const int f = (t - tm0) * kn + (nt - tn0) + SK_PF;
+                        const int tp = tm0 + f / kn, np = tn0 + f % kn;
+                        if (tp < tm1) {
+                            tma_prefetch_l2_2d(&tmDy, np * 128, tp * 128);
+                            tma_prefetch_l2_2d(&tmDy, np * 128 + 64, tp * 128);
+                        }
+                    }
                 }
             }
         }
