@@ -30,6 +30,14 @@
 // 3..10 dequant (two groups of four, one warp per TMEM lane quarter; the
 //          groups take alternate reduction blocks so two are in flight),
 // 11..18 epilogue (two per lane quarter, half of the tile's tokens each).
+//
+// Rings: the activation ring is a ring of 64-wide atoms (released per atom on
+// the double-buffered rings of single-CTA 128-wide stages), the int8 ring is
+// shared by the two dequant groups (a group waits for the slot's previous use
+// to be released before waiting for its load), and NA TMEM stages hold the
+// dequantised weight.  PAIR = 1 runs each tile on a cluster of two CTAs
+// (tcgen05.mma.cta_group::2): 256 weight rows per MMA, each CTA's 128 in its
+// own TMEM, each CTA holding half of the token tile; see the pair helpers.
 #pragma once
 #include "act.cuh"
 #include "q8_gemm.cuh"
