@@ -1,8 +1,9 @@
 """GPU parity of q8 GEMM plans the planner does not pick for these shapes by
 itself: the SMEM x SMEM kernel (REELS_Q8_TS=0, the plan for reduction scales
-that are not 16-byte aligned) and each token tile of the
-weight-in-TMEM kernel (REELS_Q8_TS=256/192/128, and 1282 for 128-token tiles
-with 128-wide pipeline stages).  The overrides are read once
+that are not 16-byte aligned), each token tile of the weight-in-TMEM kernel
+(REELS_Q8_TS=256/192/128, and 1282 for 128-token tiles with 128-wide
+pipeline stages), and the single-CTA forms of the plans the planner runs on
+CTA pairs (REELS_Q8_PAIR=0).  The overrides are read once
 per process, so each plan runs its cases in a child process."""
 import json
 import os
@@ -43,13 +44,15 @@ CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1
 
 
 @pytest.mark.parametrize("var,val", [("REELS_Q8_TS", "0"), ("REELS_Q8_TS", "256"),
-                                     ("REELS_Q8_TS", "192"), ("REELS_Q8_TS", "128"), ("REELS_Q8_TS", "1282")])
+                                     ("REELS_Q8_TS", "192"), ("REELS_Q8_TS", "128"), ("REELS_Q8_TS", "1282"),
+                                     ("REELS_Q8_PAIR", "0")])
 def test_forced_plan_parity(var, val):
     from reels_b200 import build
     build.build()
     env = dict(os.environ)
     env.pop("REELS_Q8_TILE", None)
     env.pop("REELS_Q8_TS", None)
+    env.pop("REELS_Q8_PAIR", None)
     env[var] = val
     code = CHILD.format(root=ROOT, tests=os.path.join(ROOT, "tests"), cases=CASES)
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
