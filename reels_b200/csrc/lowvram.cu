@@ -1863,6 +1863,21 @@ int reels_layernorm_modulate(const void *x, int64_t M, int64_t K, int64_t tokens
     rc = bind_device(x, &ds, scope);
     if (rc) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // one row per warp on the 16-byte path (no LayerNorm affine)
+    const bool warp_rows = dt != REELS_F32 && (K & 7) == 0 && !ln_weight && !ln_bias &&
+                           ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                             reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift)) & 15) == 0;
+    if (warp_rows) {
+        const dim3 wg((unsigned)std::min<int64_t>(cdiv(M, LN_THREADS / 32), 16LL * ds->sms));
+        if (dt == REELS_BF16)
+            launch_pdl(ln_modulate_warp_kernel<DT_BF16>, wg, dim3(LN_THREADS), 0, st, x, M, K, tokens_per_sample,
+                       scale, shift, epsilon, out);
+        else
+            launch_pdl(ln_modulate_warp_kernel<DT_F16>, wg, dim3(LN_THREADS), 0, st, x, M, K, tokens_per_sample,
+                       scale, shift, epsilon, out);
+        REELS_LAUNCHED();
+        return ok(REELS_PATH_CUDACORE);
+    }
     const dim3 grid((unsigned)std::min<int64_t>(M, 16LL * ds->sms));
     const size_t smem = (size_t)K * 4;
     if (dt == REELS_BF16)
@@ -1915,7 +1930,17 @@ int reels_layernorm_modulate_backward(const void *x, const void *dout, int64_t M
     const size_t smem = (size_t)K * 8;
     // dx, and the row statistics the parameter reduction reads
     void *dxo = dx;
-    if (dt == REELS_BF16)
+    const bool warp_rows = dt != REELS_F32 && (K & 7) == 0 && !ln_weight &&
+                           ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dout) |
+                             reinterpret_cast<uintptr_t>(dx) | reinterpret_cast<uintptr_t>(scale)) & 15) == 0;
+    const dim3 wg((unsigned)std::min<int64_t>(cdiv(M, LN_THREADS / 32), 16LL * ds->sms));
+    if (warp_rows && dt == REELS_BF16)
+        launch_pdl(ln_modulate_bwd_warp_kernel<DT_BF16>, wg, dim3(LN_THREADS), 0, st, x, dout, M, K,
+                   tokens_per_sample, scale, epsilon, dxo, stats);
+    else if (warp_rows)
+        launch_pdl(ln_modulate_bwd_warp_kernel<DT_F16>, wg, dim3(LN_THREADS), 0, st, x, dout, M, K,
+                   tokens_per_sample, scale, epsilon, dxo, stats);
+    else if (dt == REELS_BF16)
         launch_pdl(ln_modulate_bwd_kernel<DT_BF16>, grid, dim3(LN_THREADS), smem, st, x, dout, M, K,
                    tokens_per_sample, scale, ln_weight, epsilon, dxo, stats);
     else if (dt == REELS_F16)

@@ -25,7 +25,7 @@ namespace reels {
 
 constexpr int LN_THREADS = 256;
 constexpr int64_t LN_MAX_K = 16384;  // the row (x, and g in the backward) is staged in shared memory
-constexpr int LN_COL_ROWS = 512;  // rows per block of the parameter-gradient reduction
+constexpr int LN_COL_ROWS = 128;  // rows per block of the parameter-gradient reduction
 
 // Block-wide fp32 sum in a fixed order (warp shuffles, then warp totals).
 __device__ __forceinline__ float ln_block_sum(float v, float *red) {
@@ -163,6 +163,162 @@ __global__ void __launch_bounds__(LN_THREADS) ln_modulate_kernel(const void *x, 
     }
 }
 
+// ------------------------------------------------------------ one row per warp
+// The 16-byte path (16-bit types, K % 8 == 0, 16-byte aligned rows, no
+// LayerNorm affine) runs one row per warp: sums are warp shuffles in a fixed
+// order, nothing waits on a block barrier, and a CTA keeps eight rows in
+// flight.  The row is read from DRAM once; its second and third passes hit
+// L2 (or L1).  Each element takes the same single-rounded operation
+// sequence as the block kernels; the sums run in another fixed order.
+__device__ __forceinline__ float warp_sum_fixed(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// (mean, d) of row xr (K / 8 16-byte chunks), lane-strided chunks.
+template <int DT>
+__device__ __forceinline__ float2 ln_warp_stats(const uint4 *xr, int64_t nv, int64_t K, float eps, int lane) {
+    float s = 0.0f;
+    for (int64_t v = lane; v < nv; v += 32) {
+        const uint4 w = xr[v];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float a, b;
+            unpack2<DT>(ws[h], a, b);
+            s = __fadd_rn(__fadd_rn(s, a), b);
+        }
+    }
+    const float mean = __fdiv_rn(warp_sum_fixed(s), (float)K);
+    float q = 0.0f;
+    for (int64_t v = lane; v < nv; v += 32) {
+        const uint4 w = xr[v];
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float a, b;
+            unpack2<DT>(ws[h], a, b);
+            const float ca = __fsub_rn(a, mean), cb = __fsub_rn(b, mean);
+            q = __fadd_rn(__fadd_rn(q, __fmul_rn(ca, ca)), __fmul_rn(cb, cb));
+        }
+    }
+    const float var = __fdiv_rn(warp_sum_fixed(q), (float)K);
+    return make_float2(mean, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+template <int DT>
+__global__ void __launch_bounds__(LN_THREADS) ln_modulate_warp_kernel(const void *x, int64_t M, int64_t K,
+                                                                      int64_t tps, const void *scale,
+                                                                      const void *shift, float eps, void *out) {
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t nv = K / 8;
+    for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += nw) {
+        const uint4 *xr = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + m * K);
+        const float2 st = ln_warp_stats<DT>(xr, nv, K, eps, lane);
+        const int64_t b = m / tps;
+        const uint4 *sc = scale ? reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(scale) + b * K) : nullptr;
+        const uint4 *sh = shift ? reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(shift) + b * K) : nullptr;
+        uint4 *o = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) + m * K);
+        for (int64_t v = lane; v < nv; v += 32) {
+            const uint4 w = xr[v];
+            const uint4 sw = sc ? sc[v] : make_uint4(0, 0, 0, 0), hw = sh ? sh[v] : make_uint4(0, 0, 0, 0);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w}, sws[4] = {sw.x, sw.y, sw.z, sw.w},
+                           hws[4] = {hw.x, hw.y, hw.z, hw.w};
+            uint32_t ow[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float xv[2], fs[2], fh[2], f[2];
+                unpack2<DT>(ws[h], xv[0], xv[1]);
+                unpack2<DT>(sws[h], fs[0], fs[1]);
+                unpack2<DT>(hws[h], fh[0], fh[1]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float vv = round_act<DT>(__fdiv_rn(__fsub_rn(xv[e], st.x), st.y));
+                    if (sc) vv = __fmul_rn(vv, __fadd_rn(1.0f, fs[e]));
+                    if (sh) vv = __fadd_rn(vv, fh[e]);
+                    f[e] = vv;
+                }
+                ow[h] = Elem<DT>::pack2(f[0], f[1]);
+            }
+            o[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+    }
+}
+
+// dx per row, one row per warp (the 16-byte path, no LayerNorm weight);
+// also the row's (mean, d) for the parameter reduction.  g is recomputed from
+// dout in the last pass instead of being kept.
+template <int DT>
+__global__ void __launch_bounds__(LN_THREADS) ln_modulate_bwd_warp_kernel(const void *x, const void *dout, int64_t M,
+                                                                          int64_t K, int64_t tps, const void *scale,
+                                                                          float eps, void *dx, float2 *stats) {
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t nv = K / 8;
+    for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < M; m += nw) {
+        const uint4 *xr = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + m * K);
+        const uint4 *dr = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(dout) + m * K);
+        const float2 st = ln_warp_stats<DT>(xr, nv, K, eps, lane);
+        if (lane == 0 && stats) stats[m] = st;
+        const int64_t b = m / tps;
+        const uint4 *sc = scale ? reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(scale) + b * K) : nullptr;
+        // g (the modulation's pullback, rounded) and yhat of 8 elements
+        auto load8 = [&](int64_t v, float (&g)[8], float (&yh)[8]) {
+            const uint4 w = xr[v], dw = dr[v];
+            const uint4 sw = sc ? sc[v] : make_uint4(0, 0, 0, 0);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w}, dws[4] = {dw.x, dw.y, dw.z, dw.w},
+                           sws[4] = {sw.x, sw.y, sw.z, sw.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float xv[2], dv[2], sv[2];
+                unpack2<DT>(ws[h], xv[0], xv[1]);
+                unpack2<DT>(dws[h], dv[0], dv[1]);
+                unpack2<DT>(sws[h], sv[0], sv[1]);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float gg = dv[e];
+                    if (sc) gg = round_act<DT>(__fmul_rn(gg, __fadd_rn(1.0f, sv[e])));
+                    g[2 * h + e] = gg;
+                    yh[2 * h + e] = __fdiv_rn(__fsub_rn(xv[e], st.x), st.y);
+                }
+            }
+        };
+        float s1 = 0.0f, s2 = 0.0f;
+        for (int64_t v = lane; v < nv; v += 32) {
+            float g[8], yh[8];
+            load8(v, g, yh);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                s1 = __fadd_rn(s1, g[e]);
+                s2 = __fadd_rn(s2, __fmul_rn(g[e], yh[e]));
+            }
+        }
+        const float mg = __fdiv_rn(warp_sum_fixed(s1), (float)K);
+        const float mgy = __fdiv_rn(warp_sum_fixed(s2), (float)K);
+        uint4 *o = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(dx) + m * K);
+        for (int64_t v = lane; v < nv; v += 32) {
+            float g[8], yh[8];
+            load8(v, g, yh);
+            uint32_t ow[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float f[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const float t = __fsub_rn(__fsub_rn(g[2 * h + e], mg), __fmul_rn(yh[2 * h + e], mgy));
+                    f[e] = __fdiv_rn(t, st.y);
+                }
+                ow[h] = Elem<DT>::pack2(f[0], f[1]);
+            }
+            o[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+    }
+}
+
 // dx per row; also the row's (mean, d) for the parameter reduction.
 template <int DT>
 __global__ void __launch_bounds__(LN_THREADS) ln_modulate_bwd_kernel(const void *x, const void *dout, int64_t M,
@@ -216,6 +372,7 @@ __global__ void __launch_bounds__(LN_THREADS) ln_param_partial_kernel(const void
     const int64_t m0 = b * tps + c * LN_COL_ROWS, m1 = min(min(m0 + LN_COL_ROWS, (b + 1) * tps), M);
     if (k >= K) return;
     float ds = 0.0f, dh = 0.0f;
+#pragma unroll 4
     for (int64_t m = m0; m < m1; ++m) {
         const float2 st = __ldcg(&stats[m]);
         const float g = Elem<DT>::to_f(reinterpret_cast<const T *>(dout)[m * K + k]);

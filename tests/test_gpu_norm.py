@@ -29,6 +29,7 @@ CASES = [  # (M, K, tokens_per_sample, dtype, modulate, ln affine)
     (257, 1000, 100, "f16", True, False),
     (64, 4096, 64, "f32", False, True),
     (128, 24, 32, "bf16", True, True),
+    (512, 5120, 256, "bf16", False, False),  # one row per warp, no modulation
 ]
 
 
