@@ -880,10 +880,9 @@ def mode_gemm(args):
 def mode_norm(args):
     """The fused LayerNorm + modulation (forward, and the pullback with the
     modulation's parameter gradients) against PyTorch evaluating the same
-    expression as separate kernels, the way the reference's broadcasts do.
-    Bandwidth counts one read of x and one write of the output (forward), and
-    reads of x and dout, the write of dx and the parameter pass's second read
-    of x and dout (backward)."""
+    expression as separate kernels, the way the reference's broadcasts do;
+    and the gated residual with its pullback.  Bandwidth counts the arrays
+    each pass moves (see below)."""
     import torch
     from reels_b200 import build as native_build
     native_build.build()
@@ -911,17 +910,37 @@ def mode_norm(args):
         ln = (c / torch.sqrt(var + 1e-6)).to(dt)
         (ln.float() * (1 + scale.float()) + shift.float()).to(dt)
 
+    # the gated residual round(x + round(y * gate)) (transformer.jl:272,293)
+    # and its pullback (dy = round(dout * gate), dgate = sum dout * y)
+    from reels_b200.lowvram import gated_residual, gated_residual_backward
+    yres = torch.randn(M, K, device=dev).to(dt)
+    gate = (0.1 * torch.randn(1, K, device=dev)).to(dt)
+    res_out = torch.empty_like(x)
+
+    def residual():
+        gated_residual(x, yres, gate, out=res_out)
+
+    def residual_bwd():
+        gated_residual_backward(dout, yres, gate)
+
     best = _best_of_rounds(torch, dev, [("fused_fwd", fused), ("torch_fwd", torch_fwd),
-                                        ("fused_bwd_with_param_grads", fused_bwd)], args.reps)
+                                        ("fused_bwd_with_param_grads", fused_bwd),
+                                        ("gated_residual_fwd", residual),
+                                        ("gated_residual_bwd_with_gate_grad", residual_bwd)], args.reps)
     hbm = float(load_peaks()[0]["hbm_gbs"])
     e = 2
     out = {"M": M, "K": K, "dtype": args.dtype}
     for name, us in best.items():
         out[name] = {"us": round(us, 1)}
-    gb = 2 * M * K * e / (best["fused_fwd"] * 1e-6) / 1e9
-    out["fused_fwd"].update(gbs=round(gb, 1), hbm_frac=round(gb / hbm, 3))
-    gbb = 5 * M * K * e / (best["fused_bwd_with_param_grads"] * 1e-6) / 1e9
-    out["fused_bwd_with_param_grads"].update(gbs=round(gbb, 1), hbm_frac=round(gbb / hbm, 3))
+    # bytes moved per pass, in units of M*K elements: LayerNorm forward reads
+    # x and writes out (2); its backward reads x and dout, writes dx, and reads
+    # x and dout again for the parameter sums (5); the gated residual reads x
+    # and y and writes out (3); its pullback reads dout, writes dy, and reads
+    # dout and y again for dgate (4)
+    for name, arrays in (("fused_fwd", 2), ("fused_bwd_with_param_grads", 5), ("gated_residual_fwd", 3),
+                         ("gated_residual_bwd_with_gate_grad", 4)):
+        gb = arrays * M * K * e / (best[name] * 1e-6) / 1e9
+        out[name].update(gbs=round(gb, 1), hbm_frac=round(gb / hbm, 3))
     print(json.dumps(out), flush=True)
 
 
