@@ -379,12 +379,28 @@ struct Q8Plan {
 //   CTA pairs (256 output columns per tile on two SMs, 74 tiles in flight):
 //   bt 256: 0.80 + 1.05, bt 128: 0.62 + 0.30 (128-wide stages; the ratios
 //   to the single-CTA plans measured on one box, 3-7% and 2-5% faster).
+//   128-token tiles with 128-wide stages whose launch gives each CTA one
+//   unit run two MMA issuers: per stage x0.89 single, x0.98 on pairs.
 //   SMEM x SMEM kernel (q8_gemm.cuh), 128*mt tokens x bn output columns:
 //       2x256: 1.18 + 4.0, 2x128: 0.85, 1x256: 1.0, 1x128: 0.75 (+ 1.5).
 // The kernels are persistent, so a CTA runs ceil(work units / SMs) units; a
 // split reduction adds the write and re-read of fp32 partials (~5 TB/s).
 // REELS_Q8_TILE ("MTxBN") and REELS_Q8_TS (256, 192, 128; 2562,
 // 1922, 1282 for 128-wide stages; 0 for off) force a plan for measurements.
+// Two MMA issuers on 128-token tiles (q8ts_gemm.cuh) when each CTA (or CTA
+// pair) runs a single work unit.  REELS_Q8_ISS2=0 turns them off.
+bool q8_iss2_env_on() {
+    static const int env = [] {
+        const char *e = getenv("REELS_Q8_ISS2");
+        return e ? atoi(e) : 1;
+    }();
+    return env != 0;
+}
+bool q8_iss2_ok(const Q8Plan &p, int sms) {
+    const int64_t units = p.ntiles * p.mtiles * p.split.splits;
+    return q8_iss2_env_on() && p.ts == 128 && units <= (p.pair ? sms / 2 : sms);
+}
+
 Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, int act) {
     static const int forced = [] {
         const char *e = getenv("REELS_Q8_TILE");  // "MTxBN" (e.g. "2x128")
@@ -445,7 +461,11 @@ Q8Plan plan_q8(int64_t M, int64_t Nout, int64_t Kred, int sms, bool allow_ts, in
             // A fused activation lengthens the epilogue; with one accumulator
             // (256-token tiles) the MMAs wait for it.
             const double act_epi = act == ACT_NONE || sp.splits > 1 ? 0.0 : (cd.ts == 256 ? 1.5 : 0.1);
-            double cost = units * (sp.kb_per * cd.per_kb + cd.epi + act_epi);
+            // 128-token tiles with 128-wide stages, one unit per CTA: two MMA
+            // issuers (fwd / dX at 128 x 5120 x 13824: 11% faster single, 2% on pairs)
+            double per_kb = cd.per_kb;
+            if (cd.ts == 128 && cd.kb2 == 2 && units == 1.0 && q8_iss2_env_on()) per_kb *= cd.pair ? 0.98 : 0.89;
+            double cost = units * (sp.kb_per * per_kb + cd.epi + act_epi);
             if (sp.splits > 1) cost += 2.0 * sp.splits * (double)M * (double)Nout * 4.0 / 5.0e6 + 3.0;
             if (cost < best * 0.999) {
                 best = cost;
@@ -879,16 +899,17 @@ void launch_ts_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtens
                  const CUtensorMap &tsc, const CUtensorMap &to, const CUtensorMap &tp, const TsArgs &a) {
     // The activation variant only when the kernel writes the output itself
     // (split partials leave the activation to the reduce).
+    using G = TsGeom<BT, KB2>;
     const int act = a.epi_partial ? ACT_NONE : a.epi_act;
     if (act == ACT_GELU_TANH)
-        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH>, dim3(grid), dim3(TS_THREADS),
-                   TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, tp, a);
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH>, dim3(grid), dim3(G::THREADS), G::SMEM_BYTES, st, tx,
+                   tw, te, tsc, to, tp, a);
     else if (act == ACT_GELU_TANH_GRAD)
-        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD>, dim3(grid), dim3(TS_THREADS),
-                   TsGeom<BT, KB2>::SMEM_BYTES, st, tx, tw, te, tsc, to, tp, a);
-    else
-        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE>, dim3(grid), dim3(TS_THREADS), TsGeom<BT, KB2>::SMEM_BYTES,
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD>, dim3(grid), dim3(G::THREADS), G::SMEM_BYTES,
                    st, tx, tw, te, tsc, to, tp, a);
+    else
+        launch_pdl(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE>, dim3(grid), dim3(G::THREADS), G::SMEM_BYTES, st, tx, tw,
+                   te, tsc, to, tp, a);
 }
 template <int DT, int BT, int KB2>
 void launch_ts_pair_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const CUtensorMap &tw,
@@ -897,13 +918,13 @@ void launch_ts_pair_t(dim3 grid, cudaStream_t st, const CUtensorMap &tx, const C
     using G = TsGeom<BT, KB2, 1>;
     const int act = a.epi_partial ? ACT_NONE : a.epi_act;
     if (act == ACT_GELU_TANH)
-        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH, 1>, grid, dim3(TS_THREADS), G::SMEM_BYTES, st,
-                           2, tx, tw, te, tsc, to, tp, a);
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH, 1>, grid, dim3(G::THREADS), G::SMEM_BYTES,
+                           st, 2, tx, tw, te, tsc, to, tp, a);
     else if (act == ACT_GELU_TANH_GRAD)
-        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD, 1>, grid, dim3(TS_THREADS),
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_GELU_TANH_GRAD, 1>, grid, dim3(G::THREADS),
                            G::SMEM_BYTES, st, 2, tx, tw, te, tsc, to, tp, a);
     else
-        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE, 1>, grid, dim3(TS_THREADS), G::SMEM_BYTES, st, 2,
+        launch_pdl_cluster(q8ts_gemm_kernel<DT, BT, KB2, ACT_NONE, 1>, grid, dim3(G::THREADS), G::SMEM_BYTES, st, 2,
                            tx, tw, te, tsc, to, tp, a);
 }
 
@@ -1010,6 +1031,16 @@ int run_q8_ts(const Q8Call &c, int dt, const DeviceState &ds, char *ws_base, con
     a.err = ds.status;
     a.epi_act = c.epi_act;
     a.pre = c.pre;
+    {
+        // 128-token tiles: a second MMA issuer (q8ts_gemm.cuh), when every CTA
+        // runs one work unit (with more, the two accumulators serve to overlap
+        // a tile's epilogue with the next tile's MMAs) and every unit has two
+        // stages or more (each issuer's accumulator gets at least one).
+        // REELS_Q8_ISS2=0 keeps one issuer (for measurements).
+        const int n_ext = c.r > 0 ? (int)cdiv(c.r, sk) : 0;
+        const int last_main = a.kb_total - a.kb_per_split * (a.splits - 1);
+        a.iss2 = (bt == 128 && q8_iss2_ok(p, ds.sms) && a.kb_per_split >= 2 && last_main + n_ext >= 2) ? 1 : 0;
+    }
     tp = tx;
     if (!a.epi_partial) {
         // D tiles of 32 columns x 32 tokens, stored from the epilogue's staging.

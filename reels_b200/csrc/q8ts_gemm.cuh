@@ -29,7 +29,10 @@
 // Warp roles: 0 activation TMA, 1 MMA issue, 2 int8 (+ scale) TMA,
 // 3..10 dequant (two groups of four, one warp per TMEM lane quarter; the
 //          groups take alternate reduction blocks so two are in flight),
-// 11..18 epilogue (two per lane quarter, half of the tile's tokens each).
+// 11..18 epilogue (two per lane quarter, half of the tile's tokens each),
+// 19 (128-token tiles only) a second MMA issuer, used when each CTA runs one
+//          work unit: the two issuers take alternate stages into the two
+//          accumulators, which the epilogue adds.
 //
 // Rings: the activation ring is a ring of 64-wide atoms (released per atom on
 // the double-buffered rings of single-CTA 128-wide stages), the int8 ring is
@@ -128,6 +131,15 @@ struct TsGeom {
     static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
     static_assert(SMEM_BYTES <= 232448, "shared memory plan exceeds 227 KB");
     static_assert(NACC * BT + NA * ACOLS <= 512, "TMEM plan exceeds 512 columns");
+    // Second MMA issuer (128-token tiles, TsArgs::iss2).  One thread issues an
+    // N = 128 MMA every ~85 cycles against 64 of tensor work, and two threads
+    // in different warps keep the pipe at its nominal rate.  The issuers take
+    // alternate stages of a tile, each into its own accumulator (the two that
+    // otherwise double-buffer tiles), and the epilogue adds the two.
+    static constexpr bool ISS2 = BT == 128;
+    static constexpr int ISS_WARP = TS_THREADS / 32;  // the extra warp
+    static constexpr int THREADS = TS_THREADS + (ISS2 ? 32 : 0);
+    static_assert(!ISS2 || NA % 2 == 0, "two issuers split the stage barrier ring by parity");
     // Stage ga uses barrier slot ga % NA: kb_full is completed by the
     // activation TMA and the dequant group, kb_empty (which frees the TMEM A
     // stage) by the MMA commit once the stage's MMAs are done.  The producer
@@ -169,6 +181,7 @@ struct TsArgs {
     void *pre;         // the rounded pre-activation [M][Nout]: written (gelu), read (gradient); nullable for gelu
     float *partial;    // [splits][M][Nout]
     unsigned *err;
+    int iss2;          // 128-token tiles: two MMA issuers (every unit has >= 2 stages)
 };
 
 __device__ __forceinline__ void ldsm_x4_b16(uint32_t addr, uint32_t (&r)[4]) {
@@ -514,7 +527,7 @@ __device__ __forceinline__ TsTile ts_tile(const TsArgs &a, int t, uint32_t rank 
 }
 
 template <int DT, int BT, int KB2, int ACT, int PAIR = 0>
-__global__ void __launch_bounds__(TS_THREADS, 1)
+__global__ void __launch_bounds__(TsGeom<BT, KB2, PAIR>::THREADS, 1)
     q8ts_gemm_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                      const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmS,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmP,
@@ -548,6 +561,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     const bool leader = rank == 0;
     const int t_first = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int t_step = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const bool two = G::ISS2 && args.iss2 != 0;  // two MMA issuers, one accumulator each
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < G::S8; ++i) {
@@ -560,10 +574,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             mbar_init(&kb_empty[i], 1);
         }
         for (int i = 0; i < G::NACC; ++i) {
-            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_full[i], two ? 2 : 1);  // one commit per issuer
             mbar_init(&acc_empty[i], (PAIR ? 2 : 1) * TS_NEW);
         }
-        mbar_init(mma_done, 1);
+        mbar_init(mma_done, two ? 2 : 1);
         for (int i = 0; i < TS_NEW; ++i) mbar_init(&pre_bar[i], 1);
         for (int i = 0; i < G::NXE; ++i) mbar_init(&x_empty[i], 1);  // one MMA commit per use
         *abort = 0;
@@ -693,13 +707,19 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
+    } else if (warp == 1 || (G::ISS2 && warp == G::ISS_WARP)) {
+        // ------------------------------------------------ MMA issuer(s)
         // One lane runs the loop.  Each stage's MMAs are queued, then its
         // commit (releasing the stage once they complete), then the wait for
         // the next stage: the tensor pipe keeps the queued work while the
         // thread waits, and no warp-wide vote or sync sits between stages.
-        if (lane == 0 && (!PAIR || leader)) {
+        // With two issuers, issuer `iss` takes the stages ga % 2 == iss into
+        // accumulator iss; both wait for the tile's accumulators to be free and
+        // both commit acc_full (count 2).  Splitting by the running stage count
+        // (not by the stage's index in its tile) keeps each barrier slot
+        // ga % NA (NA even) with one issuer, which waits its phases in order.
+        const int iss = warp == 1 ? 0 : 1;
+        if (lane == 0 && (!PAIR || leader) && (iss == 0 || two)) {
             const int ab = (DT == DT_BF16) ? 1 : 0;
             const uint32_t id_main = idesc_f16(ab, 0, 0, PAIR ? 256 : 128, BT);
             const uint32_t id_ext = idesc_f16(ab, 0, 1, PAIR ? 256 : 128, BT);
@@ -713,15 +733,18 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
             uint32_t ga = 0, local = 0;
             for (int t = t_first; t < total_tiles && !aborted_here; t += t_step, ++local) {
                 const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
-                const int acc = local % G::NACC;
-                if (!TSW(0, wait_mma(&acc_empty[acc], ((local / G::NACC) & 1) ^ 1, DEVERR_TIMEOUT_ACC))) {
+                const int acc = two ? 0 : (int)(local % G::NACC);  // barrier slot
+                const uint32_t acc_par = two ? (local & 1) : ((local / G::NACC) & 1);
+                if (!TSW(0, wait_mma(&acc_empty[acc], acc_par ^ 1, DEVERR_TIMEOUT_ACC))) {
                     aborted_here = true;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tm = tmem + G::acc_col(acc);
+                const uint32_t d_tm = tmem + G::acc_col(two ? iss : acc);
                 const int n_iter = c.n_main + c.n_ext;
+                bool fresh = true;  // this issuer's first stage of the tile overwrites its accumulator
                 for (int it = 0; it < n_iter; ++it, ++ga) {
+                    if (two && (int)(ga & 1) != iss) continue;
                     const int sa = ga % G::NA;
                     if (!TSW(1, wait_mma(&kb_full[sa], (ga / G::NA) & 1, DEVERR_TIMEOUT_AB_FULL))) {
                         aborted_here = true;
@@ -741,7 +764,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 #pragma unroll
                         for (int kk = 0; kk < 4 * KB2; ++kk) {
                             mma(d_tm, a_tm + 8 * kk, dmain0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 32) >> 4), id_main,
-                                (it > 0 || kk > 0) ? 1u : 0u);
+                                (!fresh || kk > 0) ? 1u : 0u);
                             if ((kk & 3) == 3) release(kk >> 2);  // this atom has been read
                         }
                     } else {
@@ -749,11 +772,12 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                         const int nk = (min(G::SK, args.r - G::SK * e) + 15) / 16;
                         for (int kk = 0; kk < nk; ++kk)
                             mma(d_tm, a_tm + 8 * kk, dext0 + xoff(kk >> 2) + (uint64_t)(((kk & 3) * 2048) >> 4),
-                                id_ext, (it > 0 || kk > 0) ? 1u : 0u);
+                                id_ext, (!fresh || kk > 0) ? 1u : 0u);
 #pragma unroll
                         for (int a = 0; a < KB2; ++a) release(a);
                     }
                     commit(&kb_empty[sa]);
+                    fresh = false;
                     TS_ADD(2, tr_issue);
                 }
                 if (aborted_here) break;
@@ -896,7 +920,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         };
         for (int t = t_first; t < total_tiles && !aborted_here; t += t_step, ++local) {
             const TsTile c = ts_tile<BT, G::SK, PAIR>(args, t, rank);
-            const int acc = local % G::NACC;
+            const int acc = two ? 0 : (int)(local % G::NACC);
             if (act == ACT_GELU_TANH_GRAD && c.m0 + set * (BT / 2) < args.M) {
                 if (lane == 0)
                     for (int ch = 1; ch < BT / 64; ++ch)
@@ -904,12 +928,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                             tma_prefetch_l2_2d(&tmP, c.n0 + 32 * q, c.m0 + set * (BT / 2) + 32 * ch);
                 load_pre(c, set * (BT / 2));
             }
-            if (!TSW(0, wait_bar_all(&acc_full[acc], (local / G::NACC) & 1, abort, args.err, DEVERR_TIMEOUT_ACC))) {
+            if (!TSW(0, wait_bar_all(&acc_full[acc], two ? (local & 1) : ((local / G::NACC) & 1), abort, args.err,
+                                     DEVERR_TIMEOUT_ACC))) {
                 aborted_here = true;
                 break;
             }
             tc_fence_after();
             const uint32_t t_base = tmem + ((uint32_t)(32 * q) << 16) + G::acc_col(acc);
+            // two issuers: the second accumulator, added to the first in a fixed order
+            const uint32_t t_base1 = tmem + ((uint32_t)(32 * q) << 16) + G::acc_col(1);
             constexpr int NCH = BT / 64;  // 32-column chunks per epilogue set
             if (args.epi_partial) {
                 const int n = c.n0 + 32 * q + lane;
@@ -919,6 +946,17 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     uint32_t v[32];
                     tmem_ld32(t_base + j0, v);
                     tmem_wait_ld();
+                    if (G::ISS2 && two) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            uint32_t w[16];
+                            tmem_ld16(t_base1 + j0 + 16 * h, w);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                v[16 * h + j] = __float_as_uint(__uint_as_float(v[16 * h + j]) + __uint_as_float(w[j]));
+                        }
+                    }
                     if (ch == NCH - 1) {
                         tc_fence_before();
                         __syncwarp();
@@ -953,6 +991,17 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                 tmem_ld_16x256b_x4(t_base + j0, r[0]);
                 tmem_ld_16x256b_x4(t_base + (16u << 16) + j0, r[1]);
                 tmem_wait_ld();
+                if (G::ISS2 && two) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t w[16];
+                        tmem_ld_16x256b_x4(t_base1 + ((uint32_t)(16 * hh) << 16) + j0, w);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            r[hh][j] = __float_as_uint(__uint_as_float(r[hh][j]) + __uint_as_float(w[j]));
+                    }
+                }
                 if (ch == NCH - 1) {
                     // all of this warp's accumulator columns are in registers
                     tc_fence_before();
@@ -1046,7 +1095,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 
 #ifdef REELS_TS_TRACE
     tr_[3] = (unsigned long long)(clock64() - tr_start);
-    if (lane == 0 && blockIdx.x < 256)
+    if (lane == 0 && blockIdx.x < 256 && warp < TS_THREADS / 32)
         for (int k = 0; k < 4; ++k) atomicAdd(&g_ts_trace[((size_t)blockIdx.x * (TS_THREADS / 32) + warp) * 4 + k], tr_[k]);
 #endif
     if (aborted_here && (warp == 0 || warp == 2)) {

@@ -2,8 +2,9 @@
 itself: the SMEM x SMEM kernel (REELS_Q8_TS=0, the plan for reduction scales
 that are not 16-byte aligned), each token tile of the weight-in-TMEM kernel
 (REELS_Q8_TS=256/192/128, and 1282 for 128-token tiles with 128-wide
-pipeline stages), and the single-CTA forms of the plans the planner runs on
-CTA pairs (REELS_Q8_PAIR=0).  The overrides are read once
+pipeline stages), the single-CTA forms of the plans the planner runs on
+CTA pairs (REELS_Q8_PAIR=0), and the 128-token tiles with one MMA issuer
+instead of two (REELS_Q8_ISS2=0).  The overrides are read once
 per process, so each plan runs its cases in a child process."""
 import json
 import os
@@ -43,17 +44,18 @@ CASES = [(512, 512, 768, 16, 0, "bf16"), (300, 256, 512, 65, 1, "bf16"), (256, 1
          (1000, 640, 1152, 32, 1, "f16"), (2048, 1536, 640, 32, 0, "bf16")]
 
 
-@pytest.mark.parametrize("var,val", [("REELS_Q8_TS", "0"), ("REELS_Q8_TS", "256"),
-                                     ("REELS_Q8_TS", "192"), ("REELS_Q8_TS", "128"), ("REELS_Q8_TS", "1282"),
-                                     ("REELS_Q8_PAIR", "0")])
-def test_forced_plan_parity(var, val):
+@pytest.mark.parametrize("overrides", [{"REELS_Q8_TS": "0"}, {"REELS_Q8_TS": "256"}, {"REELS_Q8_TS": "192"},
+                                       {"REELS_Q8_TS": "128"}, {"REELS_Q8_TS": "1282"}, {"REELS_Q8_PAIR": "0"},
+                                       {"REELS_Q8_TS": "1282", "REELS_Q8_ISS2": "0"},
+                                       {"REELS_Q8_TS": "1282", "REELS_Q8_PAIR": "1", "REELS_Q8_ISS2": "0"}],
+                         ids=lambda o: ",".join(f"{k[9:]}={v}" for k, v in o.items()))
+def test_forced_plan_parity(overrides):
     from reels_b200 import build
     build.build()
     env = dict(os.environ)
-    env.pop("REELS_Q8_TILE", None)
-    env.pop("REELS_Q8_TS", None)
-    env.pop("REELS_Q8_PAIR", None)
-    env[var] = val
+    for k in ("REELS_Q8_TILE", "REELS_Q8_TS", "REELS_Q8_PAIR", "REELS_Q8_ISS2"):
+        env.pop(k, None)
+    env.update(overrides)
     code = CHILD.format(root=ROOT, tests=os.path.join(ROOT, "tests"), cases=CASES)
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stderr[-2000:]

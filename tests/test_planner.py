@@ -45,9 +45,10 @@ def test_bench_shapes_take_the_256_token_tmem_tiles(lib):
 
 
 def test_small_token_counts_take_the_wide_stage_tiles(lib):
-    # the Wan 2.1 14B FFN up-projection at 128 tokens: one 128-token tile, 128-wide stages
+    # the Wan 2.1 14B FFN up-projection at 128 tokens: one 128-token tile, 128-wide
+    # stages, single CTAs (one tile each, so two MMA issuers)
     p = q8(lib, 128, 13824, 5120)
-    assert p["kernel"] in (1, 2) and p["tokens"] == 128 and p["stage"] == 128
+    assert p["kernel"] == 1 and p["tokens"] == 128 and p["stage"] == 128
     assert p["splits"] * p["kb_per"] * p["stage"] >= 5120  # the splits cover the reduction
 
 
