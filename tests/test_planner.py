@@ -52,6 +52,19 @@ def test_small_token_counts_take_the_wide_stage_tiles(lib):
     assert p["splits"] * p["kb_per"] * p["stage"] >= 5120  # the splits cover the reduction
 
 
+def test_one_unit_per_cta_at_small_token_counts(lib):
+    # The 128-token plans run two MMA issuers only when each CTA gets one work
+    # unit with at least two stages; the planner prices them that way, so at
+    # small token counts it stays within one unit per SM: the FFN projections
+    # at 128 tokens (forward and dX) and the block's 512-token cross-attention
+    # k/v projections (four 128-token tiles per column tile).
+    for M, Nout, Kred in ((128, 13824, 5120), (128, 5120, 13824), (512, 1536, 1536), (96, 8192, 4096)):
+        p = q8(lib, M, Nout, Kred)
+        assert p["kernel"] == 1 and p["tokens"] == 128 and p["stage"] == 128, (M, Nout, Kred, p)
+        assert p["ntiles"] * p["mtiles"] * p["splits"] <= SMS, (M, Nout, Kred, p)
+        assert p["kb_per"] >= 2, (M, Nout, Kred, p)
+
+
 def test_splits_cover_the_reduction_exactly(lib):
     rng = np.random.default_rng(0)
     for _ in range(300):
